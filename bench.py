@@ -1,0 +1,335 @@
+#!/usr/bin/env python
+"""Pingala-8 batch-1 decode throughput on B200 (and the reference CPU path on the same host).
+
+Headline workload (BASELINE.json metric "decode tok/s bs1 (Llama-3.1-8B shape, 2-bit)"): one decode token through
+every Pingala-8 projection of a Llama-3.1-8B-architecture model -- 32 layers x {q, k, v, o, gate, up, down}
+(224 GEMVs, 1.80 GB of class-3 slots: seeded random valid codes, shapes of the real model). The projections are
+chained on the device (x -> q,k,v; q-out -> o; o-out -> gate,up; gate-out -> down; down-out -> next layer), captured
+once as a CUDA graph and replayed per step. Attention, norms and the LM head are not part of this path.
+
+  value     tokens/s with inputs resident in HBM (device-timed with CUDA events, max over ranks)
+  e2e       the same through the public op API with a pinned-host input vector copied in and the final output copied
+            out every step
+  roofline  p8_mul_mat_vec (k_act_prep + k_gemv + k_gemv_reduce) algorithmic bytes / event-timed call duration,
+            against MEASURED_PEAKS.json hbm_gbs
+  cpu_baseline  the reference's own CPU core (oracle/_ref, x16 vrc_tg) on one layer's 7 GEMVs, all host threads
+
+usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+LLAMA8B = dict(name="llama3.1-8b", layers=32, hidden=4096, ffn=14336, q=4096, kv=1024)
+METRIC = "decode tok/s bs1 (Llama-3.1-8B shape, 2-bit Pingala-8 projections)"
+
+
+def layer_shapes(m):
+    h, f, q, kv = m["hidden"], m["ffn"], m["q"], m["kv"]
+    # (name, rows, K): ggml [K, rows]
+    return [("q", q, h), ("k", kv, h), ("v", kv, h), ("o", h, q), ("gate", f, h), ("up", f, h), ("down", h, f)]
+
+
+def kernel_bytes_of(rows, K, cls=3):
+    nt = (rows // 32) * (K // 256)
+    nw = [0, 4, 6, 8, 10, 12, 16, 24][cls]
+    return ((2064 + 68 * nt + 15) & ~15) + 4 * nt * 64 * nw
+
+
+def algo_bytes_gemv(rows, K, cls=3):
+    """bytes one GEMV must move: M + S + payload of the slot (the rest of the header and side data are cached), x, y"""
+    nt = (rows // 32) * (K // 256)
+    nw = [0, 4, 6, 8, 10, 12, 16, 24][cls]
+    return 4 * nt + 64 * nt + 4 * nt * 64 * nw + 4 * K + 4 * rows
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+
+    Q = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
+        "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "200",
+                                          "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            self.lines.append(ln.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [x.strip() for x in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                mx = float(p[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d.get("hbm_gbs", 6650.0), "measured"
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------------------------------------ CPU reference leg
+def cpu_reference_layer(model, reps, warmup, seed=0):
+    """Reference CPU core (vrc_tg, x16) over one layer's 7 projections; returns per-layer seconds (median of reps)."""
+    from oracle.oracle import RefOracle
+    from pingala8_llm_b200 import synth
+
+    shapes = layer_shapes(model)
+    mats = []
+    for i, (nm, rows, K) in enumerate(shapes):
+        s = synth.make_slot(rows, K, seed=seed + i)
+        mats.append((RefOracle(s, rows, K), np.random.default_rng(i).normal(0, 1, K).astype(np.float32)))
+    for _ in range(warmup):
+        for r, x in mats:
+            r.gemv(x)
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        for r, x in mats:
+            r.gemv(x)
+        ts.append(time.perf_counter() - t0)
+    return statistics.median(ts), RefOracle.threads(), RefOracle.isa()
+
+
+def run_reference(args, rank, world):
+    model = LLAMA8B
+    if rank != 0:
+        return 0
+    layer_s, cores, isa = cpu_reference_layer(model, reps=max(1, args.steps), warmup=max(1, args.warmup))
+    tok_s = 1.0 / (model["layers"] * layer_s)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(tok_s, 4), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(1e3 * model["layers"] * layer_s, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int32+fp32 (x16 activations)", "data": "synthetic",
+        "config": {"workload": "llama3.1-8b-bs1-decode-projections", "layers": model["layers"], "projections_per_layer": 7,
+                   "batch": 1, "classes": "3"},
+        "cpu_baseline": {"value": round(tok_s, 4), "unit": "tok/s", "cores": cores, "kind": "reference",
+                         "sample": f"1 of {model['layers']} layers (7 GEMVs) per step, x{model['layers']}; {isa} vr-native-cpu-core.h"},
+        "e2e": {"value": round(tok_s, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------------------------ GPU leg
+def run_b200(args, rank, world, local_rank):
+    import torch
+    import torch.distributed as dist
+
+    from pingala8_llm_b200 import synth
+    from pingala8_llm_b200.ops import P8Tensor
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    model = LLAMA8B
+    shapes = layer_shapes(model)
+    # ---- weights: 32 x 7 distinct slots (1.8 GB), seeded per rank so replicas do not share L2 lines
+    layers = []
+    for L in range(model["layers"]):
+        ts = {}
+        for i, (nm, rows, K) in enumerate(shapes):
+            slot = synth.make_slot_device(rows, K, seed=1000 * L + 17 * i + 7919 * rank, device=dev)
+            ts[nm] = P8Tensor(slot, K, rows)
+        layers.append(ts)
+    ws_bytes = max(t.workspace_size(1) for ts in layers for t in ts.values())
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    h, f, q, kv = model["hidden"], model["ffn"], model["q"], model["kv"]
+    x0 = torch.randn(h, device=dev)
+    buf = dict(x=torch.empty(h, device=dev), q=torch.empty(q, device=dev), k=torch.empty(kv, device=dev),
+               v=torch.empty(kv, device=dev), o=torch.empty(h, device=dev), gate=torch.empty(f, device=dev),
+               up=torch.empty(f, device=dev), down=torch.empty(h, device=dev))
+
+    def step(stream):
+        x = buf["x"]
+        for ts in layers:
+            ts["q"].mul_mat_vec(x, out=buf["q"], workspace=ws, stream=stream)
+            ts["k"].mul_mat_vec(x, out=buf["k"], workspace=ws, stream=stream)
+            ts["v"].mul_mat_vec(x, out=buf["v"], workspace=ws, stream=stream)
+            ts["o"].mul_mat_vec(buf["q"], out=buf["o"], workspace=ws, stream=stream)
+            ts["gate"].mul_mat_vec(buf["o"], out=buf["gate"], workspace=ws, stream=stream)
+            ts["up"].mul_mat_vec(buf["o"], out=buf["up"], workspace=ws, stream=stream)
+            ts["down"].mul_mat_vec(buf["gate"], out=buf["down"], workspace=ws, stream=stream)
+            x = buf["down"]
+        return x
+
+    launches_per_step = 3 * 7 * model["layers"]
+    stream = torch.cuda.Stream(device=dev)
+    buf["x"].copy_(x0)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        step(stream)  # warm-up outside capture (kernel attributes, lazy module loading)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph, stream=stream):
+            step(stream)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- device-timed steps, inputs resident
+    for _ in range(args.warmup):
+        graph.replay()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(args.steps):
+                graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    t_dev = e0.elapsed_time(e1) / 1e3
+    # ---- end to end through the op API: pinned host input in, final output out, every step
+    x_host = torch.randn(h, pin_memory=True)
+    y_host = torch.empty(h, pin_memory=True)
+    for _ in range(args.warmup):
+        with torch.cuda.stream(stream):
+            buf["x"].copy_(x_host, non_blocking=True)
+            graph.replay()
+            y_host.copy_(buf["down"], non_blocking=True)
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(args.steps):
+            buf["x"].copy_(x_host, non_blocking=True)
+            graph.replay()
+            y_host.copy_(buf["down"], non_blocking=True)
+    e3.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    t_e2e = e2.elapsed_time(e3) / 1e3
+    # ---- roofline of the GEMV call: one eager pass with events around every call
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * 7 * model["layers"])]
+    bytes_total = 0
+    i = 0
+    with torch.cuda.stream(stream):
+        x = buf["x"]
+        for ts in layers:
+            for nm, rows, K in shapes:
+                src = {"q": x, "k": x, "v": x, "o": buf["q"], "gate": buf["o"], "up": buf["o"], "down": buf["gate"]}[nm]
+                evs[i].record(stream)
+                ts[nm].mul_mat_vec(src, out=buf[nm], workspace=ws, stream=stream)
+                evs[i + 1].record(stream)
+                bytes_total += algo_bytes_gemv(rows, K)
+                i += 2
+    torch.cuda.synchronize()
+    call_s = sum(evs[j].elapsed_time(evs[j + 1]) for j in range(0, len(evs), 2)) / 1e3
+    ncalls = len(evs) // 2
+    # ---- max over ranks
+    times = torch.tensor([t_dev, t_e2e, call_s], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    t_dev, t_e2e, call_s = times.tolist()
+    bytes_token = sum(algo_bytes_gemv(r, k) for _, r, k in shapes) * model["layers"]
+    if rank != 0:
+        return 0
+    peak, peak_kind = measured_peaks()
+    achieved = bytes_total / call_s / 1e9
+    tok_s = world * args.steps / t_dev
+    line = {
+        "metric": METRIC, "value": round(tok_s, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * t_dev / args.steps, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int32+fp32 (x16 activations)", "data": "synthetic (seeded random valid Pingala-8 codes, class 3)",
+        "config": {"workload": "llama3.1-8b-bs1-decode-projections", "layers": model["layers"], "projections_per_layer": 7,
+                   "batch": 1, "classes": "3", "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "weight_bytes_per_token": bytes_token, "l2": "inputs larger than L2 (1.80 GB of weights streamed per step)",
+                   "hbm_gbs_step": round(bytes_token / (t_dev / args.steps) / 1e9, 1)},
+        "roofline": {"kernel": "p8_mul_mat_vec (k_act_prep+k_gemv+k_gemv_reduce)", "bound": "hbm", "achieved": round(achieved, 1),
+                     "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs", "calls": ncalls},
+        "e2e": {"value": round(world * args.steps / t_e2e, 3), "unit": "tok/s", "h2d_bytes_per_step": 4 * h, "d2h_bytes_per_step": 4 * h},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk.summary(),
+    }
+    if world == 1 and not args.no_cpu:
+        layer_s, cores, isa = cpu_reference_layer(model, reps=5, warmup=1)
+        line["cpu_baseline"] = {"value": round(1.0 / (model["layers"] * layer_s), 4), "unit": "tok/s", "cores": cores, "kind": "reference",
+                                "sample": f"1 of {model['layers']} layers (7 GEMVs, x{model['layers']}), median of 5; {isa} vr-native-cpu-core.h"}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+    try:
+        return run_b200(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,144 @@
+/*
+ * pingala8.h -- C ABI of the B200 (sm_100a) Pingala-8 quantized-weight matmul path.
+ *
+ * Drop-in boundary for the reference's ggml hooks (Genrius-AI/pingala8-llm, patches/llama_cuda_vs_7ac59a6.patch = CU,
+ * patches/llama_cpu_vs_7ac59a6.patch = CP). Plain pointers, sizes and status codes; no ggml or torch types.
+ * The reference aborts (GGML_ABORT / GGML_ASSERT) or throws std::runtime_error where these functions return a status.
+ *
+ * Tensor memory ("slot") is the reference's in-memory contract byte for byte (ggml-vr-native.h, CU:1-51): kernel bytes
+ * (A | B | c, NS, TRL | M | S | D), then, top-down from the end, clamp delta E, c16, prm, pinv, Hadamard signs and a
+ * 32-byte trailer "VVRN" "RI51". Logical shape [K, rows] (ggml ne0 = K, ne1 = rows).
+ *
+ * Every compute entry point enqueues on the given stream, does not synchronise and allocates nothing: scratch comes
+ * from the caller (p8_workspace_size), as ggml's pool allocations do, so calls are capturable into CUDA graphs.
+ * p8_prepare is the one-time set-up (device->host reads, small device allocations) and must run before capture,
+ * as ggml_cuda_f44_prepare_graph does (CU:1351).
+ */
+#ifndef PINGALA8_H
+#define PINGALA8_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum p8_status {
+    P8_OK = 0,
+    P8_ERR_ARG = -1,        /* null pointer, bad shape or size argument */
+    P8_ERR_TRAILER = -2,    /* trailer magic / rows / K / NS mismatch (reference: "bad trailer/header", CU:3058-3061) */
+    P8_ERR_HEADER = -3,     /* header NS != 108 or TRL != 2 (CU:3547) */
+    P8_ERR_PAYLOAD = -4,    /* kernel bytes != size implied by the M words, or a tile outside the payload (CU:3553-3556) */
+    P8_ERR_PERM = -5,       /* prm is not a permutation / pinv inconsistent (CU:3563-3568) */
+    P8_ERR_DELTA = -6,      /* clamp-delta index out of range (CU:3573) */
+    P8_ERR_SIGNS = -7,      /* Hadamard signs not +-1 (CU:3576) */
+    P8_ERR_TABLES = -8,     /* A + c leaves int8 range (the coset add must not wrap) */
+    P8_ERR_SHAPE = -9,      /* K % 256, rows % 32, rows >= 32768 (CU:3481) */
+    P8_ERR_CUDA = -10,      /* a CUDA runtime call failed */
+    P8_ERR_WORKSPACE = -11, /* workspace missing or too small */
+    P8_ERR_NOT_PREPARED = -12, /* tensor handle unknown / released (reference: GGML_ABORT, CU:3172) */
+    P8_ERR_UNSUPPORTED = -13,  /* valid request this build does not serve */
+    P8_ERR_TIMEOUT = -14,   /* a bounded device-side wait gave up (kernel returned early, results invalid) */
+    P8_ERR_SLOT = -15       /* no slot type is large enough (loader: "no slot type fits", CU:3498) */
+} p8_status;
+
+typedef struct p8_tensor p8_tensor;
+
+/* ---------------------------------------------------------------- tensor life cycle ----------------------------- */
+
+/* Validate a slot resident in device memory and build its device-side aux data (sgn/c per column, CSR clamp delta).
+ * Replaces vr_native_probe + vr_prepare_native (CU:666-676, CU:3046-3101), i.e. ggml_cuda_f44_prepare_graph
+ * (CU:678-715) for one tensor. Reads the header, M, side data and trailer to the host (synchronises `stream`). */
+p8_status p8_prepare(const void *dev_slot, size_t nbytes, int64_t K, int64_t rows, void *stream, p8_tensor **out);
+
+/* Release a prepared tensor (the reference never frees its CSR arrays, CU:3094-3098). */
+p8_status p8_release(p8_tensor *t);
+
+/* 1 if dev_slot was prepared and not released, else 0. Replaces ggml_cuda_f44_active (CU:223-232). */
+int p8_active(const void *dev_slot);
+
+/* Shape and stats of a prepared tensor: rows, K, nd (delta entries), class histogram (8 entries, may be NULL). */
+p8_status p8_tensor_info(const p8_tensor *t, int64_t *rows, int64_t *K, int64_t *nd, uint64_t *class_hist);
+
+/* ---------------------------------------------------------------- compute -------------------------------------- */
+
+/* Scratch bytes needed by p8_mul_mat_vec / p8_mul_mat for `ncols` activation columns (ggml pool allocations in the
+ * reference, CU:3182-3184; CPU: ggml_vr_cpu_wsize, CP:1080-1088). */
+size_t p8_workspace_size(const p8_tensor *t, int64_t ncols);
+
+/* y[rows] = W x, x f32[K] (16-byte aligned). Batch-1 decode GEMV. Replaces ggml_cuda_f44_mul_mat_vec (CU:277) ->
+ * vr_mul_mat_vec (CU:3177-3232). Activations x16 (14-bit per 128-column half-slice, the reference CPU default),
+ * deterministic (no float atomics). */
+p8_status p8_mul_mat_vec(const p8_tensor *t, const float *x, float *y, void *workspace, size_t workspace_bytes, void *stream);
+
+/* Y[n][ldy] (rows per column) = W X[n][ldx], n < ncols. ncols > 1: batched decode / prefill. Replaces
+ * ggml_cuda_f44_mul_mat_q8 (CU:1014-1054). */
+p8_status p8_mul_mat(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy,
+                     void *workspace, size_t workspace_bytes, void *stream);
+
+/* out[i][ldo] = row ids[i] (ORIGINAL row index) of W in f32, bit-identical to vrc_dequant_f32 (CP:1012-1027).
+ * The get_rows / embedding lookup entry. */
+p8_status p8_get_rows(const p8_tensor *t, const int32_t *ids, int64_t n, float *out, int64_t ldo, void *stream);
+
+/* W (rows x K, row-major by ORIGINAL row) in f32, bit-identical to vrc_dequant_f32 (CP:1012-1027); ggml to_fp32. */
+p8_status p8_dequant_f32(const p8_tensor *t, float *out, void *stream);
+
+/* Exact integer weights (sorted rows x K, natural columns) = vrc_decode_tile_int (CP:992-1010) over all tiles. */
+p8_status p8_decode_int(const p8_tensor *t, int16_t *out, void *stream);
+
+/* ---------------------------------------------------------------- host format helpers ---------------------------- */
+
+/* vrn_need (CU:27-29): bytes a slot needs for the given kernel bytes, shape and delta count. */
+size_t p8_slot_need(size_t kbytes, size_t rows, size_t K, size_t nd);
+
+/* vrn_offsets (CU:30-37): offE, offC, offP, offQ, offSG, offT of a slot of n bytes (out6 = 6 entries). */
+void p8_slot_offsets(size_t n, size_t rows, size_t K, size_t nd, size_t *out6);
+
+/* vrn_kbytes(rows, K, vrn_payload_words(M)) (CU:41-51). */
+size_t p8_kbytes_from_m(size_t rows, size_t K, const uint32_t *M);
+
+/* Slot size the loader picks: smallest of IQ2_XXS, Q2_K..Q6_K holding `need` bytes (CU:3493-3497). 0 if none. */
+size_t p8_slot_nbytes(size_t rows, size_t K, size_t need, int *slot_type_index);
+
+/* Assemble a slot in host memory from kernel bytes and side tensors, as vr_native_load does (CU:3527-3580):
+ * c16 fp16[K], prm int16[rows] (NULL = identity, VR3), delta rows/cols u16[nd] + vals f32[nd], signs int8[256].
+ * `out` must hold p8_slot_nbytes(...) bytes; *out_n receives that size. All the loader's checks apply. */
+p8_status p8_slot_assemble(const uint8_t *kbytes, size_t kb_n, int64_t rows, int64_t K, const uint16_t *c16,
+                           const int16_t *prm, const uint16_t *drow, const uint16_t *dcol, const float *dval, int64_t nd,
+                           const int8_t *signs, uint8_t *out, size_t out_cap, size_t *out_n);
+
+/* Validate a slot held in HOST memory (every check p8_prepare does). */
+p8_status p8_slot_check(const uint8_t *slot, size_t nbytes, int64_t K, int64_t rows);
+
+/* VR3 file layout (llama-vr3.h, CU:3621-3661): rows of a VR3 tensor from its file size, K and header word 515
+ * (0 if inconsistent; *kbytes = expanded v2 kernel bytes), and the expansion to the v2 in-memory bytes. */
+size_t p8_vr3_rows(size_t fbytes, size_t K, uint32_t w515, size_t *kbytes);
+p8_status p8_vr3_expand(const uint8_t *f, size_t fbytes, size_t rows, size_t K, uint8_t *dst, size_t dst_cap);
+
+/* ---------------------------------------------------------------- tensor parallel (no reference counterpart) ---- */
+
+/* Column-parallel shard (q/k/v/gate/up): the ORIGINAL output rows [r0, r1) (r1 - r0 a multiple of 32) as a standalone
+ * slot. The selected rows keep their sorted order and are re-tiled (a row moved to another lane of a tile has its steps
+ * rotated, since step k holds chunk (lane + k) & 31); the shard's prm maps to original row - r0. Needs one class per
+ * new tile-block (always true for single-class tensors), else P8_ERR_UNSUPPORTED. orig_rows (optional, r1 - r0
+ * entries) receives the original row of each shard row. Host memory in and out. */
+p8_status p8_tp_shard_rows(const uint8_t *slot, size_t nbytes, int64_t K, int64_t rows, int64_t r0, int64_t r1,
+                           uint8_t *out, size_t out_cap, size_t *out_n, int32_t *orig_rows /* [r1-r0] or NULL */);
+
+/* Row-parallel shard (o/down): the slot of 256-column blocks [b0, b1) (columns [256 b0, 256 b1)) as a standalone
+ * slot; every rank keeps all rows, partial outputs are summed by an all-reduce. */
+p8_status p8_tp_shard_cols(const uint8_t *slot, size_t nbytes, int64_t K, int64_t rows, int64_t b0, int64_t b1,
+                           uint8_t *out, size_t out_cap, size_t *out_n);
+
+/* 1 if a kernel since the last call gave up on a bounded device-side wait (that launch's results are invalid), then
+ * clears the flag. Synchronises the device. */
+int p8_device_error(void);
+
+const char *p8_status_str(p8_status s);
+const char *p8_build_info(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PINGALA8_H */

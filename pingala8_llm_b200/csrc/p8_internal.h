@@ -1,0 +1,66 @@
+// p8_internal.h -- library-internal declarations (not part of the C ABI).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <vector>
+
+#include "../../include/pingala8.h"
+#include "p8_format.h"
+
+// A prepared tensor: device pointers into the caller's slot plus the small device arrays built at prepare time.
+struct p8_tensor {
+    uint32_t magic;  // kTensorMagic while alive
+    int device;
+    const uint8_t *slot;
+    size_t nbytes, kbytes, nt;
+    int rows, K, nb, ng, nsl, nd;
+    // device pointers into the slot
+    const uint32_t *A;  // codebook (header words 0..255)
+    const uint32_t *M;
+    const uint16_t *S;
+    const uint32_t *D;
+    const uint16_t *c16;
+    const int16_t *prm, *pinv;
+    // owned device arrays
+    float *ic;   // sgn/c per column, float division on the host as vrc_init (CP:264)
+    int *cp;     // clamp-delta CSR by ORIGINAL row (rows + 1), entries in slot order within a row (CP:266-273)
+    uint16_t *cc;
+    float *cv;
+    // host copies
+    uint32_t cs;              // coset word
+    uint32_t class_mask;      // bit c set if some tile has class c
+    uint64_t hist[8];
+    std::vector<uint32_t> A_host;
+};
+
+constexpr uint32_t kTensorMagic = 0x50385454u;
+
+namespace p8 {
+// host-side validation of a slot image (used by p8_prepare on the device-side reads, and by p8_slot_check)
+struct SlotView {
+    const uint8_t *hdr;       // >= 2064 bytes
+    const uint32_t *M;        // nt words
+    const Trailer *tr;
+    const int8_t *sg;         // 256
+    const int16_t *prm, *pinv;
+    const uint16_t *drow, *dcol;
+    const uint16_t *c16;
+    size_t n;
+};
+p8_status validate_slot(const SlotView &v, int64_t K, int64_t rows, size_t *kbytes_out, uint32_t *class_mask,
+                        uint64_t *hist);
+p8_status check_shape(int64_t K, int64_t rows);
+
+// launchers (p8_kernels.cu)
+cudaError_t launch_decode_int(const p8_tensor *t, int16_t *out, cudaStream_t st);
+cudaError_t launch_dequant(const p8_tensor *t, float *out, cudaStream_t st);
+cudaError_t launch_get_rows(const p8_tensor *t, const int32_t *ids, int64_t n, float *out, int64_t ldo, cudaStream_t st);
+size_t gemv_workspace(const p8_tensor *t, int64_t ncols);
+p8_status launch_gemv(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy, void *ws,
+                      size_t ws_bytes, cudaStream_t st);
+size_t gemm_workspace(const p8_tensor *t, int64_t ncols);
+p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy, void *ws,
+                      size_t ws_bytes, cudaStream_t st);
+bool gemm_supported(const p8_tensor *t, int64_t ncols);
+}  // namespace p8

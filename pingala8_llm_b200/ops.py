@@ -1,0 +1,126 @@
+"""Operator layer: a prepared Pingala-8 weight and the ggml MUL_MAT / GET_ROWS / to_fp32 ops on it.
+
+Mirrors the reference's op hooks (ggml_cuda_f44_active / _prepare_graph / _mul_mat_vec / _mul_mat_q8, CU:1293-1302)
+with torch tensors as the device-memory carrier. Every call goes through the C ABI of libpingala8_b200.so on the
+current torch CUDA stream; there is no CPU path.
+"""
+import ctypes as C
+
+import numpy as np
+import torch
+
+from ._lib import P8Error, check, lib
+
+
+def _stream(stream=None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def _ptr(t):
+    return C.c_void_p(t.data_ptr())
+
+
+class P8Tensor:
+    """A Pingala-8 slot on the GPU, prepared once (validation + side structures), like ggml_cuda_f44_prepare_graph.
+
+    slot: torch.uint8 CUDA tensor or numpy uint8 array (copied to the current device). Shape [K, rows] in ggml terms.
+    """
+
+    def __init__(self, slot, K, rows, stream=None):
+        if isinstance(slot, np.ndarray):
+            slot = torch.from_numpy(np.ascontiguousarray(slot, np.uint8)).cuda()
+        if not (isinstance(slot, torch.Tensor) and slot.is_cuda and slot.dtype == torch.uint8 and slot.is_contiguous()):
+            raise ValueError("slot must be a contiguous torch.uint8 CUDA tensor")
+        self.slot, self.K, self.rows = slot, int(K), int(rows)
+        h = C.c_void_p()
+        check(lib().p8_prepare(_ptr(slot), slot.numel(), self.K, self.rows, _stream(stream), C.byref(h)), "p8_prepare")
+        self._h = h
+        self._ws = {}
+
+    @property
+    def handle(self):
+        if self._h is None:
+            raise P8Error(-12, "tensor released")
+        return self._h
+
+    def info(self):
+        r, k, nd = C.c_int64(), C.c_int64(), C.c_int64()
+        hist = (C.c_uint64 * 8)()
+        check(lib().p8_tensor_info(self.handle, C.byref(r), C.byref(k), C.byref(nd), hist), "p8_tensor_info")
+        return dict(rows=r.value, K=k.value, nd=nd.value, class_hist=list(hist))
+
+    def workspace_size(self, ncols=1):
+        return int(lib().p8_workspace_size(self.handle, ncols))
+
+    def workspace(self, ncols=1):
+        n = self.workspace_size(ncols)
+        w = self._ws.get("buf")
+        if w is None or w.numel() < n:
+            w = torch.empty(max(n, 256), dtype=torch.uint8, device=self.slot.device)
+            self._ws["buf"] = w
+        return w
+
+    def mul_mat_vec(self, x, out=None, workspace=None, stream=None):
+        """y = W x, x float32 [K] on the GPU -> float32 [rows]."""
+        x = x.contiguous()
+        if x.dtype != torch.float32 or x.numel() != self.K or not x.is_cuda:
+            raise ValueError("x must be float32 CUDA with K elements")
+        y = out if out is not None else torch.empty(self.rows, dtype=torch.float32, device=x.device)
+        ws = workspace if workspace is not None else self.workspace(1)
+        check(lib().p8_mul_mat_vec(self.handle, _ptr(x), _ptr(y), _ptr(ws), ws.numel(), _stream(stream)), "p8_mul_mat_vec")
+        return y
+
+    def mul_mat(self, X, out=None, workspace=None, stream=None):
+        """Y = X W^T: X float32 [ncols, K] -> Y float32 [ncols, rows] (ggml dst [rows, ncols])."""
+        X = X.contiguous()
+        if X.dtype != torch.float32 or X.dim() != 2 or X.shape[1] != self.K or not X.is_cuda:
+            raise ValueError("X must be float32 CUDA [ncols, K]")
+        n = X.shape[0]
+        Y = out if out is not None else torch.empty(n, self.rows, dtype=torch.float32, device=X.device)
+        ws = workspace if workspace is not None else self.workspace(n)
+        check(lib().p8_mul_mat(self.handle, _ptr(X), n, self.K, _ptr(Y), Y.stride(0), _ptr(ws), ws.numel(), _stream(stream)),
+              "p8_mul_mat")
+        return Y
+
+    def get_rows(self, ids, out=None, stream=None):
+        """rows ids (ORIGINAL row indices, int32 CUDA) -> float32 [n, K]"""
+        ids = ids.to(torch.int32).contiguous()
+        if ids.numel() and (int(ids.min()) < 0 or int(ids.max()) >= self.rows):
+            raise P8Error(-1, "p8_get_rows: row id out of range")
+        out = out if out is not None else torch.empty(ids.numel(), self.K, dtype=torch.float32, device=self.slot.device)
+        check(lib().p8_get_rows(self.handle, _ptr(ids), ids.numel(), _ptr(out), out.stride(0), _stream(stream)), "p8_get_rows")
+        return out
+
+    def dequant(self, out=None, stream=None):
+        out = out if out is not None else torch.empty(self.rows, self.K, dtype=torch.float32, device=self.slot.device)
+        check(lib().p8_dequant_f32(self.handle, _ptr(out), _stream(stream)), "p8_dequant_f32")
+        return out
+
+    def decode_int(self, out=None, stream=None):
+        out = out if out is not None else torch.empty(self.rows, self.K, dtype=torch.int16, device=self.slot.device)
+        check(lib().p8_decode_int(self.handle, _ptr(out), _stream(stream)), "p8_decode_int")
+        return out
+
+    def release(self):
+        if self._h is not None:
+            check(lib().p8_release(self._h), "p8_release")
+            self._h = None
+
+    def __del__(self):
+        try:
+            if getattr(self, "_h", None) is not None:
+                lib().p8_release(self._h)
+                self._h = None
+        except Exception:
+            pass
+
+
+def active(slot):
+    """ggml_cuda_f44_active: is this device slot a prepared Pingala-8 tensor?"""
+    return bool(lib().p8_active(_ptr(slot)))
+
+
+def device_error():
+    """1 if a kernel gave up on a bounded device wait since the last call (synchronises)."""
+    return int(lib().p8_device_error())
