@@ -4,13 +4,14 @@
 Headline workload (BASELINE.json metric "decode tok/s bs1 (Llama-3.1-8B shape, 2-bit)"): one decode token through
 every Pingala-8 projection of a Llama-3.1-8B-architecture model -- 32 layers x {q, k, v, o, gate, up, down}
 (224 GEMVs, 1.80 GB of class-3 slots: seeded random valid codes, shapes of the real model). The projections are
-chained on the device (x -> q,k,v; q-out -> o; o-out -> gate,up; gate-out -> down; down-out -> next layer), captured
-once as a CUDA graph and replayed per step. Attention, norms and the LM head are not part of this path.
+chained on the device (x -> q,k,v; q-out -> o; o-out -> gate,up; gate-out -> down; down-out -> next layer), launched
+as 4 grouped GEMV calls per layer (tensors that read the same x share one prepared activation), captured once as a
+CUDA graph and replayed per step. Attention, norms and the LM head are not part of this path.
 
   value     tokens/s with inputs resident in HBM (device-timed with CUDA events, max over ranks)
   e2e       the same through the public op API with a pinned-host input vector copied in and the final output copied
             out every step
-  roofline  p8_mul_mat_vec (k_act_prep + k_gemv + k_gemv_reduce) algorithmic bytes / event-timed call duration,
+  roofline  p8_mul_mat_vec_group (k_act_prep + k_gemv) algorithmic bytes / event-timed call duration,
             against MEASURED_PEAKS.json hbm_gbs
   cpu_baseline  the reference's own CPU core (oracle/_ref, x16 vrc_tg) on one layer's 7 GEMVs, all host threads
 
@@ -163,7 +164,7 @@ def run_b200(args, rank, world, local_rank):
     import torch.distributed as dist
 
     from pingala8_llm_b200 import synth
-    from pingala8_llm_b200.ops import P8Tensor
+    from pingala8_llm_b200.ops import P8Tensor, group_workspace_size, mul_mat_vec_group
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -177,7 +178,8 @@ def run_b200(args, rank, world, local_rank):
             slot = synth.make_slot_device(rows, K, seed=1000 * L + 17 * i + 7919 * rank, device=dev)
             ts[nm] = P8Tensor(slot, K, rows)
         layers.append(ts)
-    ws_bytes = max(t.workspace_size(1) for ts in layers for t in ts.values())
+    groups = [("q", "k", "v"), ("o",), ("gate", "up"), ("down",)]  # tensors of a group read the same x
+    ws_bytes = max(group_workspace_size([ts[n] for n in grp]) for ts in layers for grp in groups)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     h, f, q, kv = model["hidden"], model["ffn"], model["q"], model["kv"]
     x0 = torch.randn(h, device=dev)
@@ -185,20 +187,19 @@ def run_b200(args, rank, world, local_rank):
                v=torch.empty(kv, device=dev), o=torch.empty(h, device=dev), gate=torch.empty(f, device=dev),
                up=torch.empty(f, device=dev), down=torch.empty(h, device=dev))
 
+    def inputs(x):
+        return {("q", "k", "v"): x, ("o",): buf["q"], ("gate", "up"): buf["o"], ("down",): buf["gate"]}
+
     def step(stream):
         x = buf["x"]
         for ts in layers:
-            ts["q"].mul_mat_vec(x, out=buf["q"], workspace=ws, stream=stream)
-            ts["k"].mul_mat_vec(x, out=buf["k"], workspace=ws, stream=stream)
-            ts["v"].mul_mat_vec(x, out=buf["v"], workspace=ws, stream=stream)
-            ts["o"].mul_mat_vec(buf["q"], out=buf["o"], workspace=ws, stream=stream)
-            ts["gate"].mul_mat_vec(buf["o"], out=buf["gate"], workspace=ws, stream=stream)
-            ts["up"].mul_mat_vec(buf["o"], out=buf["up"], workspace=ws, stream=stream)
-            ts["down"].mul_mat_vec(buf["gate"], out=buf["down"], workspace=ws, stream=stream)
+            src = inputs(x)
+            for grp in groups:
+                mul_mat_vec_group([ts[n] for n in grp], src[grp], outs=[buf[n] for n in grp], workspace=ws, stream=stream)
             x = buf["down"]
         return x
 
-    launches_per_step = 3 * 7 * model["layers"]
+    launches_per_step = 2 * len(groups) * model["layers"]  # k_act_prep + k_gemv per group
     stream = torch.cuda.Stream(device=dev)
     buf["x"].copy_(x0)
     torch.cuda.synchronize()
@@ -251,18 +252,19 @@ def run_b200(args, rank, world, local_rank):
     barrier()
     t_e2e = e2.elapsed_time(e3) / 1e3
     # ---- roofline of the GEMV call: one eager pass with events around every call
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * 7 * model["layers"])]
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * len(groups) * model["layers"])]
+    dims = {nm: (rows, K) for nm, rows, K in shapes}
     bytes_total = 0
     i = 0
     with torch.cuda.stream(stream):
         x = buf["x"]
         for ts in layers:
-            for nm, rows, K in shapes:
-                src = {"q": x, "k": x, "v": x, "o": buf["q"], "gate": buf["o"], "up": buf["o"], "down": buf["gate"]}[nm]
+            src = inputs(x)
+            for grp in groups:
                 evs[i].record(stream)
-                ts[nm].mul_mat_vec(src, out=buf[nm], workspace=ws, stream=stream)
+                mul_mat_vec_group([ts[n] for n in grp], src[grp], outs=[buf[n] for n in grp], workspace=ws, stream=stream)
                 evs[i + 1].record(stream)
-                bytes_total += algo_bytes_gemv(rows, K)
+                bytes_total += sum(algo_bytes_gemv(*dims[n]) for n in grp) - 4 * dims[grp[0]][1] * (len(grp) - 1)
                 i += 2
     torch.cuda.synchronize()
     call_s = sum(evs[j].elapsed_time(evs[j + 1]) for j in range(0, len(evs), 2)) / 1e3
@@ -286,7 +288,7 @@ def run_b200(args, rank, world, local_rank):
                    "batch": 1, "classes": "3", "parallelism": f"replicas{world}" if world > 1 else "single",
                    "weight_bytes_per_token": bytes_token, "l2": "inputs larger than L2 (1.80 GB of weights streamed per step)",
                    "hbm_gbs_step": round(bytes_token / (t_dev / args.steps) / 1e9, 1)},
-        "roofline": {"kernel": "p8_mul_mat_vec (k_act_prep+k_gemv+k_gemv_reduce)", "bound": "hbm", "achieved": round(achieved, 1),
+        "roofline": {"kernel": "p8_mul_mat_vec_group (k_act_prep + k_gemv)", "bound": "hbm", "achieved": round(achieved, 1),
                      "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
                      "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs", "calls": ncalls},
         "e2e": {"value": round(world * args.steps / t_e2e, 3), "unit": "tok/s", "h2d_bytes_per_step": 4 * h, "d2h_bytes_per_step": 4 * h},

@@ -72,6 +72,14 @@ size_t p8_workspace_size(const p8_tensor *t, int64_t ncols);
  * deterministic (no float atomics). */
 p8_status p8_mul_mat_vec(const p8_tensor *t, const float *x, float *y, void *workspace, size_t workspace_bytes, void *stream);
 
+/* Several tensors that read the same x (q/k/v, gate/up): y_i = W_i x for i < n (n <= 4), one prepared activation and
+ * one launch. The tensors need equal K, column scales c, signs and codebook (else P8_ERR_ARG). The reference prepares
+ * x once for consecutive tensors with the same input and c (vrc_tg activation cache, CP:1171-1180); ggml itself has no
+ * grouped op, so this entry point is an extension. */
+size_t p8_workspace_size_group(const p8_tensor *const *ts, int n, int64_t ncols);
+p8_status p8_mul_mat_vec_group(const p8_tensor *const *ts, int n, const float *x, float *const *ys, void *workspace,
+                               size_t workspace_bytes, void *stream);
+
 /* Y[n][ldy] (rows per column) = W X[n][ldx], n < ncols. ncols > 1: batched decode / prefill. Replaces
  * ggml_cuda_f44_mul_mat_q8 (CU:1014-1054). */
 p8_status p8_mul_mat(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy,

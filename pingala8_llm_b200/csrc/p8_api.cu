@@ -118,6 +118,17 @@ p8_status p8_prepare(const void *dev_slot, size_t nbytes, int64_t K, int64_t row
         cc[(size_t)q] = v.dcol[e];
         memcpy(&cv[(size_t)q], dval + e, 4);
     }
+    {  // content hash of everything the prepared activation depends on (as the reference's c hash, CP:261)
+        uint64_t h = 1469598103934665603ull;
+        auto mix = [&h](const void *p, size_t n) {
+            const uint8_t *b = (const uint8_t *)p;
+            for (size_t i = 0; i < n; ++i) { h ^= b[i]; h *= 1099511628211ull; }
+        };
+        mix(ic.data(), 4 * ic.size());
+        mix(hdr.data(), 1024);
+        mix(hdr.data() + 2048, 4);
+        t->act_hash = h;
+    }
     if (dmalloc_copy(&t->ic, ic.data(), ic.size()) != cudaSuccess || dmalloc_copy(&t->cp, cp.data(), cp.size()) != cudaSuccess ||
         dmalloc_copy(&t->cc, cc.data(), cc.size()) != cudaSuccess || dmalloc_copy(&t->cv, cv.data(), cv.size()) != cudaSuccess) {
         free_tensor(t);
@@ -175,6 +186,25 @@ p8_status p8_mul_mat_vec(const p8_tensor *t, const float *x, float *y, void *wor
     if (!valid(t)) return P8_ERR_NOT_PREPARED;
     if (!x || !y || ((uintptr_t)x & 15)) return P8_ERR_ARG;
     return launch_gemv(t, x, 1, t->K, y, t->rows, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+size_t p8_workspace_size_group(const p8_tensor *const *ts, int n, int64_t ncols) {
+    if (!ts || n < 1 || n > 4 || ncols <= 0) return 0;
+    for (int i = 0; i < n; ++i)
+        if (!valid(ts[i])) return 0;
+    return gemv_group_workspace(ts, n, ncols);
+}
+
+p8_status p8_mul_mat_vec_group(const p8_tensor *const *ts, int n, const float *x, float *const *ys, void *workspace,
+                               size_t workspace_bytes, void *stream) {
+    if (!ts || !ys || n < 1 || n > 4 || !x || ((uintptr_t)x & 15)) return P8_ERR_ARG;
+    int64_t ld[4];
+    for (int i = 0; i < n; ++i) {
+        if (!valid(ts[i])) return P8_ERR_NOT_PREPARED;
+        if (!ys[i]) return P8_ERR_ARG;
+        ld[i] = ts[i]->rows;
+    }
+    return launch_gemv_group(ts, n, x, 1, ts[0]->K, ys, ld, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 p8_status p8_mul_mat(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy, void *workspace,

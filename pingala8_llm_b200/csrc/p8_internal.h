@@ -31,6 +31,7 @@ struct p8_tensor {
     uint32_t cs;              // coset word
     uint32_t class_mask;      // bit c set if some tile has class c
     uint64_t hist[8];
+    uint64_t act_hash;        // FNV-1a of (sgn/c per column, codebook, coset): tensors with equal hashes share a prepared x
     std::vector<uint32_t> A_host;
 };
 
@@ -57,6 +58,9 @@ cudaError_t launch_decode_int(const p8_tensor *t, int16_t *out, cudaStream_t st)
 cudaError_t launch_dequant(const p8_tensor *t, float *out, cudaStream_t st);
 cudaError_t launch_get_rows(const p8_tensor *t, const int32_t *ids, int64_t n, float *out, int64_t ldo, cudaStream_t st);
 size_t gemv_workspace(const p8_tensor *t, int64_t ncols);
+size_t gemv_group_workspace(const p8_tensor *const *ts, int nt, int64_t ncols);
+p8_status launch_gemv_group(const p8_tensor *const *ts, int nt, const float *X, int64_t ncols, int64_t ldx, float *const *Ys,
+                            const int64_t *ldys, void *ws, size_t ws_bytes, cudaStream_t st);
 p8_status launch_gemv(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy, void *ws,
                       size_t ws_bytes, cudaStream_t st);
 size_t gemm_workspace(const p8_tensor *t, int64_t ncols);

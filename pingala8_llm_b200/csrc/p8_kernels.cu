@@ -207,20 +207,43 @@ cudaError_t launch_get_rows(const p8_tensor *t, const int32_t *ids, int64_t n, f
 // T[f][hs][t] = <A[f], q_t> (exact int32). The integer sums equal the reference's exact integer dot products, so the
 // only difference to the CPU result is float rounding in the final scale-and-sum.
 //
-//   k_act_prep   grid (nb, ncols), 256 thr : x -> FWHT(x sgn/c)/16 -> q, d; tables T (64 KB per 256-col block),
-//                                            coset nibble tables G (8 groups x 16 per half-slice)
-//   k_gemv       grid (nb * chunks, ncols), 512 thr : one 256-col block x (32 * 16 * tpw) rows per CTA. The block's
-//                                            T and G arrive by one bulk copy (TMA engine, mbarrier); each lane owns one
-//                                            row and walks its 2 x 32 chunks: 1 PRMT (field byte + rotated chunk
-//                                            offset -> table address) + 1 LDS + 1 add per chunk.
-//   k_gemv_reduce grid (rows/256, ncols)    : fixed-order sum over blocks, clamp delta, un-permute (deterministic)
+//   k_act_prep  grid (nb, 8, ncols), 256 thr: x -> FWHT(x sgn/c)/16 -> q, d (per 128-col half-slice); 1/8 of the
+//               table T[b] (64 KB per 256-col block) per CTA; coset nibble tables G; zeroes the accumulators.
+//   k_gemv      grid (items, ncols), 512 thr: an item is one 256-col block b x 512 * tpw sorted rows of one tensor
+//               (up to 4 tensors sharing x run in one launch: q/k/v, gate/up). The block's T and G arrive by one bulk
+//               copy (TMA engine, mbarrier) while the warps load their first payload words; each lane owns one row
+//               and walks its 2 x 32 chunks: 1 PRMT (field byte + rotated chunk offset -> table address) + 1 LDS +
+//               1 add per chunk. Row partials go to int64 fixed-point accumulators with integer atomics (exact, so
+//               the result does not depend on arrival order); the last item of a row range (arrival counter)
+//               converts, adds the clamp delta and scatters y[prm[r]].
+// Both kernels use programmatic dependent launch: a GEMV's CTAs start while the previous kernel drains, stream
+// their weight tiles toward L2, and only then wait for the activation tables.
 // ================================================================================================================
 constexpr int kTabInts = 256 * 64;          // T ints per 256-column block: [f][hs][t]
 constexpr int kTabBytes = kTabInts * 4;      // 64 KB
 constexpr int kGInts = 128;                  // per half-slice: 8 nibble groups x 16
 constexpr int kGemvThreads = 512;
 constexpr int kGemvWarps = kGemvThreads / 32;
+constexpr int kMaxGroup = 4;
 constexpr uint32_t kWaitPolls = 1u << 20;  // a healthy table copy lands within a few polls
+constexpr double kFixScale = 4294967296.0; // fixed-point accumulators: 2^32 units per 1.0
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+struct GemvTensor {
+    const uint32_t *M, *D;
+    const uint16_t *S;
+    const int16_t *prm;
+    const int *cp;
+    const uint16_t *cc;
+    const float *cv;
+    float *Y;
+    int64_t ldy;
+    unsigned long long *acc;  // [ncols][rows]
+    unsigned int *cnt;        // [ncols][chunks]
+    int rows, ng, chunks, item0;
+};
 
 struct PrepArgs {
     const float *X;
@@ -232,20 +255,33 @@ struct PrepArgs {
     int *T;     // [ncols][nb][16384]
     int *G;     // [ncols][nsl][128]
     float *d;   // [ncols][nsl]
+    unsigned long long *zero64;  // accumulators to clear
+    size_t nzero64;
+    unsigned int *zero32;        // arrival counters to clear
+    size_t nzero32;
 };
 
 __global__ void __launch_bounds__(256) k_act_prep(PrepArgs a) {
     __shared__ int q_s[256];
-    __shared__ uint32_t A_s[256];
+    __shared__ uint32_t A_s[32];
     __shared__ int cx_s[64];
-    const int b = blockIdx.x, n = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
-    A_s[tid] = a.A[tid];
+    const int b = blockIdx.x, fg = blockIdx.y, n = blockIdx.z, tid = threadIdx.x, lane = tid & 31;
+    pdl_launch_dependents();
+    if (tid < 32) A_s[tid] = a.A[32 * fg + tid];
+    pdl_wait();  // x and the workspace belong to the previous kernel until it completes
+    {
+        const size_t nthreads = (size_t)gridDim.x * gridDim.y * gridDim.z * 256;
+        const size_t id = (((size_t)n * gridDim.y + fg) * gridDim.x + b) * 256 + tid;
+        for (size_t i = id; i < a.nzero64; i += nthreads) a.zero64[i] = 0ull;
+        for (size_t i = id; i < a.nzero32; i += nthreads) a.zero32[i] = 0u;
+    }
     if (tid < 32) {
         const float *x = a.X + (size_t)n * a.ldx + b * 256 + 8 * lane;
         const float *ic = a.ic + b * 256 + 8 * lane;
-        float v[8];
-#pragma unroll
-        for (int m = 0; m < 8; ++m) v[m] = __fmul_rn(x[m], ic[m]);
+        const float4 x0 = *reinterpret_cast<const float4 *>(x), x1 = *reinterpret_cast<const float4 *>(x + 4);
+        const float4 i0 = *reinterpret_cast<const float4 *>(ic), i1 = *reinterpret_cast<const float4 *>(ic + 4);
+        float v[8] = {__fmul_rn(x0.x, i0.x), __fmul_rn(x0.y, i0.y), __fmul_rn(x0.z, i0.z), __fmul_rn(x0.w, i0.w),
+                      __fmul_rn(x1.x, i1.x), __fmul_rn(x1.y, i1.y), __fmul_rn(x1.z, i1.z), __fmul_rn(x1.w, i1.w)};
         fwht256_warp(v, lane);
         float am = 0.f;
 #pragma unroll
@@ -255,17 +291,17 @@ __global__ void __launch_bounds__(256) k_act_prep(PrepArgs a) {
         const float d = __fdiv_rn(am, 8191.f), id = d > 0.f ? __fdiv_rn(1.f, d) : 0.f;
 #pragma unroll
         for (int m = 0; m < 8; ++m) q_s[8 * lane + m] = __float2int_rn(__fmul_rn(v[m], id));
-        if ((lane & 15) == 0) a.d[(size_t)n * a.nsl + 2 * b + (lane >> 4)] = d;
+        if (fg == 0 && (lane & 15) == 0) a.d[(size_t)n * a.nsl + 2 * b + (lane >> 4)] = d;
     }
     __syncthreads();
-    if (tid < 64) {  // <c, q_t> for the 64 chunks of the block
-        int cx = 0;
+    if (fg == 0) {
+        if (tid < 64) {  // <c, q_t> for the 64 chunks of the block
+            int cx = 0;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) cx += (int)(int8_t)(a.cs >> (8 * e)) * q_s[4 * tid + e];
-        cx_s[tid] = cx;
-    }
-    __syncthreads();
-    {
+            for (int e = 0; e < 4; ++e) cx += (int)(int8_t)(a.cs >> (8 * e)) * q_s[4 * tid + e];
+            cx_s[tid] = cx;
+        }
+        __syncthreads();
         const int hs = tid >> 7, grp = (tid >> 4) & 7, m = tid & 15;
         int gsum = 0;
 #pragma unroll
@@ -273,23 +309,26 @@ __global__ void __launch_bounds__(256) k_act_prep(PrepArgs a) {
             if ((m >> i) & 1) gsum += cx_s[hs * 32 + 4 * grp + i];
         a.G[((size_t)n * a.nsl + 2 * b + hs) * kGInts + grp * 16 + m] = gsum;
     }
-    const int ht = tid & 63;  // (hs, t) of this thread
+    // this CTA's 32 codebook entries x 64 (hs, t): thread = (f-quarter, hs, t), 8 entries each, coalesced stores
+    const int ht = tid & 63;
     const int q0 = q_s[4 * ht], q1 = q_s[4 * ht + 1], q2 = q_s[4 * ht + 2], q3 = q_s[4 * ht + 3];
-    int *T = a.T + ((size_t)n * a.nb + b) * kTabInts;
-#pragma unroll 8
-    for (int f = tid >> 6; f < 256; f += 4) {
+    int *T = a.T + ((size_t)n * a.nb + b) * kTabInts + (32 * fg) * 64;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int f = (tid >> 6) + 4 * i;
         const uint32_t w = A_s[f];
         T[f * 64 + ht] = (int)(int8_t)w * q0 + (int)(int8_t)(w >> 8) * q1 + (int)(int8_t)(w >> 16) * q2 + (int)(int8_t)(w >> 24) * q3;
     }
 }
 
 struct GemvArgs {
-    const uint32_t *M, *D;
-    const uint16_t *S;
+    GemvTensor t[kMaxGroup];
+    int ntensors;
     const int *T, *G;
     const float *d;
-    float *part;  // [ncols][nb][rows]
-    int rows, nb, ng, nsl, tpw, chunks;
+    const float *X;
+    int64_t ldx;
+    int nb, nsl, tpw;
 };
 
 // PRMT selector for step k: result byte 0 = chunk offset byte (k % 3) of po[k / 3], byte 1 = field byte (k % 4) of the
@@ -359,31 +398,47 @@ __device__ __forceinline__ float tile_row_dot(const uint32_t *p0, const uint32_t
     return __fadd_rn(__fmul_rn((float)i0, d0), __fmul_rn((float)i1, d1));
 }
 
-__global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(GemvArgs a) {
+__device__ __forceinline__ float tile_row_any(int c, const uint32_t *p0, const uint32_t (&po)[11], const char *Ts, const int *Gs, int lane,
+                                              float d0, float d1) {
+    switch (c) {
+        case 0: return 0.f;
+        case 1: return tile_row_dot<1>(p0, po, Ts, Gs, lane, d0, d1);
+        case 2: return tile_row_dot<2>(p0, po, Ts, Gs, lane, d0, d1);
+        case 3: return tile_row_dot<3>(p0, po, Ts, Gs, lane, d0, d1);
+        case 4: return tile_row_dot<4>(p0, po, Ts, Gs, lane, d0, d1);
+        case 5: return tile_row_dot<5>(p0, po, Ts, Gs, lane, d0, d1);
+        case 6: return tile_row_dot<6>(p0, po, Ts, Gs, lane, d0, d1);
+        default: return tile_row_dot<7>(p0, po, Ts, Gs, lane, d0, d1);
+    }
+}
+
+__global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(const __grid_constant__ GemvArgs a) {
     extern __shared__ __align__(128) uint8_t sm[];
     int *Ts = reinterpret_cast<int *>(sm);
     int *Gs = Ts + kTabInts;
     uint64_t *bar = reinterpret_cast<uint64_t *>(Gs + 2 * kGInts);
-    const int b = blockIdx.x % a.nb, chunk = blockIdx.x / a.nb, n = blockIdx.y;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    __shared__ int s_last;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, n = blockIdx.y;
+    // item -> (tensor, block, row chunk)
+    int ti = 0;
+#pragma unroll
+    for (int i = 1; i < kMaxGroup; ++i)
+        if (i < a.ntensors && (int)blockIdx.x >= a.t[i].item0) ti = i;
+    const GemvTensor &T = a.t[ti];
+    const int item = blockIdx.x - T.item0, b = item % a.nb, chunk = item / a.nb;
+    const int g_first = chunk * kGemvWarps * a.tpw + warp;
+    pdl_launch_dependents();
     if (tid == 0) {
         mbar_init(bar, 1);
         fence_mbar_init();
     }
-    __syncthreads();
-    if (tid == 0) {
-        mbar_expect_tx(bar, kTabBytes + 2 * kGInts * 4);
-        bulk_g2s(Ts, a.T + ((size_t)n * a.nb + b) * kTabInts, kTabBytes, bar);
-        bulk_g2s(Gs, a.G + ((size_t)n * a.nsl + 2 * b) * kGInts, 2 * kGInts * 4, bar);
-    }
-    const int g_first = chunk * kGemvWarps * a.tpw + warp;
-    if (lane == 0) {  // stream this warp's tile payloads toward L2 while the tables arrive
+    if (lane == 0) {  // stream this warp's tile payloads toward L2 before waiting on the producer of x
         for (int i = 0; i < a.tpw; ++i) {
             const int g = g_first + kGemvWarps * i;
-            if (g >= a.ng) break;
-            const uint32_t mt = __ldg(a.M + (size_t)g * a.nb + b);
+            if (g >= T.ng) break;
+            const uint32_t mt = __ldg(T.M + (size_t)g * a.nb + b);
             const int c = (int)(mt >> 29);
-            if (c) bulk_prefetch_l2(a.D + (mt & 0x1FFFFFFFu), (uint32_t)NW(c) * 256u);
+            if (c) bulk_prefetch_l2(T.D + (mt & 0x1FFFFFFFu), (uint32_t)NW(c) * 256u);
         }
     }
     uint32_t po[11];
@@ -395,6 +450,13 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(GemvArgs a) {
             if (3 * q + i < 32) r |= (((uint32_t)(lane + 3 * q + i) & 31u) << 2) << (8 * i);
         po[q] = r;
     }
+    pdl_wait();  // tables, accumulators and x are written by the preceding prep kernel
+    __syncthreads();
+    if (tid == 0) {
+        mbar_expect_tx(bar, kTabBytes + 2 * kGInts * 4);
+        bulk_g2s(Ts, a.T + ((size_t)n * a.nb + b) * kTabInts, kTabBytes, bar);
+        bulk_g2s(Gs, a.G + ((size_t)n * a.nsl + 2 * b) * kGInts, 2 * kGInts * 4, bar);
+    }
     const float d0 = a.d[(size_t)n * a.nsl + 2 * b], d1 = a.d[(size_t)n * a.nsl + 2 * b + 1];
     if (!mbar_wait_bounded(bar, 0, kWaitPolls)) {
         if (lane == 0) atomicOr(&g_p8_device_error, 1u);
@@ -402,107 +464,148 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(GemvArgs a) {
         return;
     }
     const char *Tc = reinterpret_cast<const char *>(Ts);
+    unsigned long long *acc = T.acc + (size_t)n * T.rows;
     for (int i = 0; i < a.tpw; ++i) {
         const int g = g_first + kGemvWarps * i;
-        if (g >= a.ng) break;
-        const uint32_t mt = __ldg(a.M + (size_t)g * a.nb + b);
-        const int c = (int)(mt >> 29);
-        const uint32_t *p0 = a.D + (mt & 0x1FFFFFFFu);
-        float acc = 0.f;
-        switch (c) {
-            case 0: break;
-            case 1: acc = tile_row_dot<1>(p0, po, Tc, Gs, lane, d0, d1); break;
-            case 2: acc = tile_row_dot<2>(p0, po, Tc, Gs, lane, d0, d1); break;
-            case 3: acc = tile_row_dot<3>(p0, po, Tc, Gs, lane, d0, d1); break;
-            case 4: acc = tile_row_dot<4>(p0, po, Tc, Gs, lane, d0, d1); break;
-            case 5: acc = tile_row_dot<5>(p0, po, Tc, Gs, lane, d0, d1); break;
-            case 6: acc = tile_row_dot<6>(p0, po, Tc, Gs, lane, d0, d1); break;
-            default: acc = tile_row_dot<7>(p0, po, Tc, Gs, lane, d0, d1); break;
-        }
+        if (g >= T.ng) break;
+        const uint32_t mt = __ldg(T.M + (size_t)g * a.nb + b);
+        const float part = tile_row_any((int)(mt >> 29), T.D + (mt & 0x1FFFFFFFu), po, Tc, Gs, lane, d0, d1);
         const int r = g * 32 + lane;
-        a.part[((size_t)n * a.nb + b) * a.rows + r] = __fmul_rn(acc, h2f(a.S[(size_t)b * a.rows + r]));
+        const float v = __fmul_rn(part, h2f(T.S[(size_t)b * T.rows + r]));
+        atomicAdd(acc + r, (unsigned long long)__double2ll_rn((double)v * kFixScale));
+    }
+    // arrival counter of this row chunk; the last of its nb items finishes the rows
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        const unsigned prev = atomicAdd(T.cnt + (size_t)n * T.chunks + chunk, 1u);
+        s_last = prev == (unsigned)(a.nb - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const int r0 = chunk * kGemvWarps * a.tpw * 32, r1 = min(T.rows, r0 + kGemvWarps * a.tpw * 32);
+    const float *x = a.X + (size_t)n * a.ldx;
+    for (int r = r0 + tid; r < r1; r += kGemvThreads) {
+        const long long s = (long long)__ldcg(acc + r);
+        float v = (float)((double)s * (1.0 / kFixScale));
+        const int ro = T.prm[r];
+        for (int e = T.cp[ro]; e < T.cp[ro + 1]; ++e) v = __fadd_rn(v, __fmul_rn(T.cv[e], x[T.cc[e]]));
+        T.Y[(size_t)n * T.ldy + ro] = v;
     }
 }
 
-struct ReduceArgs {
-    const float *part;
-    const int16_t *prm;
-    const int *cp;
-    const uint16_t *cc;
-    const float *cv;
-    const float *X;
-    int64_t ldx;
-    float *Y;
-    int64_t ldy;
-    int rows, nb;
-};
-
-__global__ void __launch_bounds__(256) k_gemv_reduce(ReduceArgs a) {
-    const int r = blockIdx.x * 256 + threadIdx.x, n = blockIdx.y;
-    if (r >= a.rows) return;
-    const float *p = a.part + (size_t)n * a.nb * a.rows + r;
-    float s = 0.f;
-    for (int b = 0; b < a.nb; ++b) s = __fadd_rn(s, p[(size_t)b * a.rows]);
-    const int ro = a.prm[r];
-    const float *x = a.X + (size_t)n * a.ldx;
-    for (int e = a.cp[ro]; e < a.cp[ro + 1]; ++e) s = __fadd_rn(s, __fmul_rn(a.cv[e], x[a.cc[e]]));
-    a.Y[(size_t)n * a.ldy + ro] = s;
-}
-
-// workspace layout (bytes, each part 256-aligned): T | G | d | partials
+// workspace layout (bytes, each part 256-aligned): T | G | d | acc (int64 per row) | counters
 struct GemvWs {
-    size_t T, G, d, part, total;
+    size_t T, G, d, acc, cnt, total;
 };
 static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
-static GemvWs gemv_ws_layout(const p8_tensor *t, int64_t ncols) {
+static int gemv_tpw_for(int ng_total, int nb) {
+    // rows per item = 512 * tpw: the largest that still leaves ~2 items per SM (148 SMs) in the launch
+    int tpw = 1;
+    while (tpw < 8 && (size_t)nb * (size_t)((ng_total + kGemvWarps * tpw * 2 - 1) / (kGemvWarps * tpw * 2)) >= 296) tpw *= 2;
+    return tpw;
+}
+static GemvWs gemv_ws_layout(const p8_tensor *const *ts, int nt, int64_t ncols, int tpw) {
+    const p8_tensor *t = ts[0];
+    size_t rows = 0, chunks = 0;
+    for (int i = 0; i < nt; ++i) {
+        rows += (size_t)ts[i]->rows;
+        chunks += (size_t)((ts[i]->ng + kGemvWarps * tpw - 1) / (kGemvWarps * tpw));
+    }
     GemvWs w;
     w.T = 0;
     w.G = w.T + al256((size_t)ncols * t->nb * kTabBytes);
     w.d = w.G + al256((size_t)ncols * t->nsl * kGInts * 4);
-    w.part = w.d + al256((size_t)ncols * t->nsl * 4);
-    w.total = w.part + al256((size_t)ncols * t->nb * t->rows * 4);
+    w.acc = w.d + al256((size_t)ncols * t->nsl * 4);
+    w.cnt = w.acc + al256((size_t)ncols * rows * 8);
+    w.total = w.cnt + al256((size_t)ncols * chunks * 4);
     return w;
 }
-size_t gemv_workspace(const p8_tensor *t, int64_t ncols) { return gemv_ws_layout(t, ncols).total; }
+size_t gemv_workspace(const p8_tensor *t, int64_t ncols) {
+    // sized for the smallest row chunk (tpw = 1): covers every tpw choice
+    return gemv_ws_layout(&t, 1, ncols, 1).total;
+}
+size_t gemv_group_workspace(const p8_tensor *const *ts, int nt, int64_t ncols) { return gemv_ws_layout(ts, nt, ncols, 1).total; }
 
-static int gemv_tpw(const p8_tensor *t) {
-    // rows per CTA = 512 * tpw: aim at >= 2 CTAs per SM in flight without shrinking a CTA below 512 rows
-    const int sms = 148;
-    int tpw = 1;
-    while (tpw < 4 && (size_t)t->nb * ((t->ng + kGemvWarps * (tpw * 2) - 1) / (kGemvWarps * (tpw * 2))) >= (size_t)2 * sms) tpw *= 2;
-    return tpw;
+static cudaError_t launch_pdl(const void *fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void **args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
-p8_status launch_gemv(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy, void *ws, size_t ws_bytes,
-                      cudaStream_t st) {
-    const GemvWs L = gemv_ws_layout(t, ncols);
-    if (!ws || ws_bytes < L.total) return P8_ERR_WORKSPACE;
+p8_status launch_gemv_group(const p8_tensor *const *ts, int nt, const float *X, int64_t ncols, int64_t ldx, float *const *Ys,
+                            const int64_t *ldys, void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (nt < 1 || nt > kMaxGroup) return P8_ERR_ARG;
+    const p8_tensor *t0 = ts[0];
+    int ng_total = 0;
+    for (int i = 0; i < nt; ++i) {
+        // tensors of one launch share x and its table: same K, column scales, signs and codebook (content hash)
+        if (ts[i]->K != t0->K || ts[i]->act_hash != t0->act_hash) return P8_ERR_ARG;
+        ng_total += ts[i]->ng;
+    }
     if (ncols > 65535) return P8_ERR_ARG;
+    const int tpw = gemv_tpw_for(ng_total, t0->nb);
+    const GemvWs L = gemv_ws_layout(ts, nt, ncols, tpw);
+    if (!ws || ws_bytes < L.total) return P8_ERR_WORKSPACE;
     uint8_t *w = static_cast<uint8_t *>(ws);
     PrepArgs pa;
-    pa.X = X; pa.ldx = ldx; pa.ic = t->ic; pa.A = t->A; pa.cs = t->cs; pa.K = t->K; pa.nb = t->nb; pa.nsl = t->nsl;
+    pa.X = X; pa.ldx = ldx; pa.ic = t0->ic; pa.A = t0->A; pa.cs = t0->cs; pa.K = t0->K; pa.nb = t0->nb; pa.nsl = t0->nsl;
     pa.T = reinterpret_cast<int *>(w + L.T);
     pa.G = reinterpret_cast<int *>(w + L.G);
     pa.d = reinterpret_cast<float *>(w + L.d);
-    k_act_prep<<<dim3(t->nb, (unsigned)ncols), 256, 0, st>>>(pa);
+    pa.zero64 = reinterpret_cast<unsigned long long *>(w + L.acc);
+    pa.nzero64 = (L.cnt - L.acc) / 8;
+    pa.zero32 = reinterpret_cast<unsigned int *>(w + L.cnt);
+    pa.nzero32 = (L.total - L.cnt) / 4;
+    {
+        void *args[] = {&pa};
+        if (launch_pdl((const void *)k_act_prep, dim3(t0->nb, 8, (unsigned)ncols), dim3(256), 0, st, args) != cudaSuccess)
+            return P8_ERR_CUDA;
+    }
     GemvArgs ga;
-    ga.M = t->M; ga.D = t->D; ga.S = t->S; ga.T = pa.T; ga.G = pa.G; ga.d = pa.d;
-    ga.part = reinterpret_cast<float *>(w + L.part);
-    ga.rows = t->rows; ga.nb = t->nb; ga.ng = t->ng; ga.nsl = t->nsl;
-    ga.tpw = gemv_tpw(t);
-    ga.chunks = (t->ng + kGemvWarps * ga.tpw - 1) / (kGemvWarps * ga.tpw);
+    memset(&ga, 0, sizeof(ga));
+    ga.ntensors = nt; ga.T = pa.T; ga.G = pa.G; ga.d = pa.d; ga.X = X; ga.ldx = ldx;
+    ga.nb = t0->nb; ga.nsl = t0->nsl; ga.tpw = tpw;
+    int item0 = 0;
+    size_t acc_off = 0, cnt_off = 0;
+    for (int i = 0; i < nt; ++i) {
+        const p8_tensor *t = ts[i];
+        GemvTensor &g = ga.t[i];
+        g.M = t->M; g.D = t->D; g.S = t->S; g.prm = t->prm; g.cp = t->cp; g.cc = t->cc; g.cv = t->cv;
+        g.Y = Ys[i]; g.ldy = ldys[i];
+        g.rows = t->rows; g.ng = t->ng;
+        g.chunks = (t->ng + kGemvWarps * tpw - 1) / (kGemvWarps * tpw);
+        g.item0 = item0;
+        g.acc = pa.zero64 + acc_off * ncols;
+        g.cnt = pa.zero32 + cnt_off * ncols;
+        acc_off += (size_t)t->rows;
+        cnt_off += (size_t)g.chunks;
+        item0 += g.chunks * t->nb;
+    }
     const size_t smem = kTabBytes + 2 * kGInts * 4 + 16;
     static bool attr_set = false;
     if (!attr_set) {
         if (cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return P8_ERR_CUDA;
         attr_set = true;
     }
-    k_gemv<<<dim3((unsigned)(t->nb * ga.chunks), (unsigned)ncols), kGemvThreads, smem, st>>>(ga);
-    ReduceArgs ra;
-    ra.part = ga.part; ra.prm = t->prm; ra.cp = t->cp; ra.cc = t->cc; ra.cv = t->cv; ra.X = X; ra.ldx = ldx; ra.Y = Y; ra.ldy = ldy;
-    ra.rows = t->rows; ra.nb = t->nb;
-    k_gemv_reduce<<<dim3((unsigned)((t->rows + 255) / 256), (unsigned)ncols), 256, 0, st>>>(ra);
-    return cudaGetLastError() == cudaSuccess ? P8_OK : P8_ERR_CUDA;
+    void *args[] = {&ga};
+    if (launch_pdl((const void *)k_gemv, dim3((unsigned)item0, (unsigned)ncols), dim3(kGemvThreads), smem, st, args) != cudaSuccess)
+        return P8_ERR_CUDA;
+    return P8_OK;
+}
+
+p8_status launch_gemv(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy, void *ws, size_t ws_bytes,
+                      cudaStream_t st) {
+    return launch_gemv_group(&t, 1, X, ncols, ldx, &Y, &ldy, ws, ws_bytes, st);
 }
 
 unsigned int read_and_clear_device_error() {

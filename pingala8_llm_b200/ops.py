@@ -116,6 +116,27 @@ class P8Tensor:
             pass
 
 
+def group_workspace_size(tensors, ncols=1):
+    arr = (C.c_void_p * len(tensors))(*[t.handle.value for t in tensors])
+    return int(lib().p8_workspace_size_group(arr, len(tensors), ncols))
+
+
+def mul_mat_vec_group(tensors, x, outs=None, workspace=None, stream=None):
+    """y_i = W_i x for tensors sharing x (q/k/v, gate/up): one prepared activation, one launch (<= 4 tensors)."""
+    x = x.contiguous()
+    if x.dtype != torch.float32 or not x.is_cuda or x.numel() != tensors[0].K:
+        raise ValueError("x must be float32 CUDA with K elements")
+    outs = outs if outs is not None else [torch.empty(t.rows, dtype=torch.float32, device=x.device) for t in tensors]
+    n = len(tensors)
+    arr = (C.c_void_p * n)(*[t.handle.value for t in tensors])
+    ys = (C.c_void_p * n)(*[o.data_ptr() for o in outs])
+    if workspace is None:
+        workspace = torch.empty(max(group_workspace_size(tensors), 256), dtype=torch.uint8, device=x.device)
+    check(lib().p8_mul_mat_vec_group(arr, n, _ptr(x), ys, _ptr(workspace), workspace.numel(), _stream(stream)),
+          "p8_mul_mat_vec_group")
+    return outs
+
+
 def active(slot):
     """ggml_cuda_f44_active: is this device slot a prepared Pingala-8 tensor?"""
     return bool(lib().p8_active(_ptr(slot)))

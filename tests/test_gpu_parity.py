@@ -162,6 +162,23 @@ def test_mixed_class_tiles_vs_oracle():
     assert rel(t.mul_mat_vec(torch.from_numpy(x).cuda()).cpu().numpy(), o.mul_mat(x)[0]) < TIGHT
 
 
+def test_group_gemv_equals_single_calls():
+    """q/k/v (and gate/up) as one grouped launch == three single calls, bit for bit (exact fixed-point accumulation)."""
+    from pingala8_llm_b200.ops import mul_mat_vec_group
+
+    shapes = [(1024, 2048), (256, 2048), (256, 2048)]
+    ts = [P8Tensor(synth.make_slot(r, k, seed=40 + i, nd=3 * i), k, r) for i, (r, k) in enumerate(shapes)]
+    x = torch.randn(2048, device="cuda")
+    ys = mul_mat_vec_group(ts, x)
+    for t, y in zip(ts, ys):
+        assert torch.equal(y, t.mul_mat_vec(x))
+    o = Oracle(ts[0].slot.cpu().numpy(), 1024, 2048)
+    assert rel(ys[0].cpu().numpy(), o.mul_mat(x.cpu().numpy())[0]) < TIGHT
+    other = P8Tensor(synth.make_slot(256, 2048, seed=1, c16="random"), 2048, 256)
+    with pytest.raises(p8.P8Error):  # different column scales: cannot share the prepared activation
+        mul_mat_vec_group([ts[0], other], x)
+
+
 # --------------------------------------------------------------------------- error behaviour through the C ABI
 def test_prepare_rejects_corrupted_device_slot():
     f = load_fixture("cls3_64x512")
