@@ -1,0 +1,52 @@
+"""Run one grouped GEMV of a model shape repeatedly: a small, self-contained case for profilers (ncu) and timing.
+
+usage: python -m pingala8_llm_b200.profile [--group gate_up|qkv|o|down] [--iters N] [--copies C]
+
+Weights are seeded synthetic class-3 slots of the Llama-3.1-8B shapes. With --copies > 1 the calls rotate over
+distinct weight copies so repeated calls read DRAM rather than L2. Prints the mean time per call (CUDA events).
+"""
+import argparse
+
+import torch
+
+from . import synth
+from .ops import P8Tensor, group_workspace_size, mul_mat_vec_group
+
+GROUPS = {  # Llama-3.1-8B: (rows, K) per tensor of a group that reads one x
+    "qkv": [(4096, 4096), (1024, 4096), (1024, 4096)],
+    "o": [(4096, 4096)],
+    "gate_up": [(14336, 4096), (14336, 4096)],
+    "down": [(4096, 14336)],
+}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--group", default="gate_up", choices=sorted(GROUPS))
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--copies", type=int, default=1)
+    a = ap.parse_args()
+    shapes = GROUPS[a.group]
+    copies = []
+    for c in range(a.copies):
+        copies.append([P8Tensor(synth.make_slot_device(r, k, seed=100 * c + i), k, r) for i, (r, k) in enumerate(shapes)])
+    K = shapes[0][1]
+    x = torch.randn(K, device="cuda")
+    outs = [torch.empty(r, device="cuda") for r, _ in shapes]
+    ws = torch.empty(max(group_workspace_size(ts) for ts in copies), dtype=torch.uint8, device="cuda")
+    for ts in copies:  # warm-up
+        mul_mat_vec_group(ts, x, outs=outs, workspace=ws)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(a.iters):
+        mul_mat_vec_group(copies[i % len(copies)], x, outs=outs, workspace=ws)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / a.iters
+    nbytes = sum((r // 32) * (k // 256) * (68 + 2048) for r, k in shapes)
+    print(f"group {a.group}: {us:.2f} us/call, {nbytes / us / 1e3:.1f} GB/s (algorithmic, class 3)")
+
+
+if __name__ == "__main__":
+    main()
