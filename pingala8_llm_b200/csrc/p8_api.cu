@@ -35,6 +35,7 @@ void free_tensor(p8_tensor *t) {
     cudaFree(t->cp);
     cudaFree(t->cc);
     cudaFree(t->cv);
+    cudaFree(t->tile_cnt);
     t->magic = 0;
     delete t;
 }
@@ -43,7 +44,7 @@ void free_tensor(p8_tensor *t) {
 extern "C" {
 
 p8_status p8_prepare(const void *dev_slot, size_t nbytes, int64_t K, int64_t rows, void *stream, p8_tensor **out) {
-    if (!dev_slot || !out) return P8_ERR_ARG;
+    if (!dev_slot || !out || ((uintptr_t)dev_slot & 15)) return P8_ERR_ARG;  // kernels stream the slot in 16-byte units
     *out = nullptr;
     p8_status st = check_shape(K, rows);
     if (st) return st;
@@ -130,7 +131,9 @@ p8_status p8_prepare(const void *dev_slot, size_t nbytes, int64_t K, int64_t row
         t->act_hash = h;
     }
     if (dmalloc_copy(&t->ic, ic.data(), ic.size()) != cudaSuccess || dmalloc_copy(&t->cp, cp.data(), cp.size()) != cudaSuccess ||
-        dmalloc_copy(&t->cc, cc.data(), cc.size()) != cudaSuccess || dmalloc_copy(&t->cv, cv.data(), cv.size()) != cudaSuccess) {
+        dmalloc_copy(&t->cc, cc.data(), cc.size()) != cudaSuccess || dmalloc_copy(&t->cv, cv.data(), cv.size()) != cudaSuccess ||
+        cudaMalloc((void **)&t->tile_cnt, sizeof(unsigned int) * ng) != cudaSuccess ||
+        cudaMemset(t->tile_cnt, 0, sizeof(unsigned int) * ng) != cudaSuccess) {
         free_tensor(t);
         return P8_ERR_CUDA;
     }

@@ -207,17 +207,18 @@ cudaError_t launch_get_rows(const p8_tensor *t, const int32_t *ids, int64_t n, f
 // T[f][hs][t] = <A[f], q_t> (exact int32). The integer sums equal the reference's exact integer dot products, so the
 // only difference to the CPU result is float rounding in the final scale-and-sum.
 //
-//   k_act_prep  grid (nb, 8, ncols), 256 thr: x -> FWHT(x sgn/c)/16 -> q, d (per 128-col half-slice); 1/8 of the
-//               table T[b] (64 KB per 256-col block) per CTA; coset nibble tables G; zeroes the accumulators.
-//   k_gemv      grid (items, ncols), 512 thr: an item is one 256-col block b x 512 * tpw sorted rows of one tensor
-//               (up to 4 tensors sharing x run in one launch: q/k/v, gate/up). The block's T and G arrive by one bulk
-//               copy (TMA engine, mbarrier) while the warps load their first payload words; each lane owns one row
-//               and walks its 2 x 32 chunks: 1 PRMT (field byte + rotated chunk offset -> table address) + 1 LDS +
-//               1 add per chunk. Row partials go to int64 fixed-point accumulators with integer atomics (exact, so
-//               the result does not depend on arrival order); the last item of a row range (arrival counter)
-//               converts, adds the clamp delta and scatters y[prm[r]].
-// Both kernels use programmatic dependent launch: a GEMV's CTAs start while the previous kernel drains, stream
-// their weight tiles toward L2, and only then wait for the activation tables.
+//   k_act_prep  grid (nb, 8), 256 thr: first streams the group's weight tiles toward L2 (they do not depend on x),
+//               then waits for the producer of x; x -> FWHT(x sgn/c)/16 -> q, d per 128-col half-slice; 1/8 of the
+//               table T[b] (64 KB per 256-col block) per CTA; coset nibble tables G.
+//   k_gemv      persistent, one 512-thread CTA per SM. The work is the list of (block b, tile g) units of up to four
+//               tensors that read the same x, ordered block-major and cut into equal contiguous ranges, so a CTA
+//               touches at most a few blocks. Block tables arrive by bulk copy (TMA engine, mbarrier), double
+//               buffered; the payload words of a warp's next unit are loaded into registers while the current unit
+//               computes. Each lane owns one row: per chunk 1 PRMT (field byte + rotated chunk offset -> table byte
+//               address) + 1 LDS + 1 add. A unit stores its 32 row partials (plain coalesced stores, [b][rows]); the
+//               warp that completes a tile's last block (per-tile arrival counter) sums its partials in block order,
+//               adds the clamp delta and scatters y[prm[r]] (deterministic, no float atomics).
+// Both kernels use programmatic dependent launch.
 // ================================================================================================================
 constexpr int kTabInts = 256 * 64;          // T ints per 256-column block: [f][hs][t]
 constexpr int kTabBytes = kTabInts * 4;      // 64 KB
@@ -226,7 +227,9 @@ constexpr int kGemvThreads = 512;
 constexpr int kGemvWarps = kGemvThreads / 32;
 constexpr int kMaxGroup = 4;
 constexpr uint32_t kWaitPolls = 1u << 20;  // a healthy table copy lands within a few polls
-constexpr double kFixScale = 4294967296.0; // fixed-point accumulators: 2^32 units per 1.0
+// dynamic shared memory of k_gemv: two table buffers, two G buffers (both half-slices), two mbarriers
+constexpr int kSmemT0 = 0, kSmemT1 = kTabBytes, kSmemG0 = 2 * kTabBytes, kSmemG1 = kSmemG0 + 2 * kGInts * 4,
+              kSmemBar = kSmemG1 + 2 * kGInts * 4, kGemvSmem = kSmemBar + 16;
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -239,44 +242,45 @@ struct GemvTensor {
     const uint16_t *cc;
     const float *cv;
     float *Y;
-    int64_t ldy;
-    unsigned long long *acc;  // [ncols][rows]
-    unsigned int *cnt;        // [ncols][chunks]
-    int rows, ng, chunks, item0;
+    float *part;          // [nb][rows] row partials per block
+    unsigned int *cnt;    // [ng] per-tile arrival counters (tensor-owned, zero between calls)
+    size_t dbytes;        // payload bytes (for the L2 prefetch)
+    int rows, ng, g0;     // g0: first unit index of this tensor inside one block
 };
 
 struct PrepArgs {
     const float *X;
-    int64_t ldx;
     const float *ic;
     const uint32_t *A;
     uint32_t cs;
-    int K, nb, nsl;
-    int *T;     // [ncols][nb][16384]
-    int *G;     // [ncols][nsl][128]
-    float *d;   // [ncols][nsl]
-    unsigned long long *zero64;  // accumulators to clear
-    size_t nzero64;
-    unsigned int *zero32;        // arrival counters to clear
-    size_t nzero32;
+    int K, nb, nsl, ntensors;
+    int *T;     // [nb][16384]
+    int *G;     // [nsl][128]
+    float *d;   // [nsl]
+    const uint8_t *pf[kMaxGroup];  // weight regions to stream toward L2 before waiting (M..D of each tensor)
+    size_t pfbytes[kMaxGroup];
 };
 
 __global__ void __launch_bounds__(256) k_act_prep(PrepArgs a) {
     __shared__ int q_s[256];
     __shared__ uint32_t A_s[32];
     __shared__ int cx_s[64];
-    const int b = blockIdx.x, fg = blockIdx.y, n = blockIdx.z, tid = threadIdx.x, lane = tid & 31;
+    const int b = blockIdx.x, fg = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
     pdl_launch_dependents();
+    {   // the weights do not depend on the producer of x: start their HBM -> L2 stream now (16 KB pieces)
+        const size_t nthreads = (size_t)gridDim.x * gridDim.y * 256, id = ((size_t)fg * gridDim.x + b) * 256 + tid;
+        for (int i = 0; i < a.ntensors; ++i) {
+            const size_t pieces = (a.pfbytes[i] + 16383) / 16384;
+            for (size_t p = id; p < pieces; p += nthreads) {
+                const size_t off = p * 16384, len = a.pfbytes[i] - off < 16384 ? a.pfbytes[i] - off : 16384;
+                bulk_prefetch_l2(a.pf[i] + off, (uint32_t)(len & ~(size_t)15));
+            }
+        }
+    }
     if (tid < 32) A_s[tid] = a.A[32 * fg + tid];
     pdl_wait();  // x and the workspace belong to the previous kernel until it completes
-    {
-        const size_t nthreads = (size_t)gridDim.x * gridDim.y * gridDim.z * 256;
-        const size_t id = (((size_t)n * gridDim.y + fg) * gridDim.x + b) * 256 + tid;
-        for (size_t i = id; i < a.nzero64; i += nthreads) a.zero64[i] = 0ull;
-        for (size_t i = id; i < a.nzero32; i += nthreads) a.zero32[i] = 0u;
-    }
     if (tid < 32) {
-        const float *x = a.X + (size_t)n * a.ldx + b * 256 + 8 * lane;
+        const float *x = a.X + b * 256 + 8 * lane;
         const float *ic = a.ic + b * 256 + 8 * lane;
         const float4 x0 = *reinterpret_cast<const float4 *>(x), x1 = *reinterpret_cast<const float4 *>(x + 4);
         const float4 i0 = *reinterpret_cast<const float4 *>(ic), i1 = *reinterpret_cast<const float4 *>(ic + 4);
@@ -291,7 +295,7 @@ __global__ void __launch_bounds__(256) k_act_prep(PrepArgs a) {
         const float d = __fdiv_rn(am, 8191.f), id = d > 0.f ? __fdiv_rn(1.f, d) : 0.f;
 #pragma unroll
         for (int m = 0; m < 8; ++m) q_s[8 * lane + m] = __float2int_rn(__fmul_rn(v[m], id));
-        if (fg == 0 && (lane & 15) == 0) a.d[(size_t)n * a.nsl + 2 * b + (lane >> 4)] = d;
+        if (fg == 0 && (lane & 15) == 0) a.d[2 * b + (lane >> 4)] = d;
     }
     __syncthreads();
     if (fg == 0) {
@@ -307,12 +311,12 @@ __global__ void __launch_bounds__(256) k_act_prep(PrepArgs a) {
 #pragma unroll
         for (int i = 0; i < 4; ++i)
             if ((m >> i) & 1) gsum += cx_s[hs * 32 + 4 * grp + i];
-        a.G[((size_t)n * a.nsl + 2 * b + hs) * kGInts + grp * 16 + m] = gsum;
+        a.G[(2 * b + hs) * kGInts + grp * 16 + m] = gsum;
     }
     // this CTA's 32 codebook entries x 64 (hs, t): thread = (f-quarter, hs, t), 8 entries each, coalesced stores
     const int ht = tid & 63;
     const int q0 = q_s[4 * ht], q1 = q_s[4 * ht + 1], q2 = q_s[4 * ht + 2], q3 = q_s[4 * ht + 3];
-    int *T = a.T + ((size_t)n * a.nb + b) * kTabInts + (32 * fg) * 64;
+    int *T = a.T + (size_t)b * kTabInts + (32 * fg) * 64;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int f = (tid >> 6) + 4 * i;
@@ -327,119 +331,156 @@ struct GemvArgs {
     const int *T, *G;
     const float *d;
     const float *X;
-    int64_t ldx;
-    int nb, nsl, tpw;
+    int nb, nsl, ng_total;
+    long long units;  // nb * ng_total
 };
 
-// PRMT selector for step k: result byte 0 = chunk offset byte (k % 3) of po[k / 3], byte 1 = field byte (k % 4) of the
-// word, bytes 2-3 = po's zero byte 3 -> (field << 8) | (((lane + k) & 31) * 4) = byte offset into T[f][hs][t].
+extern __shared__ __align__(1024) uint8_t g_smem[];
+
+// table byte address of the chunk at step k: PRMT places the field byte (k % 4 of word k / 4) in bits 8-15 and the
+// lane's rotated chunk offset ((lane + k) & 31) * 4 (byte k % 3 of po[k / 3]; po byte 3 is zero) in bits 0-7.
 template <int k>
 struct Sel {
     static constexpr uint32_t v = (uint32_t)(4 + k % 3) | ((uint32_t)(k % 4) << 4) | 0x7700u;
 };
 
+__device__ __forceinline__ int lds32(uint32_t saddr) {
+    int v;
+    asm("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(saddr));
+    return v;
+}
+
 template <int C, int k>
-__device__ __forceinline__ int stage_sum_step(const uint32_t (&w)[24], const uint32_t (&po)[11], const char *Th, int lane, int stage) {
+__device__ __forceinline__ uint32_t stage_addr(const uint32_t (&w)[24], const uint32_t (&po)[11], int lane, int stage) {
     constexpr int w1 = W1(C), w2 = W2(C), w3 = W3(C);
     const int W = stage == 0 ? w1 : stage == 1 ? w2 : w3;
     const int wb = stage == 0 ? 0 : stage == 1 ? w1 : w1 + w2;
-    uint32_t addr;
-    if (W == 8) {
-        addr = __byte_perm(w[wb + k / 4], po[k / 3], Sel<k>::v);
+    if (W == 8) return __byte_perm(w[wb + k / 4], po[k / 3], Sel<k>::v);
+    const uint32_t off = ((uint32_t)(lane + k) & 31u) << 2;
+    uint32_t f;
+    if (stage == 0) {
+        constexpr int we = w1 > 1 ? w1 - 1 : 1, pos = we * k, bb = pos % 32;
+        f = w[1 + pos / 32] >> bb;
+        if (bb + we > 32) f |= w[2 + pos / 32] << ((32 - bb) & 31);
+        f = (f & ((1u << we) - 1u)) | (((w[0] >> k) & 1u) << we);
     } else {
-        const uint32_t off = ((uint32_t)(lane + k) & 31u) << 2;
-        uint32_t f;
-        if (stage == 0) f = ((w[1 + ((w1 - 1) * k) / 32] >> (((w1 - 1) * k) % 32)) |
-                             ((((w1 - 1) * k) % 32 + (w1 - 1) > 32) ? (w[2 + ((w1 - 1) * k) / 32] << (32 - ((w1 - 1) * k) % 32)) : 0u)) &
-                            ((1u << (w1 - 1)) - 1u);
-        else f = (w[wb + (W * k) / 32] >> ((W * k) % 32)) & ((1u << W) - 1u);
-        if (stage == 0) f |= ((w[0] >> k) & 1u) << (w1 - 1);
-        addr = (f << 8) | off;
+        f = (w[wb + (W * k) / 32] >> ((W * k) % 32)) & ((1u << W) - 1u);
     }
-    return *reinterpret_cast<const int *>(Th + addr);
+    return (f << 8) | off;
 }
 
 template <int C, int k>
 struct StepLoop {
-    static __device__ __forceinline__ void run(const uint32_t (&w)[24], const uint32_t (&po)[11], const char *Th, int lane, int &a1, int &a2,
+    static __device__ __forceinline__ void run(const uint32_t (&w)[24], const uint32_t (&po)[11], uint32_t tb, int lane, int &a1, int &a2,
                                                int &a3) {
-        a1 += stage_sum_step<C, k>(w, po, Th, lane, 0);
-        if (W2(C)) a2 += stage_sum_step<C, k>(w, po, Th, lane, 1);
-        if (W3(C)) a3 += stage_sum_step<C, k>(w, po, Th, lane, 2);
-        StepLoop<C, k + 1>::run(w, po, Th, lane, a1, a2, a3);
+        a1 += lds32(tb + stage_addr<C, k>(w, po, lane, 0));
+        if (W2(C)) a2 += lds32(tb + stage_addr<C, k>(w, po, lane, 1));
+        if (W3(C)) a3 += lds32(tb + stage_addr<C, k>(w, po, lane, 2));
+        StepLoop<C, k + 1>::run(w, po, tb, lane, a1, a2, a3);
     }
 };
 template <int C>
 struct StepLoop<C, 32> {
-    static __device__ __forceinline__ void run(const uint32_t (&)[24], const uint32_t (&)[11], const char *, int, int &, int &, int &) {}
+    static __device__ __forceinline__ void run(const uint32_t (&)[24], const uint32_t (&)[11], uint32_t, int, int &, int &, int &) {}
 };
 
-// integer total of one lane-slice: sum of table entries per stage << SH + MC * coset term
+// z bits (stage-1 MSBs) in step order. For W1 = 8: the MSBs of two words are merged (word b shifted right by 4) and
+// one multiply gathers their 8 bits into bits 24-31 without carries (all partial-product bits land on distinct places).
 template <int C>
-__device__ __forceinline__ int lane_slice_dot(const uint32_t (&w)[24], const uint32_t (&po)[11], const char *Th, const int *Gh, int lane) {
-    const uint32_t pm = zbits<C>(w);
+__device__ __forceinline__ uint32_t zbits_fast(const uint32_t (&w)[24]) {
+    if (W1(C) != 8) return w[0];
+    uint32_t pm = 0;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        const uint32_t x = (w[2 * p] & 0x80808080u) | ((w[2 * p + 1] >> 4) & 0x08080808u);
+        pm |= ((x * 0x00204081u) >> 24) << (8 * p);  // bits 0-3: steps 8p..8p+3 (word 2p), bits 4-7: word 2p+1
+    }
+    return pm;
+}
+
+// integer total of one lane-slice (table base tb, G base gb are shared-memory byte addresses)
+template <int C>
+__device__ __forceinline__ int lane_slice_dot(const uint32_t (&w)[24], const uint32_t (&po)[11], uint32_t tb, uint32_t gb, int lane) {
+    const uint32_t pm = zbits_fast<C>(w);
     const uint32_t H = pingala8_h(__funnelshift_l(pm, pm, lane));
     int cs = 0;
 #pragma unroll
-    for (int grp = 0; grp < 8; ++grp) cs += Gh[grp * 16 + ((H >> (4 * grp)) & 15u)];
+    for (int grp = 0; grp < 8; ++grp) cs += lds32(gb + grp * 64 + (((H >> (4 * grp)) & 15u) << 2));
     int a1 = 0, a2 = 0, a3 = 0;
-    StepLoop<C, 0>::run(w, po, Th, lane, a1, a2, a3);
+    StepLoop<C, 0>::run(w, po, tb, lane, a1, a2, a3);
     return a1 * (1 << SH1(C)) + a2 * (1 << SH2(C)) + a3 + MC(C) * cs;
 }
 
 template <int C>
-__device__ __forceinline__ float tile_row_dot(const uint32_t *p0, const uint32_t (&po)[11], const char *Ts, const int *Gs, int lane, float d0,
-                                              float d1) {
-    uint32_t w0[24], w1[24];
-    load_lane_words<C>(p0, 0, lane, w0);
-    load_lane_words<C>(p0, 1, lane, w1);
-    const int i0 = lane_slice_dot<C>(w0, po, Ts, Gs, lane);
-    const int i1 = lane_slice_dot<C>(w1, po, Ts + 128, Gs + kGInts, lane);
+__device__ __forceinline__ float tile_row_dot_w(const uint32_t (&w0)[24], const uint32_t (&w1)[24], const uint32_t (&po)[11], uint32_t tb,
+                                                uint32_t gb, int lane, float d0, float d1) {
+    const int i0 = lane_slice_dot<C>(w0, po, tb, gb, lane);
+    const int i1 = lane_slice_dot<C>(w1, po, tb + 128, gb + kGInts * 4, lane);
     return __fadd_rn(__fmul_rn((float)i0, d0), __fmul_rn((float)i1, d1));
 }
 
-__device__ __forceinline__ float tile_row_any(int c, const uint32_t *p0, const uint32_t (&po)[11], const char *Ts, const int *Gs, int lane,
-                                              float d0, float d1) {
+template <int C>
+__device__ __noinline__ float tile_row_dot(const uint32_t *p0, const uint32_t (&po)[11], uint32_t tb, uint32_t gb, int lane, float d0,
+                                           float d1) {
+    uint32_t w[24];
+    load_lane_words<C>(p0, 0, lane, w);
+    const int i0 = lane_slice_dot<C>(w, po, tb, gb, lane);
+    load_lane_words<C>(p0, 1, lane, w);
+    const int i1 = lane_slice_dot<C>(w, po, tb + 128, gb + kGInts * 4, lane);
+    return __fadd_rn(__fmul_rn((float)i0, d0), __fmul_rn((float)i1, d1));
+}
+
+__device__ __forceinline__ float tile_row_other(int c, const uint32_t *p0, const uint32_t (&po)[11], uint32_t tb, uint32_t gb, int lane,
+                                                float d0, float d1) {
     switch (c) {
-        case 0: return 0.f;
-        case 1: return tile_row_dot<1>(p0, po, Ts, Gs, lane, d0, d1);
-        case 2: return tile_row_dot<2>(p0, po, Ts, Gs, lane, d0, d1);
-        case 3: return tile_row_dot<3>(p0, po, Ts, Gs, lane, d0, d1);
-        case 4: return tile_row_dot<4>(p0, po, Ts, Gs, lane, d0, d1);
-        case 5: return tile_row_dot<5>(p0, po, Ts, Gs, lane, d0, d1);
-        case 6: return tile_row_dot<6>(p0, po, Ts, Gs, lane, d0, d1);
-        default: return tile_row_dot<7>(p0, po, Ts, Gs, lane, d0, d1);
+        case 1: return tile_row_dot<1>(p0, po, tb, gb, lane, d0, d1);
+        case 2: return tile_row_dot<2>(p0, po, tb, gb, lane, d0, d1);
+        case 4: return tile_row_dot<4>(p0, po, tb, gb, lane, d0, d1);
+        case 5: return tile_row_dot<5>(p0, po, tb, gb, lane, d0, d1);
+        case 6: return tile_row_dot<6>(p0, po, tb, gb, lane, d0, d1);
+        case 7: return tile_row_dot<7>(p0, po, tb, gb, lane, d0, d1);
+        default: return 0.f;
     }
 }
 
-__global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(const __grid_constant__ GemvArgs a) {
-    extern __shared__ __align__(128) uint8_t sm[];
-    int *Ts = reinterpret_cast<int *>(sm);
-    int *Gs = Ts + kTabInts;
-    uint64_t *bar = reinterpret_cast<uint64_t *>(Gs + 2 * kGInts);
-    __shared__ int s_last;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, n = blockIdx.y;
-    // item -> (tensor, block, row chunk)
-    int ti = 0;
+struct Unit {
+    int ti, b, g;
+};
+__device__ __forceinline__ Unit unit_of(const GemvArgs &a, long long u) {
+    Unit r;
+    r.b = (int)(u / a.ng_total);
+    int rr = (int)(u - (long long)r.b * a.ng_total);
+    r.ti = 0;
 #pragma unroll
     for (int i = 1; i < kMaxGroup; ++i)
-        if (i < a.ntensors && (int)blockIdx.x >= a.t[i].item0) ti = i;
-    const GemvTensor &T = a.t[ti];
-    const int item = blockIdx.x - T.item0, b = item % a.nb, chunk = item / a.nb;
-    const int g_first = chunk * kGemvWarps * a.tpw + warp;
+        if (i < a.ntensors && rr >= a.t[i].g0) r.ti = i;
+    r.g = rr - a.t[r.ti].g0;
+    return r;
+}
+
+// class-3 payload of one tile row (both half-slices): 8 words each
+__device__ __forceinline__ void load3(const uint32_t *p0, int lane, uint32_t (&v)[16]) {
+    const uint2 *q = reinterpret_cast<const uint2 *>(p0) + lane;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const uint2 u = __ldg(q + i * 32);  // hs 0: i < 4, hs 1: i >= 4 (hs stride = 8 words * 32 lanes = 128 uint2)
+        v[2 * i] = u.x;
+        v[2 * i + 1] = u.y;
+    }
+}
+
+__global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t sbase = smem_u32(g_smem);
+    uint64_t *bar = reinterpret_cast<uint64_t *>(g_smem + kSmemBar);
+    // contiguous, equal share of the block-major unit list
+    const long long u0 = a.units * blockIdx.x / gridDim.x, u1 = a.units * (blockIdx.x + 1) / gridDim.x;
+    const int b_first = (int)(u0 / a.ng_total), b_last = (int)((u1 - 1) / a.ng_total);
     pdl_launch_dependents();
     if (tid == 0) {
         mbar_init(bar, 1);
+        mbar_init(bar + 1, 1);
         fence_mbar_init();
-    }
-    if (lane == 0) {  // stream this warp's tile payloads toward L2 before waiting on the producer of x
-        for (int i = 0; i < a.tpw; ++i) {
-            const int g = g_first + kGemvWarps * i;
-            if (g >= T.ng) break;
-            const uint32_t mt = __ldg(T.M + (size_t)g * a.nb + b);
-            const int c = (int)(mt >> 29);
-            if (c) bulk_prefetch_l2(T.D + (mt & 0x1FFFFFFFu), (uint32_t)NW(c) * 256u);
-        }
     }
     uint32_t po[11];
 #pragma unroll
@@ -450,83 +491,133 @@ __global__ void __launch_bounds__(kGemvThreads, 2) k_gemv(const __grid_constant_
             if (3 * q + i < 32) r |= (((uint32_t)(lane + 3 * q + i) & 31u) << 2) << (8 * i);
         po[q] = r;
     }
-    pdl_wait();  // tables, accumulators and x are written by the preceding prep kernel
+    pdl_wait();  // tables and x come from the preceding prep kernel
     __syncthreads();
+    auto issue_table = [&](int seg) {  // segment seg (block b_first + seg) -> buffer seg & 1
+        const int bb = b_first + seg, buf = seg & 1;
+        mbar_expect_tx(bar + buf, kTabBytes + 2 * kGInts * 4);
+        bulk_g2s(g_smem + (buf ? kSmemT1 : kSmemT0), a.T + (size_t)bb * kTabInts, kTabBytes, bar + buf);
+        bulk_g2s(g_smem + (buf ? kSmemG1 : kSmemG0), a.G + (size_t)2 * bb * kGInts, 2 * kGInts * 4, bar + buf);
+    };
     if (tid == 0) {
-        mbar_expect_tx(bar, kTabBytes + 2 * kGInts * 4);
-        bulk_g2s(Ts, a.T + ((size_t)n * a.nb + b) * kTabInts, kTabBytes, bar);
-        bulk_g2s(Gs, a.G + ((size_t)n * a.nsl + 2 * b) * kGInts, 2 * kGInts * 4, bar);
+        issue_table(0);
+        if (b_last > b_first) issue_table(1);
     }
-    const float d0 = a.d[(size_t)n * a.nsl + 2 * b], d1 = a.d[(size_t)n * a.nsl + 2 * b + 1];
-    if (!mbar_wait_bounded(bar, 0, kWaitPolls)) {
-        if (lane == 0) atomicOr(&g_p8_device_error, 1u);
-        mbar_wait_bounded(bar, 0, kWaitPolls);  // the copy must land before the CTA's shared memory goes away
-        return;
+    // this warp's units: in every segment (block) of the CTA's range, units seg_begin + warp + 16 j, segments in order;
+    // the payload of the warp's next unit is loaded while the current one computes
+    auto first_in = [&](long long s) -> long long {  // first unit of this warp at or after segment start s
+        while (s < u1) {
+            const long long e = min(u1, (s / a.ng_total + 1) * a.ng_total);
+            if (s + warp < e) return s + warp;
+            s = e;
+        }
+        return u1;
+    };
+    auto next_of = [&](long long u) -> long long {
+        const long long e = min(u1, (u / a.ng_total + 1) * a.ng_total);
+        return u + kGemvWarps < e ? u + kGemvWarps : first_in(e);
+    };
+    long long nu = first_in(u0);
+    uint32_t nxt[16];
+    uint32_t mt_n = 0;
+    Unit un = {0, 0, 0};
+    if (nu < u1) {
+        un = unit_of(a, nu);
+        mt_n = __ldg(a.t[un.ti].M + (size_t)un.g * a.nb + un.b);
+        if ((mt_n >> 29) == 3) load3(a.t[un.ti].D + (mt_n & 0x1FFFFFFFu), lane, nxt);
     }
-    const char *Tc = reinterpret_cast<const char *>(Ts);
-    unsigned long long *acc = T.acc + (size_t)n * T.rows;
-    for (int i = 0; i < a.tpw; ++i) {
-        const int g = g_first + kGemvWarps * i;
-        if (g >= T.ng) break;
-        const uint32_t mt = __ldg(T.M + (size_t)g * a.nb + b);
-        const float part = tile_row_any((int)(mt >> 29), T.D + (mt & 0x1FFFFFFFu), po, Tc, Gs, lane, d0, d1);
-        const int r = g * 32 + lane;
-        const float v = __fmul_rn(part, h2f(T.S[(size_t)b * T.rows + r]));
-        atomicAdd(acc + r, (unsigned long long)__double2ll_rn((double)v * kFixScale));
+    int seg_done = -1;
+    bool ok = true;
+    for (int seg = 0; b_first + seg <= b_last; ++seg) {
+        const int b = b_first + seg;
+        const long long s1 = min(u1, (long long)(b + 1) * a.ng_total);
+        if (!mbar_wait_bounded(bar + (seg & 1), (uint32_t)((seg >> 1) & 1), kWaitPolls)) {
+            if (lane == 0) atomicOr(&g_p8_device_error, 1u);
+            ok = false;
+            break;
+        }
+        const uint32_t tb = sbase + ((seg & 1) ? kSmemT1 : kSmemT0), gb = sbase + ((seg & 1) ? kSmemG1 : kSmemG0);
+        const float d0 = a.d[2 * b], d1 = a.d[2 * b + 1];
+        while (nu < s1) {
+            const Unit uc = un;
+            const uint32_t mt = mt_n;
+            uint32_t cur[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) cur[i] = nxt[i];
+            nu = next_of(nu);
+            if (nu < u1) {  // prefetch the payload of this warp's next unit (possibly in the next segment)
+                un = unit_of(a, nu);
+                mt_n = __ldg(a.t[un.ti].M + (size_t)un.g * a.nb + un.b);
+                if ((mt_n >> 29) == 3) load3(a.t[un.ti].D + (mt_n & 0x1FFFFFFFu), lane, nxt);
+            }
+            const GemvTensor &T = a.t[uc.ti];
+            const int c = (int)(mt >> 29);
+            float part;
+            if (c == 3) {
+                uint32_t w0[24], w1[24];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    w0[2 * i] = cur[2 * i]; w0[2 * i + 1] = cur[2 * i + 1];
+                    w1[2 * i] = cur[8 + 2 * i]; w1[2 * i + 1] = cur[8 + 2 * i + 1];
+                }
+#pragma unroll
+                for (int i = 8; i < 24; ++i) { w0[i] = 0; w1[i] = 0; }
+                part = tile_row_dot_w<3>(w0, w1, po, tb, gb, lane, d0, d1);
+            } else {
+                part = tile_row_other(c, T.D + (mt & 0x1FFFFFFFu), po, tb, gb, lane, d0, d1);
+            }
+            const int r = uc.g * 32 + lane;
+            T.part[(size_t)b * T.rows + r] = __fmul_rn(part, h2f(T.S[(size_t)b * T.rows + r]));
+            // tile arrival: the warp that brings the last block of tile g finishes its 32 rows
+            __threadfence();  // every lane's partial is visible device-wide before the arrival is counted
+            __syncwarp();
+            unsigned prev = 0;
+            if (lane == 0) prev = atomicAdd(T.cnt + uc.g, 1u);
+            prev = __shfl_sync(0xffffffffu, prev, 0);
+            if (prev == (unsigned)(a.nb - 1)) {
+                __threadfence();
+                float s = 0.f;
+                for (int bb = 0; bb < a.nb; ++bb) s = __fadd_rn(s, __ldcg(T.part + (size_t)bb * T.rows + r));
+                const int ro = T.prm[r];
+                for (int e = T.cp[ro]; e < T.cp[ro + 1]; ++e) s = __fadd_rn(s, __fmul_rn(T.cv[e], a.X[T.cc[e]]));
+                T.Y[ro] = s;
+                if (lane == 0) T.cnt[uc.g] = 0u;  // leave the counter zero for the next call
+            }
+        }
+        seg_done = seg;
+        __syncthreads();  // every warp is done with this segment's buffer
+        if (tid == 0 && b_first + seg + 2 <= b_last) {
+            fence_proxy_async();  // the buffer's generic-proxy reads are ordered before the bulk copy overwrites it
+            issue_table(seg + 2);
+        }
     }
-    // arrival counter of this row chunk; the last of its nb items finishes the rows
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        const unsigned prev = atomicAdd(T.cnt + (size_t)n * T.chunks + chunk, 1u);
-        s_last = prev == (unsigned)(a.nb - 1);
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    const int r0 = chunk * kGemvWarps * a.tpw * 32, r1 = min(T.rows, r0 + kGemvWarps * a.tpw * 32);
-    const float *x = a.X + (size_t)n * a.ldx;
-    for (int r = r0 + tid; r < r1; r += kGemvThreads) {
-        const long long s = (long long)__ldcg(acc + r);
-        float v = (float)((double)s * (1.0 / kFixScale));
-        const int ro = T.prm[r];
-        for (int e = T.cp[ro]; e < T.cp[ro + 1]; ++e) v = __fadd_rn(v, __fmul_rn(T.cv[e], x[T.cc[e]]));
-        T.Y[(size_t)n * T.ldy + ro] = v;
+    if (!ok) {  // copies in flight must land before the CTA's shared memory goes away
+        if (tid == 0) {
+            for (int s = seg_done + 1; s <= seg_done + 2 && b_first + s <= b_last; ++s)
+                mbar_wait_bounded(bar + (s & 1), (uint32_t)((s >> 1) & 1), kWaitPolls);
+        }
     }
 }
 
-// workspace layout (bytes, each part 256-aligned): T | G | d | acc (int64 per row) | counters
+// workspace layout (bytes, each part 256-aligned): T | G | d | partials ([nb][rows] per tensor)
 struct GemvWs {
-    size_t T, G, d, acc, cnt, total;
+    size_t T, G, d, part, total;
 };
 static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
-static int gemv_tpw_for(int ng_total, int nb) {
-    // rows per item = 512 * tpw: the largest that still leaves ~2 items per SM (148 SMs) in the launch
-    int tpw = 1;
-    while (tpw < 8 && (size_t)nb * (size_t)((ng_total + kGemvWarps * tpw * 2 - 1) / (kGemvWarps * tpw * 2)) >= 296) tpw *= 2;
-    return tpw;
-}
-static GemvWs gemv_ws_layout(const p8_tensor *const *ts, int nt, int64_t ncols, int tpw) {
+static GemvWs gemv_ws_layout(const p8_tensor *const *ts, int nt) {
     const p8_tensor *t = ts[0];
-    size_t rows = 0, chunks = 0;
-    for (int i = 0; i < nt; ++i) {
-        rows += (size_t)ts[i]->rows;
-        chunks += (size_t)((ts[i]->ng + kGemvWarps * tpw - 1) / (kGemvWarps * tpw));
-    }
+    size_t part = 0;
+    for (int i = 0; i < nt; ++i) part += al256((size_t)ts[i]->nb * ts[i]->rows * 4);
     GemvWs w;
     w.T = 0;
-    w.G = w.T + al256((size_t)ncols * t->nb * kTabBytes);
-    w.d = w.G + al256((size_t)ncols * t->nsl * kGInts * 4);
-    w.acc = w.d + al256((size_t)ncols * t->nsl * 4);
-    w.cnt = w.acc + al256((size_t)ncols * rows * 8);
-    w.total = w.cnt + al256((size_t)ncols * chunks * 4);
+    w.G = w.T + al256((size_t)t->nb * kTabBytes);
+    w.d = w.G + al256((size_t)t->nsl * kGInts * 4);
+    w.part = w.d + al256((size_t)t->nsl * 4);
+    w.total = w.part + part;
     return w;
 }
-size_t gemv_workspace(const p8_tensor *t, int64_t ncols) {
-    // sized for the smallest row chunk (tpw = 1): covers every tpw choice
-    return gemv_ws_layout(&t, 1, ncols, 1).total;
-}
-size_t gemv_group_workspace(const p8_tensor *const *ts, int nt, int64_t ncols) { return gemv_ws_layout(ts, nt, ncols, 1).total; }
+size_t gemv_workspace(const p8_tensor *t, int64_t) { return gemv_ws_layout(&t, 1).total; }
+size_t gemv_group_workspace(const p8_tensor *const *ts, int nt, int64_t) { return gemv_ws_layout(ts, nt).total; }
 
 static cudaError_t launch_pdl(const void *fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void **args) {
     cudaLaunchConfig_t cfg = {};
@@ -542,64 +633,78 @@ static cudaError_t launch_pdl(const void *fn, dim3 grid, dim3 block, size_t smem
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
-p8_status launch_gemv_group(const p8_tensor *const *ts, int nt, const float *X, int64_t ncols, int64_t ldx, float *const *Ys,
-                            const int64_t *ldys, void *ws, size_t ws_bytes, cudaStream_t st) {
-    if (nt < 1 || nt > kMaxGroup) return P8_ERR_ARG;
-    const p8_tensor *t0 = ts[0];
-    int ng_total = 0;
-    for (int i = 0; i < nt; ++i) {
-        // tensors of one launch share x and its table: same K, column scales, signs and codebook (content hash)
-        if (ts[i]->K != t0->K || ts[i]->act_hash != t0->act_hash) return P8_ERR_ARG;
-        ng_total += ts[i]->ng;
+static int sm_count() {
+    static int n[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (!n[dev]) {
+        int v = 0;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        n[dev] = v > 0 ? v : 148;
+        cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
     }
-    if (ncols > 65535) return P8_ERR_ARG;
-    const int tpw = gemv_tpw_for(ng_total, t0->nb);
-    const GemvWs L = gemv_ws_layout(ts, nt, ncols, tpw);
+    return n[dev];
+}
+
+// one column: prep + persistent GEMV over the group
+static p8_status launch_gemv_col(const p8_tensor *const *ts, int nt, const float *x, float *const *Ys, void *ws, size_t ws_bytes,
+                                 cudaStream_t st) {
+    const p8_tensor *t0 = ts[0];
+    const GemvWs L = gemv_ws_layout(ts, nt);
     if (!ws || ws_bytes < L.total) return P8_ERR_WORKSPACE;
     uint8_t *w = static_cast<uint8_t *>(ws);
+    const int nsm = sm_count();
     PrepArgs pa;
-    pa.X = X; pa.ldx = ldx; pa.ic = t0->ic; pa.A = t0->A; pa.cs = t0->cs; pa.K = t0->K; pa.nb = t0->nb; pa.nsl = t0->nsl;
+    memset(&pa, 0, sizeof(pa));
+    pa.X = x; pa.ic = t0->ic; pa.A = t0->A; pa.cs = t0->cs; pa.K = t0->K; pa.nb = t0->nb; pa.nsl = t0->nsl; pa.ntensors = nt;
     pa.T = reinterpret_cast<int *>(w + L.T);
     pa.G = reinterpret_cast<int *>(w + L.G);
     pa.d = reinterpret_cast<float *>(w + L.d);
-    pa.zero64 = reinterpret_cast<unsigned long long *>(w + L.acc);
-    pa.nzero64 = (L.cnt - L.acc) / 8;
-    pa.zero32 = reinterpret_cast<unsigned int *>(w + L.cnt);
-    pa.nzero32 = (L.total - L.cnt) / 4;
-    {
-        void *args[] = {&pa};
-        if (launch_pdl((const void *)k_act_prep, dim3(t0->nb, 8, (unsigned)ncols), dim3(256), 0, st, args) != cudaSuccess)
-            return P8_ERR_CUDA;
-    }
     GemvArgs ga;
     memset(&ga, 0, sizeof(ga));
-    ga.ntensors = nt; ga.T = pa.T; ga.G = pa.G; ga.d = pa.d; ga.X = X; ga.ldx = ldx;
-    ga.nb = t0->nb; ga.nsl = t0->nsl; ga.tpw = tpw;
-    int item0 = 0;
-    size_t acc_off = 0, cnt_off = 0;
+    ga.ntensors = nt; ga.T = pa.T; ga.G = pa.G; ga.d = pa.d; ga.X = x; ga.nb = t0->nb; ga.nsl = t0->nsl;
+    size_t poff = L.part;
+    int g0 = 0;
     for (int i = 0; i < nt; ++i) {
         const p8_tensor *t = ts[i];
         GemvTensor &g = ga.t[i];
         g.M = t->M; g.D = t->D; g.S = t->S; g.prm = t->prm; g.cp = t->cp; g.cc = t->cc; g.cv = t->cv;
-        g.Y = Ys[i]; g.ldy = ldys[i];
-        g.rows = t->rows; g.ng = t->ng;
-        g.chunks = (t->ng + kGemvWarps * tpw - 1) / (kGemvWarps * tpw);
-        g.item0 = item0;
-        g.acc = pa.zero64 + acc_off * ncols;
-        g.cnt = pa.zero32 + cnt_off * ncols;
-        acc_off += (size_t)t->rows;
-        cnt_off += (size_t)g.chunks;
-        item0 += g.chunks * t->nb;
+        g.Y = Ys[i];
+        g.part = reinterpret_cast<float *>(w + poff);
+        poff += al256((size_t)t->nb * t->rows * 4);
+        g.cnt = t->tile_cnt;
+        g.rows = t->rows; g.ng = t->ng; g.g0 = g0;
+        g0 += t->ng;
+        pa.pf[i] = reinterpret_cast<const uint8_t *>(t->M);
+        pa.pfbytes[i] = (t->kbytes - kHdrBytes);  // M, S and the payload are contiguous after the header
     }
-    const size_t smem = kTabBytes + 2 * kGInts * 4 + 16;
-    static bool attr_set = false;
-    if (!attr_set) {
-        if (cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return P8_ERR_CUDA;
-        attr_set = true;
+    ga.ng_total = g0;
+    ga.units = (long long)g0 * t0->nb;
+    {
+        void *args[] = {&pa};
+        if (launch_pdl((const void *)k_act_prep, dim3(t0->nb, 8), dim3(256), 0, st, args) != cudaSuccess) return P8_ERR_CUDA;
     }
+    const unsigned grid = (unsigned)(ga.units < nsm ? ga.units : nsm);
     void *args[] = {&ga};
-    if (launch_pdl((const void *)k_gemv, dim3((unsigned)item0, (unsigned)ncols), dim3(kGemvThreads), smem, st, args) != cudaSuccess)
-        return P8_ERR_CUDA;
+    if (launch_pdl((const void *)k_gemv, dim3(grid), dim3(kGemvThreads), kGemvSmem, st, args) != cudaSuccess) return P8_ERR_CUDA;
+    return P8_OK;
+}
+
+p8_status launch_gemv_group(const p8_tensor *const *ts, int nt, const float *X, int64_t ncols, int64_t ldx, float *const *Ys,
+                            const int64_t *ldys, void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (nt < 1 || nt > kMaxGroup) return P8_ERR_ARG;
+    const p8_tensor *t0 = ts[0];
+    for (int i = 0; i < nt; ++i)  // tensors of one launch share x and its table: same K, column scales, signs and codebook
+        if (ts[i]->K != t0->K || ts[i]->act_hash != t0->act_hash) return P8_ERR_ARG;
+    (void)sm_count();
+    // columns run one after another (the per-tile counters are per tensor); ncols > 1 is the batched fallback
+    for (int64_t n = 0; n < ncols; ++n) {
+        float *Yn[kMaxGroup];
+        for (int i = 0; i < nt; ++i) Yn[i] = Ys[i] + n * ldys[i];
+        p8_status s = launch_gemv_col(ts, nt, X + n * ldx, Yn, ws, ws_bytes, st);
+        if (s) return s;
+    }
     return P8_OK;
 }
 
