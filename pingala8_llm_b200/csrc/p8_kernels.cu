@@ -384,16 +384,17 @@ struct StepLoop<C, 32> {
     static __device__ __forceinline__ void run(const uint32_t (&)[24], const uint32_t (&)[11], uint32_t, int, int &, int &, int &) {}
 };
 
-// z bits (stage-1 MSBs) in step order. For W1 = 8: the MSBs of two words are merged (word b shifted right by 4) and
-// one multiply gathers their 8 bits into bits 24-31 without carries (all partial-product bits land on distinct places).
+// z bits (stage-1 MSBs) in step order. For W1 = 8: the byte MSBs of words 2p+1 (bits 7, 15, 23, 31) and 2p (shifted to
+// bits 3, 11, 19, 27) are merged, and one multiply by 0x00204081 gathers them into bits 24-27 (word 2p, steps 8p..8p+3)
+// and 28-31 (word 2p+1) without carries: every partial-product bit lands on a distinct position.
 template <int C>
 __device__ __forceinline__ uint32_t zbits_fast(const uint32_t (&w)[24]) {
     if (W1(C) != 8) return w[0];
     uint32_t pm = 0;
 #pragma unroll
     for (int p = 0; p < 4; ++p) {
-        const uint32_t x = (w[2 * p] & 0x80808080u) | ((w[2 * p + 1] >> 4) & 0x08080808u);
-        pm |= ((x * 0x00204081u) >> 24) << (8 * p);  // bits 0-3: steps 8p..8p+3 (word 2p), bits 4-7: word 2p+1
+        const uint32_t x = (w[2 * p + 1] & 0x80808080u) | ((w[2 * p] >> 4) & 0x08080808u);
+        pm |= ((x * 0x00204081u) >> 24) << (8 * p);
     }
     return pm;
 }

@@ -86,3 +86,19 @@ def test_planted_mistake_is_caught():
     offD = (2064 + 68 * nt + 15) & ~15
     bad[offD + 5] ^= 0x10
     assert not np.array_equal(Oracle(bad, f.rows, f.K).dequant(), Oracle(f.slot, f.rows, f.K).dequant())
+
+
+def test_zbit_gather_identity():
+    """The GEMV gathers the 32 stage-1 MSBs of a class-3 lane (8 words) with one multiply per word pair:
+    x = (w[2p+1] & 0x80808080) | ((w[2p] >> 4) & 0x08080808); bits 24-31 of x * 0x00204081 = steps 8p..8p+7.
+    Checked here against the bit-by-bit definition."""
+    rng = np.random.default_rng(0)
+    for w in rng.integers(0, 2**32, (3000, 8), dtype=np.uint64):
+        ref = 0
+        for k in range(32):
+            ref |= ((int(w[k // 4]) >> (8 * (k % 4) + 7)) & 1) << k
+        pm = 0
+        for p in range(4):
+            x = (int(w[2 * p + 1]) & 0x80808080) | ((int(w[2 * p]) >> 4) & 0x08080808)
+            pm |= (((x * 0x00204081) & 0xFFFFFFFF) >> 24) << (8 * p)
+        assert pm == ref
