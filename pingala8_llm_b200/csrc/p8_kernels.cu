@@ -344,10 +344,11 @@ struct Sel {
     static constexpr uint32_t v = (uint32_t)(4 + k % 3) | ((uint32_t)(k % 4) << 4) | 0x7700u;
 };
 
-__device__ __forceinline__ int lds32(uint32_t saddr) {
-    int v;
-    asm("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(saddr));
-    return v;
+// shared-memory int at a compile-time offset plus a register byte offset: indexing the extern __shared__ symbol
+// directly lets the compiler fold the offset into the load's immediate (no address add per lookup)
+template <int OFF>
+__device__ __forceinline__ int lds_at(uint32_t byte_off) {
+    return *reinterpret_cast<const int *>(g_smem + OFF + byte_off);
 }
 
 template <int C, int k>
@@ -369,19 +370,18 @@ __device__ __forceinline__ uint32_t stage_addr(const uint32_t (&w)[24], const ui
     return (f << 8) | off;
 }
 
-template <int C, int k>
+template <int C, int TOFF, int k>
 struct StepLoop {
-    static __device__ __forceinline__ void run(const uint32_t (&w)[24], const uint32_t (&po)[11], uint32_t tb, int lane, int &a1, int &a2,
-                                               int &a3) {
-        a1 += lds32(tb + stage_addr<C, k>(w, po, lane, 0));
-        if (W2(C)) a2 += lds32(tb + stage_addr<C, k>(w, po, lane, 1));
-        if (W3(C)) a3 += lds32(tb + stage_addr<C, k>(w, po, lane, 2));
-        StepLoop<C, k + 1>::run(w, po, tb, lane, a1, a2, a3);
+    static __device__ __forceinline__ void run(const uint32_t (&w)[24], const uint32_t (&po)[11], int lane, int &a1, int &a2, int &a3) {
+        a1 += lds_at<TOFF>(stage_addr<C, k>(w, po, lane, 0));
+        if (W2(C)) a2 += lds_at<TOFF>(stage_addr<C, k>(w, po, lane, 1));
+        if (W3(C)) a3 += lds_at<TOFF>(stage_addr<C, k>(w, po, lane, 2));
+        StepLoop<C, TOFF, k + 1>::run(w, po, lane, a1, a2, a3);
     }
 };
-template <int C>
-struct StepLoop<C, 32> {
-    static __device__ __forceinline__ void run(const uint32_t (&)[24], const uint32_t (&)[11], uint32_t, int, int &, int &, int &) {}
+template <int C, int TOFF>
+struct StepLoop<C, TOFF, 32> {
+    static __device__ __forceinline__ void run(const uint32_t (&)[24], const uint32_t (&)[11], int, int &, int &, int &) {}
 };
 
 // z bits (stage-1 MSBs) in step order. For W1 = 8: the byte MSBs of words 2p+1 (bits 7, 15, 23, 31) and 2p (shifted to
@@ -399,64 +399,50 @@ __device__ __forceinline__ uint32_t zbits_fast(const uint32_t (&w)[24]) {
     return pm;
 }
 
-// integer total of one lane-slice (table base tb, G base gb are shared-memory byte addresses)
-template <int C>
-__device__ __forceinline__ int lane_slice_dot(const uint32_t (&w)[24], const uint32_t (&po)[11], uint32_t tb, uint32_t gb, int lane) {
+// integer total of one lane-slice; TOFF / GOFF: shared-memory byte offsets of its table and coset tables
+template <int C, int TOFF, int GOFF>
+__device__ __forceinline__ int lane_slice_dot(const uint32_t (&w)[24], const uint32_t (&po)[11], int lane) {
     const uint32_t pm = zbits_fast<C>(w);
     const uint32_t H = pingala8_h(__funnelshift_l(pm, pm, lane));
     int cs = 0;
 #pragma unroll
-    for (int grp = 0; grp < 8; ++grp) cs += lds32(gb + grp * 64 + (((H >> (4 * grp)) & 15u) << 2));
+    for (int grp = 0; grp < 8; ++grp) cs += lds_at<GOFF>(grp * 64 + (((H >> (4 * grp)) & 15u) << 2));
     int a1 = 0, a2 = 0, a3 = 0;
-    StepLoop<C, 0>::run(w, po, tb, lane, a1, a2, a3);
+    StepLoop<C, TOFF, 0>::run(w, po, lane, a1, a2, a3);
     return a1 * (1 << SH1(C)) + a2 * (1 << SH2(C)) + a3 + MC(C) * cs;
 }
 
-template <int C>
-__device__ __forceinline__ float tile_row_dot_w(const uint32_t (&w0)[24], const uint32_t (&w1)[24], const uint32_t (&po)[11], uint32_t tb,
-                                                uint32_t gb, int lane, float d0, float d1) {
-    const int i0 = lane_slice_dot<C>(w0, po, tb, gb, lane);
-    const int i1 = lane_slice_dot<C>(w1, po, tb + 128, gb + kGInts * 4, lane);
+template <int C, int BUF>
+__device__ __forceinline__ float tile_row_dot_w(const uint32_t (&w0)[24], const uint32_t (&w1)[24], const uint32_t (&po)[11], int lane, float d0,
+                                                float d1) {
+    constexpr int T0 = BUF ? kSmemT1 : kSmemT0, G0 = BUF ? kSmemG1 : kSmemG0;
+    const int i0 = lane_slice_dot<C, T0, G0>(w0, po, lane);
+    const int i1 = lane_slice_dot<C, T0 + 128, G0 + kGInts * 4>(w1, po, lane);
     return __fadd_rn(__fmul_rn((float)i0, d0), __fmul_rn((float)i1, d1));
 }
 
-template <int C>
-__device__ __noinline__ float tile_row_dot(const uint32_t *p0, const uint32_t (&po)[11], uint32_t tb, uint32_t gb, int lane, float d0,
-                                           float d1) {
+template <int C, int BUF>
+__device__ __noinline__ float tile_row_dot(const uint32_t *p0, const uint32_t (&po)[11], int lane, float d0, float d1) {
+    constexpr int T0 = BUF ? kSmemT1 : kSmemT0, G0 = BUF ? kSmemG1 : kSmemG0;
     uint32_t w[24];
     load_lane_words<C>(p0, 0, lane, w);
-    const int i0 = lane_slice_dot<C>(w, po, tb, gb, lane);
+    const int i0 = lane_slice_dot<C, T0, G0>(w, po, lane);
     load_lane_words<C>(p0, 1, lane, w);
-    const int i1 = lane_slice_dot<C>(w, po, tb + 128, gb + kGInts * 4, lane);
+    const int i1 = lane_slice_dot<C, T0 + 128, G0 + kGInts * 4>(w, po, lane);
     return __fadd_rn(__fmul_rn((float)i0, d0), __fmul_rn((float)i1, d1));
 }
 
-__device__ __forceinline__ float tile_row_other(int c, const uint32_t *p0, const uint32_t (&po)[11], uint32_t tb, uint32_t gb, int lane,
-                                                float d0, float d1) {
+template <int BUF>
+__device__ __forceinline__ float tile_row_other(int c, const uint32_t *p0, const uint32_t (&po)[11], int lane, float d0, float d1) {
     switch (c) {
-        case 1: return tile_row_dot<1>(p0, po, tb, gb, lane, d0, d1);
-        case 2: return tile_row_dot<2>(p0, po, tb, gb, lane, d0, d1);
-        case 4: return tile_row_dot<4>(p0, po, tb, gb, lane, d0, d1);
-        case 5: return tile_row_dot<5>(p0, po, tb, gb, lane, d0, d1);
-        case 6: return tile_row_dot<6>(p0, po, tb, gb, lane, d0, d1);
-        case 7: return tile_row_dot<7>(p0, po, tb, gb, lane, d0, d1);
+        case 1: return tile_row_dot<1, BUF>(p0, po, lane, d0, d1);
+        case 2: return tile_row_dot<2, BUF>(p0, po, lane, d0, d1);
+        case 4: return tile_row_dot<4, BUF>(p0, po, lane, d0, d1);
+        case 5: return tile_row_dot<5, BUF>(p0, po, lane, d0, d1);
+        case 6: return tile_row_dot<6, BUF>(p0, po, lane, d0, d1);
+        case 7: return tile_row_dot<7, BUF>(p0, po, lane, d0, d1);
         default: return 0.f;
     }
-}
-
-struct Unit {
-    int ti, b, g;
-};
-__device__ __forceinline__ Unit unit_of(const GemvArgs &a, long long u) {
-    Unit r;
-    r.b = (int)(u / a.ng_total);
-    int rr = (int)(u - (long long)r.b * a.ng_total);
-    r.ti = 0;
-#pragma unroll
-    for (int i = 1; i < kMaxGroup; ++i)
-        if (i < a.ntensors && rr >= a.t[i].g0) r.ti = i;
-    r.g = rr - a.t[r.ti].g0;
-    return r;
 }
 
 // class-3 payload of one tile row (both half-slices): 8 words each
@@ -470,13 +456,30 @@ __device__ __forceinline__ void load3(const uint32_t *p0, int lane, uint32_t (&v
     }
 }
 
+__device__ __forceinline__ int tensor_of(const GemvArgs &a, int rr) {
+    int ti = 0;
+#pragma unroll
+    for (int i = 1; i < kMaxGroup; ++i)
+        if (i < a.ntensors && rr >= a.t[i].g0) ti = i;
+    return ti;
+}
+
+// the warp's units of a CTA: per block b (segment), units rr = first + warp + 16 j of [rr_begin(b), rr_end(b)); a
+// unit is tile g = rr - g0 of tensor tensor_of(rr). Pure integer bookkeeping, no divisions.
+struct WarpCursor {
+    int b, rr;  // current unit; b > b_last: exhausted
+};
+
 __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t sbase = smem_u32(g_smem);
     uint64_t *bar = reinterpret_cast<uint64_t *>(g_smem + kSmemBar);
     // contiguous, equal share of the block-major unit list
     const long long u0 = a.units * blockIdx.x / gridDim.x, u1 = a.units * (blockIdx.x + 1) / gridDim.x;
     const int b_first = (int)(u0 / a.ng_total), b_last = (int)((u1 - 1) / a.ng_total);
+    const int rr_first = (int)(u0 - (long long)b_first * a.ng_total);             // first unit's rr in block b_first
+    const int rr_last_end = (int)(u1 - (long long)b_last * a.ng_total);           // end rr in block b_last
+    auto rr_begin = [&](int b) { return b == b_first ? rr_first : 0; };
+    auto rr_end = [&](int b) { return b == b_last ? rr_last_end : a.ng_total; };
     pdl_launch_dependents();
     if (tid == 0) {
         mbar_init(bar, 1);
@@ -504,54 +507,48 @@ __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
         issue_table(0);
         if (b_last > b_first) issue_table(1);
     }
-    // this warp's units: in every segment (block) of the CTA's range, units seg_begin + warp + 16 j, segments in order;
-    // the payload of the warp's next unit is loaded while the current one computes
-    auto first_in = [&](long long s) -> long long {  // first unit of this warp at or after segment start s
-        while (s < u1) {
-            const long long e = min(u1, (s / a.ng_total + 1) * a.ng_total);
-            if (s + warp < e) return s + warp;
-            s = e;
+    // cursor over this warp's units; the payload of the next unit is loaded while the current one computes
+    auto advance = [&](WarpCursor c) -> WarpCursor {
+        c.rr += kGemvWarps;
+        while (c.b <= b_last && c.rr >= rr_end(c.b)) {
+            ++c.b;
+            c.rr = (c.b <= b_last ? rr_begin(c.b) : 0) + warp;
         }
-        return u1;
+        return c;
     };
-    auto next_of = [&](long long u) -> long long {
-        const long long e = min(u1, (u / a.ng_total + 1) * a.ng_total);
-        return u + kGemvWarps < e ? u + kGemvWarps : first_in(e);
-    };
-    long long nu = first_in(u0);
+    WarpCursor nc = {b_first, rr_first + warp};
+    while (nc.b <= b_last && nc.rr >= rr_end(nc.b)) {
+        ++nc.b;
+        nc.rr = (nc.b <= b_last ? rr_begin(nc.b) : 0) + warp;
+    }
     uint32_t nxt[16];
     uint32_t mt_n = 0;
-    Unit un = {0, 0, 0};
-    if (nu < u1) {
-        un = unit_of(a, nu);
-        mt_n = __ldg(a.t[un.ti].M + (size_t)un.g * a.nb + un.b);
-        if ((mt_n >> 29) == 3) load3(a.t[un.ti].D + (mt_n & 0x1FFFFFFFu), lane, nxt);
-    }
-    int seg_done = -1;
+    auto fetch = [&](const WarpCursor &c) {
+        const int ti = tensor_of(a, c.rr), g = c.rr - a.t[ti].g0;
+        mt_n = __ldg(a.t[ti].M + (size_t)g * a.nb + c.b);
+        if ((mt_n >> 29) == 3) load3(a.t[ti].D + (mt_n & 0x1FFFFFFFu), lane, nxt);
+    };
+    if (nc.b <= b_last) fetch(nc);
     bool ok = true;
-    for (int seg = 0; b_first + seg <= b_last; ++seg) {
+    int seg = 0;
+    for (; b_first + seg <= b_last; ++seg) {
         const int b = b_first + seg;
-        const long long s1 = min(u1, (long long)(b + 1) * a.ng_total);
         if (!mbar_wait_bounded(bar + (seg & 1), (uint32_t)((seg >> 1) & 1), kWaitPolls)) {
             if (lane == 0) atomicOr(&g_p8_device_error, 1u);
             ok = false;
             break;
         }
-        const uint32_t tb = sbase + ((seg & 1) ? kSmemT1 : kSmemT0), gb = sbase + ((seg & 1) ? kSmemG1 : kSmemG0);
         const float d0 = a.d[2 * b], d1 = a.d[2 * b + 1];
-        while (nu < s1) {
-            const Unit uc = un;
+        while (nc.b == b) {
+            const int rr = nc.rr;
             const uint32_t mt = mt_n;
             uint32_t cur[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) cur[i] = nxt[i];
-            nu = next_of(nu);
-            if (nu < u1) {  // prefetch the payload of this warp's next unit (possibly in the next segment)
-                un = unit_of(a, nu);
-                mt_n = __ldg(a.t[un.ti].M + (size_t)un.g * a.nb + un.b);
-                if ((mt_n >> 29) == 3) load3(a.t[un.ti].D + (mt_n & 0x1FFFFFFFu), lane, nxt);
-            }
-            const GemvTensor &T = a.t[uc.ti];
+            nc = advance(nc);
+            if (nc.b <= b_last) fetch(nc);  // possibly in the next segment
+            const int ti = tensor_of(a, rr), g = rr - a.t[ti].g0;
+            const GemvTensor &T = a.t[ti];
             const int c = (int)(mt >> 29);
             float part;
             if (c == 3) {
@@ -563,40 +560,44 @@ __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
                 }
 #pragma unroll
                 for (int i = 8; i < 24; ++i) { w0[i] = 0; w1[i] = 0; }
-                part = tile_row_dot_w<3>(w0, w1, po, tb, gb, lane, d0, d1);
+                part = (seg & 1) ? tile_row_dot_w<3, 1>(w0, w1, po, lane, d0, d1) : tile_row_dot_w<3, 0>(w0, w1, po, lane, d0, d1);
             } else {
-                part = tile_row_other(c, T.D + (mt & 0x1FFFFFFFu), po, tb, gb, lane, d0, d1);
+                const uint32_t *p0 = T.D + (mt & 0x1FFFFFFFu);
+                part = (seg & 1) ? tile_row_other<1>(c, p0, po, lane, d0, d1) : tile_row_other<0>(c, p0, po, lane, d0, d1);
             }
-            const int r = uc.g * 32 + lane;
+            const int r = g * 32 + lane;
             T.part[(size_t)b * T.rows + r] = __fmul_rn(part, h2f(T.S[(size_t)b * T.rows + r]));
-            // tile arrival: the warp that brings the last block of tile g finishes its 32 rows
-            __threadfence();  // every lane's partial is visible device-wide before the arrival is counted
-            __syncwarp();
+        }
+        // arrivals of this warp's tiles of block b; the warp that brings a tile's last block finishes its 32 rows
+        __syncwarp();
+        if (lane == 0) __threadfence();  // release: the warp's partial stores (ordered by __syncwarp) before the counts
+        __syncwarp();
+        for (int rr = rr_begin(b) + warp; rr < rr_end(b); rr += kGemvWarps) {
+            const int ti = tensor_of(a, rr), g = rr - a.t[ti].g0;
+            const GemvTensor &T = a.t[ti];
             unsigned prev = 0;
-            if (lane == 0) prev = atomicAdd(T.cnt + uc.g, 1u);
+            if (lane == 0) prev = atomicAdd(T.cnt + g, 1u);
             prev = __shfl_sync(0xffffffffu, prev, 0);
             if (prev == (unsigned)(a.nb - 1)) {
                 __threadfence();
+                const int r = g * 32 + lane;
                 float s = 0.f;
                 for (int bb = 0; bb < a.nb; ++bb) s = __fadd_rn(s, __ldcg(T.part + (size_t)bb * T.rows + r));
                 const int ro = T.prm[r];
                 for (int e = T.cp[ro]; e < T.cp[ro + 1]; ++e) s = __fadd_rn(s, __fmul_rn(T.cv[e], a.X[T.cc[e]]));
                 T.Y[ro] = s;
-                if (lane == 0) T.cnt[uc.g] = 0u;  // leave the counter zero for the next call
+                if (lane == 0) T.cnt[g] = 0u;  // leave the counter zero for the next call
             }
         }
-        seg_done = seg;
         __syncthreads();  // every warp is done with this segment's buffer
         if (tid == 0 && b_first + seg + 2 <= b_last) {
             fence_proxy_async();  // the buffer's generic-proxy reads are ordered before the bulk copy overwrites it
             issue_table(seg + 2);
         }
     }
-    if (!ok) {  // copies in flight must land before the CTA's shared memory goes away
-        if (tid == 0) {
-            for (int s = seg_done + 1; s <= seg_done + 2 && b_first + s <= b_last; ++s)
-                mbar_wait_bounded(bar + (s & 1), (uint32_t)((s >> 1) & 1), kWaitPolls);
-        }
+    if (!ok && tid == 0) {  // copies in flight must land before the CTA's shared memory goes away
+        for (int s2 = seg; s2 <= seg + 1 && b_first + s2 <= b_last; ++s2)
+            mbar_wait_bounded(bar + (s2 & 1), (uint32_t)((s2 >> 1) & 1), kWaitPolls);
     }
 }
 
