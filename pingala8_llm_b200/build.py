@@ -21,15 +21,16 @@ def nvcc():
     return "nvcc"
 
 
-def build(verbose_ptxas=False, out=LIB):
+def build(verbose_ptxas=False, out=LIB, csrc=None, bdir=None):
+    csrc = csrc or CSRC
     objs = []
-    bdir = os.path.join(HERE, "_build")
+    bdir = bdir or os.path.join(HERE, "_build")
     os.makedirs(bdir, exist_ok=True)
     for s in SOURCES:
-        src = os.path.join(CSRC, s)
+        src = os.path.join(csrc, s)
         obj = os.path.join(bdir, s + ".o")
         cmd = [nvcc(), "-std=c++17", "-O3", "-lineinfo", *ARCH, "-Xcompiler", "-fPIC,-O2,-Wall", "-c", src, "-o", obj,
-               "-I", CSRC, "-I", os.path.join(os.path.dirname(HERE), "include")]
+               "-I", csrc, "-I", os.path.join(os.path.dirname(HERE), "include")]
         if s.endswith(".cu") and verbose_ptxas:
             cmd += ["-Xptxas", "-v"]
         print("+", " ".join(cmd), flush=True)

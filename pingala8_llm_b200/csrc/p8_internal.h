@@ -5,7 +5,7 @@
 
 #include <vector>
 
-#include "../../include/pingala8.h"
+#include "pingala8.h"
 #include "p8_format.h"
 
 // A prepared tensor: device pointers into the caller's slot plus the small device arrays built at prepare time.

@@ -25,6 +25,7 @@ def main():
     ap.add_argument("--group", default="gate_up", choices=sorted(GROUPS))
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--copies", type=int, default=1)
+    ap.add_argument("--graph", action="store_true", help="capture the calls in a CUDA graph (no host launch overhead)")
     a = ap.parse_args()
     shapes = GROUPS[a.group]
     copies = []
@@ -38,10 +39,23 @@ def main():
         mul_mat_vec_group(ts, x, outs=outs, workspace=ws)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(a.iters):
-        mul_mat_vec_group(copies[i % len(copies)], x, outs=outs, workspace=ws)
-    e1.record()
+    if a.graph:
+        s = torch.cuda.Stream()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for i in range(a.iters):
+                    mul_mat_vec_group(copies[i % len(copies)], x, outs=outs, workspace=ws, stream=s)
+        g.replay()
+        torch.cuda.synchronize()
+        e0.record()
+        g.replay()
+        e1.record()
+    else:
+        e0.record()
+        for i in range(a.iters):
+            mul_mat_vec_group(copies[i % len(copies)], x, outs=outs, workspace=ws)
+        e1.record()
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / a.iters
     nbytes = sum((r // 32) * (k // 256) * (68 + 2048) for r, k in shapes)
