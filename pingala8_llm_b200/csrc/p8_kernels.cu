@@ -207,8 +207,8 @@ cudaError_t launch_get_rows(const p8_tensor *t, const int32_t *ids, int64_t n, f
 // T[f][hs][t] = <A[f], q_t> (exact int32). The integer sums equal the reference's exact integer dot products, so the
 // only difference to the CPU result is float rounding in the final scale-and-sum.
 //
-//   k_act_prep  grid (nb, 8), 256 thr: first streams the group's weight tiles toward L2 (they do not depend on x),
-//               then waits for the producer of x; x -> FWHT(x sgn/c)/16 -> q, d per 128-col half-slice; 1/8 of the
+//   k_act_prep  grid (nb, 8), 256 thr: waits for the producer of x; x -> FWHT(x sgn/c)/16 -> q, d per 128-col
+//               half-slice; 1/8 of the
 //               table T[b] (64 KB per 256-col block) per CTA; coset nibble tables G.
 //   k_gemv      persistent, one 512-thread CTA per SM. The work is the list of (block b, tile g) units of up to four
 //               tensors that read the same x, ordered block-major and cut into equal contiguous ranges, so a CTA
@@ -257,8 +257,6 @@ struct PrepArgs {
     int *T;     // [nb][16384]
     int *G;     // [nsl][128]
     float *d;   // [nsl]
-    const uint8_t *pf[kMaxGroup];  // weight regions to stream toward L2 before waiting (M..D of each tensor)
-    size_t pfbytes[kMaxGroup];
 };
 
 __global__ void __launch_bounds__(256) k_act_prep(PrepArgs a) {
@@ -267,16 +265,6 @@ __global__ void __launch_bounds__(256) k_act_prep(PrepArgs a) {
     __shared__ int cx_s[64];
     const int b = blockIdx.x, fg = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
     pdl_launch_dependents();
-    {   // the weights do not depend on the producer of x: start their HBM -> L2 stream now (16 KB pieces)
-        const size_t nthreads = (size_t)gridDim.x * gridDim.y * 256, id = ((size_t)fg * gridDim.x + b) * 256 + tid;
-        for (int i = 0; i < a.ntensors; ++i) {
-            const size_t pieces = (a.pfbytes[i] + 16383) / 16384;
-            for (size_t p = id; p < pieces; p += nthreads) {
-                const size_t off = p * 16384, len = a.pfbytes[i] - off < 16384 ? a.pfbytes[i] - off : 16384;
-                bulk_prefetch_l2(a.pf[i] + off, (uint32_t)(len & ~(size_t)15));
-            }
-        }
-    }
     if (tid < 32) A_s[tid] = a.A[32 * fg + tid];
     pdl_wait();  // x and the workspace belong to the previous kernel until it completes
     if (tid < 32) {
@@ -516,19 +504,32 @@ __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
         }
         return c;
     };
+    // Three-deep cursor: the unit being computed, the next one (payload + scale in registers) and the one after
+    // (M word in a register). Every global load is issued one unit ahead of its first use.
     WarpCursor nc = {b_first, rr_first + warp};
     while (nc.b <= b_last && nc.rr >= rr_end(nc.b)) {
         ++nc.b;
         nc.rr = (nc.b <= b_last ? rr_begin(nc.b) : 0) + warp;
     }
-    uint32_t nxt[16];
-    uint32_t mt_n = 0;
-    auto fetch = [&](const WarpCursor &c) {
-        const int ti = tensor_of(a, c.rr), g = c.rr - a.t[ti].g0;
-        mt_n = __ldg(a.t[ti].M + (size_t)g * a.nb + c.b);
-        if ((mt_n >> 29) == 3) load3(a.t[ti].D + (mt_n & 0x1FFFFFFFu), lane, nxt);
+    auto m_of = [&](const WarpCursor &c) -> uint32_t {
+        const int ti = tensor_of(a, c.rr);
+        return __ldg(a.t[ti].M + (size_t)(c.rr - a.t[ti].g0) * a.nb + c.b);
     };
-    if (nc.b <= b_last) fetch(nc);
+    uint32_t nxt[16];
+    uint32_t mt_n = 0, mt_nn = 0;
+    uint16_t s_n = 0;
+    auto fetch = [&](const WarpCursor &c, uint32_t mt) {  // payload + row scale of unit c (its M word known)
+        const int ti = tensor_of(a, c.rr), g = c.rr - a.t[ti].g0;
+        if ((mt >> 29) == 3) load3(a.t[ti].D + (mt & 0x1FFFFFFFu), lane, nxt);
+        s_n = __ldg(a.t[ti].S + (size_t)c.b * a.t[ti].rows + g * 32 + lane);
+    };
+    WarpCursor nc2 = nc;
+    if (nc.b <= b_last) {
+        mt_n = m_of(nc);
+        fetch(nc, mt_n);
+        nc2 = advance(nc);
+        if (nc2.b <= b_last) mt_nn = m_of(nc2);
+    }
     bool ok = true;
     int seg = 0;
     for (; b_first + seg <= b_last; ++seg) {
@@ -542,11 +543,17 @@ __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
         while (nc.b == b) {
             const int rr = nc.rr;
             const uint32_t mt = mt_n;
+            const uint16_t sc = s_n;
             uint32_t cur[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) cur[i] = nxt[i];
-            nc = advance(nc);
-            if (nc.b <= b_last) fetch(nc);  // possibly in the next segment
+            nc = nc2;
+            mt_n = mt_nn;
+            if (nc.b <= b_last) {
+                fetch(nc, mt_n);  // possibly in the next segment
+                nc2 = advance(nc);
+                if (nc2.b <= b_last) mt_nn = m_of(nc2);
+            }
             const int ti = tensor_of(a, rr), g = rr - a.t[ti].g0;
             const GemvTensor &T = a.t[ti];
             const int c = (int)(mt >> 29);
@@ -566,7 +573,7 @@ __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
                 part = (seg & 1) ? tile_row_other<1>(c, p0, po, lane, d0, d1) : tile_row_other<0>(c, p0, po, lane, d0, d1);
             }
             const int r = g * 32 + lane;
-            T.part[(size_t)b * T.rows + r] = __fmul_rn(part, h2f(T.S[(size_t)b * T.rows + r]));
+            T.part[(size_t)b * T.rows + r] = __fmul_rn(part, h2f(sc));
         }
         // arrivals of this warp's tiles of block b; the warp that brings a tile's last block finishes its 32 rows
         __syncwarp();
@@ -678,8 +685,6 @@ static p8_status launch_gemv_col(const p8_tensor *const *ts, int nt, const float
         g.cnt = t->tile_cnt;
         g.rows = t->rows; g.ng = t->ng; g.g0 = g0;
         g0 += t->ng;
-        pa.pf[i] = reinterpret_cast<const uint8_t *>(t->M);
-        pa.pfbytes[i] = (t->kbytes - kHdrBytes);  // M, S and the payload are contiguous after the header
     }
     ga.ng_total = g0;
     ga.units = (long long)g0 * t0->nb;
