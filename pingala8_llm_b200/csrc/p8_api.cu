@@ -35,7 +35,6 @@ void free_tensor(p8_tensor *t) {
     cudaFree(t->cp);
     cudaFree(t->cc);
     cudaFree(t->cv);
-    cudaFree(t->tile_cnt);
     t->magic = 0;
     delete t;
 }
@@ -131,9 +130,7 @@ p8_status p8_prepare(const void *dev_slot, size_t nbytes, int64_t K, int64_t row
         t->act_hash = h;
     }
     if (dmalloc_copy(&t->ic, ic.data(), ic.size()) != cudaSuccess || dmalloc_copy(&t->cp, cp.data(), cp.size()) != cudaSuccess ||
-        dmalloc_copy(&t->cc, cc.data(), cc.size()) != cudaSuccess || dmalloc_copy(&t->cv, cv.data(), cv.size()) != cudaSuccess ||
-        cudaMalloc((void **)&t->tile_cnt, sizeof(unsigned int) * ng) != cudaSuccess ||
-        cudaMemset(t->tile_cnt, 0, sizeof(unsigned int) * ng) != cudaSuccess) {
+        dmalloc_copy(&t->cc, cc.data(), cc.size()) != cudaSuccess || dmalloc_copy(&t->cv, cv.data(), cv.size()) != cudaSuccess) {
         free_tensor(t);
         return P8_ERR_CUDA;
     }

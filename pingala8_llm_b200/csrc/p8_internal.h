@@ -27,7 +27,6 @@ struct p8_tensor {
     int *cp;     // clamp-delta CSR by ORIGINAL row (rows + 1), entries in slot order within a row (CP:266-273)
     uint16_t *cc;
     float *cv;
-    unsigned int *tile_cnt;   // per-tile arrival counters of the GEMV (zero between calls)
     // host copies
     uint32_t cs;              // coset word
     uint32_t class_mask;      // bit c set if some tile has class c

@@ -215,9 +215,10 @@ cudaError_t launch_get_rows(const p8_tensor *t, const int32_t *ids, int64_t n, f
 //               touches at most a few blocks. Block tables arrive by bulk copy (TMA engine, mbarrier), double
 //               buffered; the payload words of a warp's next unit are loaded into registers while the current unit
 //               computes. Each lane owns one row: per chunk 1 PRMT (field byte + rotated chunk offset -> table byte
-//               address) + 1 LDS + 1 add. A unit stores its 32 row partials (plain coalesced stores, [b][rows]); the
-//               warp that completes a tile's last block (per-tile arrival counter) sums its partials in block order,
-//               adds the clamp delta and scatters y[prm[r]] (deterministic, no float atomics).
+//               address) + 1 LDS + 1 add. A unit stores its 32 row partials (plain coalesced stores, [b][rows]).
+//               After a grid barrier (the grid is one CTA per SM, all resident) every CTA sums an equal share of the
+//               rows over the blocks in block order, adds the clamp delta and scatters y[prm[r]] (deterministic,
+//               no float atomics).
 // Both kernels use programmatic dependent launch.
 // ================================================================================================================
 constexpr int kTabInts = 256 * 64;          // T ints per 256-column block: [f][hs][t]
@@ -243,9 +244,7 @@ struct GemvTensor {
     const float *cv;
     float *Y;
     float *part;          // [nb][rows] row partials per block
-    unsigned int *cnt;    // [ng] per-tile arrival counters (tensor-owned, zero between calls)
-    size_t dbytes;        // payload bytes (for the L2 prefetch)
-    int rows, ng, g0;     // g0: first unit index of this tensor inside one block
+    int rows, ng, g0, row0;  // g0: first unit index of this tensor inside one block; row0: first row in the group
 };
 
 struct PrepArgs {
@@ -257,6 +256,7 @@ struct PrepArgs {
     int *T;     // [nb][16384]
     int *G;     // [nsl][128]
     float *d;   // [nsl]
+    unsigned int *arrive;  // the GEMV's grid-barrier counter
 };
 
 __global__ void __launch_bounds__(256) k_act_prep(PrepArgs a) {
@@ -267,6 +267,7 @@ __global__ void __launch_bounds__(256) k_act_prep(PrepArgs a) {
     pdl_launch_dependents();
     if (tid < 32) A_s[tid] = a.A[32 * fg + tid];
     pdl_wait();  // x and the workspace belong to the previous kernel until it completes
+    if (b == 0 && fg == 0 && tid == 0) *a.arrive = 0u;
     if (tid < 32) {
         const float *x = a.X + b * 256 + 8 * lane;
         const float *ic = a.ic + b * 256 + 8 * lane;
@@ -315,6 +316,8 @@ __global__ void __launch_bounds__(256) k_act_prep(PrepArgs a) {
 
 struct GemvArgs {
     GemvTensor t[kMaxGroup];
+    unsigned int *arrive;  // grid-barrier counter, zeroed by the prep kernel
+    int rows_total;
     int ntensors;
     const int *T, *G;
     const float *d;
@@ -575,27 +578,6 @@ __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
             const int r = g * 32 + lane;
             T.part[(size_t)b * T.rows + r] = __fmul_rn(part, h2f(sc));
         }
-        // arrivals of this warp's tiles of block b; the warp that brings a tile's last block finishes its 32 rows
-        __syncwarp();
-        if (lane == 0) __threadfence();  // release: the warp's partial stores (ordered by __syncwarp) before the counts
-        __syncwarp();
-        for (int rr = rr_begin(b) + warp; rr < rr_end(b); rr += kGemvWarps) {
-            const int ti = tensor_of(a, rr), g = rr - a.t[ti].g0;
-            const GemvTensor &T = a.t[ti];
-            unsigned prev = 0;
-            if (lane == 0) prev = atomicAdd(T.cnt + g, 1u);
-            prev = __shfl_sync(0xffffffffu, prev, 0);
-            if (prev == (unsigned)(a.nb - 1)) {
-                __threadfence();
-                const int r = g * 32 + lane;
-                float s = 0.f;
-                for (int bb = 0; bb < a.nb; ++bb) s = __fadd_rn(s, __ldcg(T.part + (size_t)bb * T.rows + r));
-                const int ro = T.prm[r];
-                for (int e = T.cp[ro]; e < T.cp[ro + 1]; ++e) s = __fadd_rn(s, __fmul_rn(T.cv[e], a.X[T.cc[e]]));
-                T.Y[ro] = s;
-                if (lane == 0) T.cnt[g] = 0u;  // leave the counter zero for the next call
-            }
-        }
         __syncthreads();  // every warp is done with this segment's buffer
         if (tid == 0 && b_first + seg + 2 <= b_last) {
             fence_proxy_async();  // the buffer's generic-proxy reads are ordered before the bulk copy overwrites it
@@ -606,11 +588,44 @@ __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
         for (int s2 = seg; s2 <= seg + 1 && b_first + s2 <= b_last; ++s2)
             mbar_wait_bounded(bar + (s2 & 1), (uint32_t)((s2 >> 1) & 1), kWaitPolls);
     }
+    // grid barrier (all CTAs are resident: one per SM), then every CTA reduces an equal share of the rows:
+    // y[prm[r]] = sum_b part[b][r] (block order, deterministic) + sum_e val_e x[col_e]
+    __shared__ int s_ok;
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        atomicAdd(a.arrive, 1u);
+        uint32_t n = 0;
+        int spins = 0;
+        while ((n = *reinterpret_cast<volatile unsigned int *>(a.arrive)) < gridDim.x && spins < (1 << 26)) {
+            __nanosleep(32);
+            ++spins;
+        }
+        s_ok = n >= gridDim.x;
+        if (!s_ok) atomicOr(&g_p8_device_error, 2u);
+        __threadfence();
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    const int r0 = (int)((long long)a.rows_total * blockIdx.x / gridDim.x), r1 = (int)((long long)a.rows_total * (blockIdx.x + 1) / gridDim.x);
+    for (int rt = r0 + tid; rt < r1; rt += kGemvThreads) {
+        int ti = 0;
+#pragma unroll
+        for (int i = 1; i < kMaxGroup; ++i)
+            if (i < a.ntensors && rt >= a.t[i].row0) ti = i;
+        const GemvTensor &T = a.t[ti];
+        const int r = rt - T.row0;
+        float s = 0.f;
+        for (int bb = 0; bb < a.nb; ++bb) s = __fadd_rn(s, __ldcg(T.part + (size_t)bb * T.rows + r));
+        const int ro = T.prm[r];
+        for (int e = T.cp[ro]; e < T.cp[ro + 1]; ++e) s = __fadd_rn(s, __fmul_rn(T.cv[e], a.X[T.cc[e]]));
+        T.Y[ro] = s;
+    }
 }
 
 // workspace layout (bytes, each part 256-aligned): T | G | d | partials ([nb][rows] per tensor)
 struct GemvWs {
-    size_t T, G, d, part, total;
+    size_t T, G, d, arrive, part, total;
 };
 static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
 static GemvWs gemv_ws_layout(const p8_tensor *const *ts, int nt) {
@@ -621,7 +636,8 @@ static GemvWs gemv_ws_layout(const p8_tensor *const *ts, int nt) {
     w.T = 0;
     w.G = w.T + al256((size_t)t->nb * kTabBytes);
     w.d = w.G + al256((size_t)t->nsl * kGInts * 4);
-    w.part = w.d + al256((size_t)t->nsl * 4);
+    w.arrive = w.d + al256((size_t)t->nsl * 4);
+    w.part = w.arrive + 256;
     w.total = w.part + part;
     return w;
 }
@@ -670,9 +686,11 @@ static p8_status launch_gemv_col(const p8_tensor *const *ts, int nt, const float
     pa.T = reinterpret_cast<int *>(w + L.T);
     pa.G = reinterpret_cast<int *>(w + L.G);
     pa.d = reinterpret_cast<float *>(w + L.d);
+    pa.arrive = reinterpret_cast<unsigned int *>(w + L.arrive);
     GemvArgs ga;
     memset(&ga, 0, sizeof(ga));
     ga.ntensors = nt; ga.T = pa.T; ga.G = pa.G; ga.d = pa.d; ga.X = x; ga.nb = t0->nb; ga.nsl = t0->nsl;
+    ga.arrive = pa.arrive;
     size_t poff = L.part;
     int g0 = 0;
     for (int i = 0; i < nt; ++i) {
@@ -682,9 +700,9 @@ static p8_status launch_gemv_col(const p8_tensor *const *ts, int nt, const float
         g.Y = Ys[i];
         g.part = reinterpret_cast<float *>(w + poff);
         poff += al256((size_t)t->nb * t->rows * 4);
-        g.cnt = t->tile_cnt;
-        g.rows = t->rows; g.ng = t->ng; g.g0 = g0;
+        g.rows = t->rows; g.ng = t->ng; g.g0 = g0; g.row0 = ga.rows_total;
         g0 += t->ng;
+        ga.rows_total += t->rows;
     }
     ga.ng_total = g0;
     ga.units = (long long)g0 * t0->nb;
