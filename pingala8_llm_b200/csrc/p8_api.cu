@@ -100,6 +100,12 @@ p8_status p8_prepare(const void *dev_slot, size_t nbytes, int64_t K, int64_t row
     t->pinv = (const int16_t *)(base + so.Q);
     memcpy(&t->cs, hdr.data() + 2048, 4);
     t->class_mask = cm;
+    {   // uniform layout: one class everywhere, payloads back to back in tile order (single-class writers, VR3)
+        const int c0 = (int)(M[0] >> 29);
+        bool uni = c0 != 0;
+        for (size_t i = 0; uni && i < nt; ++i) uni = M[i] == ((uint32_t)(i * 64 * NW(c0)) | ((uint32_t)c0 << 29));
+        t->uniform_class = uni ? c0 : 0;
+    }
     memcpy(t->hist, hist, sizeof(hist));
     t->A_host.assign((const uint32_t *)hdr.data(), (const uint32_t *)hdr.data() + 256);
     // sgn / c per column, float division as vrc_init (CP:264)

@@ -30,6 +30,7 @@ struct p8_tensor {
     // host copies
     uint32_t cs;              // coset word
     uint32_t class_mask;      // bit c set if some tile has class c
+    int uniform_class;        // c if every tile has class c and tile i's payload starts at word i * 64 NW(c), else 0
     uint64_t hist[8];
     uint64_t act_hash;        // FNV-1a of (sgn/c per column, codebook, coset): tensors with equal hashes share a prepared x
     std::vector<uint32_t> A_host;

@@ -245,6 +245,7 @@ struct GemvTensor {
     float *Y;
     float *part;          // [nb][rows] row partials per block
     int rows, ng, g0, row0;  // g0: first unit index of this tensor inside one block; row0: first row in the group
+    int ucls;                // uniform class (payload of tile i at word i * 64 NW), 0 if the M words must be read
 };
 
 struct PrepArgs {
@@ -516,7 +517,10 @@ __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
     }
     auto m_of = [&](const WarpCursor &c) -> uint32_t {
         const int ti = tensor_of(a, c.rr);
-        return __ldg(a.t[ti].M + (size_t)(c.rr - a.t[ti].g0) * a.nb + c.b);
+        const uint32_t tile = (uint32_t)(c.rr - a.t[ti].g0) * (uint32_t)a.nb + (uint32_t)c.b;
+        const int uc = a.t[ti].ucls;
+        if (uc) return (tile * (uint32_t)(64 * NW(uc))) | ((uint32_t)uc << 29);
+        return __ldg(a.t[ti].M + tile);
     };
     uint32_t nxt[16];
     uint32_t mt_n = 0, mt_nn = 0;
@@ -700,7 +704,7 @@ static p8_status launch_gemv_col(const p8_tensor *const *ts, int nt, const float
         g.Y = Ys[i];
         g.part = reinterpret_cast<float *>(w + poff);
         poff += al256((size_t)t->nb * t->rows * 4);
-        g.rows = t->rows; g.ng = t->ng; g.g0 = g0; g.row0 = ga.rows_total;
+        g.rows = t->rows; g.ng = t->ng; g.g0 = g0; g.row0 = ga.rows_total; g.ucls = t->uniform_class;
         g0 += t->ng;
         ga.rows_total += t->rows;
     }
