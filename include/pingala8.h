@@ -80,6 +80,16 @@ size_t p8_workspace_size_group(const p8_tensor *const *ts, int n, int64_t ncols)
 p8_status p8_mul_mat_vec_group(const p8_tensor *const *ts, int n, const float *x, float *const *ys, void *workspace,
                                size_t workspace_bytes, void *stream);
 
+/* y = W x like p8_mul_mat_vec, but with no workspace argument and no allocation: the scratch is a fixed 6 MiB device
+ * array inside the library, for callers that cannot allocate device memory at call time and have no buffer to lend
+ * (e.g. a host framework that plans all device memory up front). No counterpart in the reference (its GEMV takes
+ * scratch from the ggml pool, CU:3182-3184). Limit: tensors with p8_workspace_size(t, 1) <= p8_noalloc_scratch_bytes()
+ * (else P8_ERR_WORKSPACE). Every GPU that loads the library holds the array until exit; calls share it, so calls that
+ * can overlap on the GPU race and must be serialised by the caller. The first call on a device looks up the array's
+ * device address: make it before any stream capture. */
+size_t p8_noalloc_scratch_bytes(void);
+p8_status p8_mul_mat_vec_noalloc(const p8_tensor *t, const float *x, float *y, void *stream);
+
 /* Y[n][ldy] (rows per column) = W X[n][ldx], n < ncols. ncols > 1: batched decode / prefill. Replaces
  * ggml_cuda_f44_mul_mat_q8 (CU:1014-1054). */
 p8_status p8_mul_mat(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy,

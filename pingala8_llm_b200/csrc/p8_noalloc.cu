@@ -1,0 +1,63 @@
+// p8_noalloc.cu -- a batch-1 GEMV entry point that allocates nothing and needs no caller workspace.
+//
+// For callers that cannot allocate device memory when they run the op and have no scratch buffer to lend it: for
+// example a host application that plans every device allocation up front and gives this op only its weight, input and
+// output buffers, or a code path that must not call cudaMalloc (which can synchronise the device and can fail under
+// memory pressure). The scratch the GEMV needs (activation tables, coset tables, scales, the grid-barrier counter and
+// the row partials) lives in one fixed device array of this file instead of a caller workspace.
+//
+// The array is kNoAllocScratchBytes (6 MiB); every GPU that loads this library holds it until the process exits.
+// A tensor whose GEMV needs more scratch than that (p8_workspace_size(t, 1) > 6 MiB, e.g. K > 16384 or very many rows
+// per 256-column block) is rejected with P8_ERR_WORKSPACE.
+//
+// All calls share the array and it keeps the previous call's contents: the kernels rewrite every table and partial
+// they read and clear the barrier counter at the start of each call, so no state leaks between calls. Calls that can
+// overlap on the GPU (other streams, other host threads) race on the array and must be serialised by the caller.
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "p8_internal.h"
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = (size_t)6 << 20;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_mu;
+void *g_scratch_addr[64] = {nullptr};  // per device: the device address of g_noalloc_scratch
+
+// Device address of the scratch array on the current device. The array's name in host code is only a host-side
+// stand-in, so the address is looked up once per device with that device current (the first call on a device does
+// this set-up; make that first call before any stream capture).
+p8_status scratch_for_current_device(void **out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return P8_ERR_CUDA;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_scratch_addr[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return P8_ERR_CUDA;
+        g_scratch_addr[dev] = p;
+    }
+    *out = g_scratch_addr[dev];
+    return P8_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t p8_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+p8_status p8_mul_mat_vec_noalloc(const p8_tensor *t, const float *x, float *y, void *stream) {
+    if (!t || t->magic != kTensorMagic) return P8_ERR_NOT_PREPARED;
+    if (!x || !y || ((uintptr_t)x & 15)) return P8_ERR_ARG;
+    if (p8::gemv_workspace(t, 1) > kNoAllocScratchBytes) return P8_ERR_WORKSPACE;
+    void *scratch = nullptr;
+    p8_status st = scratch_for_current_device(&scratch);
+    if (st) return st;
+    return p8::launch_gemv(t, x, 1, t->K, y, t->rows, scratch, kNoAllocScratchBytes, (cudaStream_t)stream);
+}
+
+}  // extern "C"
