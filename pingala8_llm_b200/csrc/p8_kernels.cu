@@ -592,38 +592,58 @@ __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
         for (int s2 = seg; s2 <= seg + 1 && b_first + s2 <= b_last; ++s2)
             mbar_wait_bounded(bar + (s2 & 1), (uint32_t)((s2 >> 1) & 1), kWaitPolls);
     }
-    // grid barrier (all CTAs are resident: one per SM), then every CTA reduces an equal share of the rows:
-    // y[prm[r]] = sum_b part[b][r] (block order, deterministic) + sum_e val_e x[col_e]
+    // grid barrier (all CTAs are resident: one per SM; the prep kernel zeroed the counter), then every CTA reduces an
+    // equal share of the rows: y[prm[r]] = sum_b part[b][r] (block order, deterministic) + sum_e val_e x[col_e]
     __shared__ int s_ok;
     __syncthreads();
     if (tid == 0) {
-        __threadfence();
-        atomicAdd(a.arrive, 1u);
-        uint32_t n = 0;
-        int spins = 0;
-        while ((n = *reinterpret_cast<volatile unsigned int *>(a.arrive)) < gridDim.x && spins < (1 << 26)) {
-            __nanosleep(32);
-            ++spins;
-        }
+        unsigned int n;  // release: this CTA's partial stores are visible before its arrival is counted
+        asm volatile("atom.add.release.gpu.global.u32 %0, [%1], 1;" : "=r"(n) : "l"(a.arrive) : "memory");
+        ++n;
+        for (int spins = 0; n < gridDim.x && spins < (1 << 26); ++spins)
+            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(n) : "l"(a.arrive) : "memory");
         s_ok = n >= gridDim.x;
         if (!s_ok) atomicOr(&g_p8_device_error, 2u);
-        __threadfence();
     }
     __syncthreads();
     if (!s_ok) return;
+    // 128 rows x 4 block slices per pass: each slice sums its blocks in order with four loads in flight, slice 0
+    // then adds the four slice sums in order
+    constexpr int kRedRows = 128, kRedSlices = kGemvThreads / kRedRows;
+    float *red = reinterpret_cast<float *>(g_smem + kSmemT0);  // the table buffers are free now
     const int r0 = (int)((long long)a.rows_total * blockIdx.x / gridDim.x), r1 = (int)((long long)a.rows_total * (blockIdx.x + 1) / gridDim.x);
-    for (int rt = r0 + tid; rt < r1; rt += kGemvThreads) {
+    const int rl = tid % kRedRows, sl = tid / kRedRows;
+    const int b_lo = a.nb * sl / kRedSlices, b_hi = a.nb * (sl + 1) / kRedSlices;
+    for (int base = r0; base < r1; base += kRedRows) {
+        const int rt = base + rl;
         int ti = 0;
-#pragma unroll
-        for (int i = 1; i < kMaxGroup; ++i)
-            if (i < a.ntensors && rt >= a.t[i].row0) ti = i;
-        const GemvTensor &T = a.t[ti];
-        const int r = rt - T.row0;
         float s = 0.f;
-        for (int bb = 0; bb < a.nb; ++bb) s = __fadd_rn(s, __ldcg(T.part + (size_t)bb * T.rows + r));
-        const int ro = T.prm[r];
-        for (int e = T.cp[ro]; e < T.cp[ro + 1]; ++e) s = __fadd_rn(s, __fmul_rn(T.cv[e], a.X[T.cc[e]]));
-        T.Y[ro] = s;
+        if (rt < r1) {
+#pragma unroll
+            for (int i = 1; i < kMaxGroup; ++i)
+                if (i < a.ntensors && rt >= a.t[i].row0) ti = i;
+            const GemvTensor &T = a.t[ti];
+            const float *p = T.part + (rt - T.row0);
+            int bb = b_lo;
+            for (; bb + 4 <= b_hi; bb += 4) {
+                const float p0 = __ldcg(p + (size_t)bb * T.rows), p1 = __ldcg(p + (size_t)(bb + 1) * T.rows);
+                const float p2 = __ldcg(p + (size_t)(bb + 2) * T.rows), p3 = __ldcg(p + (size_t)(bb + 3) * T.rows);
+                s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, p0), p1), p2), p3);
+            }
+            for (; bb < b_hi; ++bb) s = __fadd_rn(s, __ldcg(p + (size_t)bb * T.rows));
+        }
+        red[sl * kRedRows + rl] = s;
+        __syncthreads();
+        if (sl == 0 && rt < r1) {
+            float y = red[rl];
+#pragma unroll
+            for (int j = 1; j < kRedSlices; ++j) y = __fadd_rn(y, red[j * kRedRows + rl]);
+            const GemvTensor &T = a.t[ti];
+            const int ro = T.prm[rt - T.row0];
+            for (int e = T.cp[ro]; e < T.cp[ro + 1]; ++e) y = __fadd_rn(y, __fmul_rn(T.cv[e], a.X[T.cc[e]]));
+            T.Y[ro] = y;
+        }
+        __syncthreads();
     }
 }
 
