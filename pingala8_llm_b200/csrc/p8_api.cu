@@ -35,6 +35,7 @@ void free_tensor(p8_tensor *t) {
     cudaFree(t->cp);
     cudaFree(t->cc);
     cudaFree(t->cv);
+    cudaFree(t->rsc);
     t->magic = 0;
     delete t;
 }
@@ -139,6 +140,10 @@ p8_status p8_prepare(const void *dev_slot, size_t nbytes, int64_t K, int64_t row
         dmalloc_copy(&t->cc, cc.data(), cc.size()) != cudaSuccess || dmalloc_copy(&t->cv, cv.data(), cv.size()) != cudaSuccess) {
         free_tensor(t);
         return P8_ERR_CUDA;
+    }
+    if ((st = gemm_prepare(t, s)) != P8_OK) {
+        free_tensor(t);
+        return st;
     }
     {
         std::lock_guard<std::mutex> lk(g_mu);

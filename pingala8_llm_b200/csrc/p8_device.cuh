@@ -64,12 +64,11 @@ __device__ __forceinline__ uint32_t f1_at(const uint32_t (&w)[NWA], int k) {
     return field(w, 1, W1(C) - 1, k) | (((w[0] >> k) & 1u) << (W1(C) - 1));
 }
 
-// Exact integer weights of chunk t (4 values) of lane j from its words (coset folded in, no int8 wrap: the tables are
-// checked at prepare time). A is a shared-memory copy of the codebook.
+// Exact integer weights of the chunk at step k (chunk t = (j + k) & 31 of lane j) from the lane's words (coset folded
+// in, no int8 wrap: the tables are checked at prepare time). A is a shared-memory copy of the codebook.
 template <int C, int NWA>
-__device__ __forceinline__ void chunk_ints(const uint32_t (&w)[NWA], const uint32_t *A, uint32_t cs, uint32_t H, int j, int t,
-                                           int (&v)[4]) {
-    const int k = (t - j) & 31;
+__device__ __forceinline__ void chunk_ints_step(const uint32_t (&w)[NWA], const uint32_t *A, uint32_t cs, uint32_t H, int k, int t,
+                                                int (&v)[4]) {
     const int h = (H >> t) & 1u;
     const uint32_t a1 = A[f1_at<C>(w, k)];
     const uint32_t a2 = W2(C) ? A[field(w, W1(C), W2(C) ? W2(C) : 1, k)] : 0u;
@@ -82,6 +81,12 @@ __device__ __forceinline__ void chunk_ints(const uint32_t (&w)[NWA], const uint3
         if (W3(C)) x += (int)(int8_t)(a3 >> (8 * e)) + ce;
         v[e] = x;
     }
+}
+// the same for chunk t of lane j (step k = (t - j) & 31)
+template <int C, int NWA>
+__device__ __forceinline__ void chunk_ints(const uint32_t (&w)[NWA], const uint32_t *A, uint32_t cs, uint32_t H, int j, int t,
+                                           int (&v)[4]) {
+    chunk_ints_step<C>(w, A, cs, H, (t - j) & 31, t, v);
 }
 
 // lane words of half-slice hs: word i of lane j at D[off + hs*NW*32 + (i>>1)*64 + 2j + (i&1)]

@@ -27,6 +27,7 @@ struct p8_tensor {
     int *cp;     // clamp-delta CSR by ORIGINAL row (rows + 1), entries in slot order within a row (CP:266-273)
     uint16_t *cc;
     float *cv;
+    float2 *rsc;  // per sorted row {2^sigma, 2^-sigma}: power-of-two weight scale that keeps the GEMM's fp16 operand in range
     // host copies
     uint32_t cs;              // coset word
     uint32_t class_mask;      // bit c set if some tile has class c
@@ -68,4 +69,5 @@ size_t gemm_workspace(const p8_tensor *t, int64_t ncols);
 p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy, void *ws,
                       size_t ws_bytes, cudaStream_t st);
 bool gemm_supported(const p8_tensor *t, int64_t ncols);
+p8_status gemm_prepare(p8_tensor *t, cudaStream_t st);  // prepare-time per-row scales (rsc)
 }  // namespace p8

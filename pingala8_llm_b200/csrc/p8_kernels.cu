@@ -769,4 +769,9 @@ unsigned int read_and_clear_device_error() {
     return v;
 }
 
+// ================================================================================================================
+// 3. Batched GEMM (tcgen05)
+// ================================================================================================================
+#include "p8_gemm.cuh"
+
 }  // namespace p8

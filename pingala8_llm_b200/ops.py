@@ -72,15 +72,21 @@ class P8Tensor:
         return y
 
     def mul_mat(self, X, out=None, workspace=None, stream=None):
-        """Y = X W^T: X float32 [ncols, K] -> Y float32 [ncols, rows] (ggml dst [rows, ncols])."""
-        X = X.contiguous()
+        """Y = X W^T: X float32 [ncols, K] -> Y float32 [ncols, rows] (ggml dst [rows, ncols]).
+
+        X and out may be row-strided views (unit column stride; X's row stride a multiple of 4 floats), as ggml's
+        src1 / dst with nb[1] > ne[0] * 4."""
+        if X.dim() == 2 and (X.stride(1) != 1 or X.stride(0) % 4 or X.data_ptr() % 16):
+            X = X.contiguous()
         if X.dtype != torch.float32 or X.dim() != 2 or X.shape[1] != self.K or not X.is_cuda:
             raise ValueError("X must be float32 CUDA [ncols, K]")
         n = X.shape[0]
         Y = out if out is not None else torch.empty(n, self.rows, dtype=torch.float32, device=X.device)
+        if Y.dim() != 2 or Y.shape[0] != n or Y.shape[1] != self.rows or Y.stride(1) != 1 or Y.dtype != torch.float32:
+            raise ValueError("out must be float32 [ncols, rows] with unit column stride")
         ws = workspace if workspace is not None else self.workspace(n)
-        check(lib().p8_mul_mat(self.handle, _ptr(X), n, self.K, _ptr(Y), Y.stride(0), _ptr(ws), ws.numel(), _stream(stream)),
-              "p8_mul_mat")
+        check(lib().p8_mul_mat(self.handle, _ptr(X), n, X.stride(0), _ptr(Y), Y.stride(0), _ptr(ws), ws.numel(),
+                               _stream(stream)), "p8_mul_mat")
         return Y
 
     def get_rows(self, ids, out=None, stream=None):
