@@ -11,8 +11,9 @@ CUDA graph and replayed per step. Attention, norms and the LM head are not part 
   value     tokens/s with inputs resident in HBM (device-timed with CUDA events, max over ranks)
   e2e       the same through the public op API with a pinned-host input vector copied in and the final output copied
             out every step
-  roofline  p8_mul_mat_vec_group (k_act_prep + k_gemv) algorithmic bytes / event-timed call duration,
-            against MEASURED_PEAKS.json hbm_gbs
+  roofline  the dominant call type (p8_mul_mat_vec_group = k_act_prep + k_gemv): algorithmic bytes / per-call
+            duration, timed with CUDA events around a graph of that call type's 32 per-layer calls, against
+            MEASURED_PEAKS.json hbm_gbs; traffic = DRAM bytes of the same call from an ncu capture
   cpu_baseline  the reference's own CPU core (oracle/_ref, x16 vrc_tg) on one layer's 7 GEMVs, all host threads
 
 usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
@@ -32,7 +33,7 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 LLAMA8B = dict(name="llama3.1-8b", layers=32, hidden=4096, ffn=14336, q=4096, kv=1024)
-METRIC = "decode tok/s bs1 (Llama-3.1-8B shape, 2-bit Pingala-8 projections)"
+METRIC = "decode tok/s bs1 (Llama-3.1-8B shape, 2-bit); dequant-GEMV HBM GB/s % of peak"
 
 
 def layer_shapes(m):
@@ -55,56 +56,92 @@ def algo_bytes_gemv(rows, K, cls=3):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    """SM clocks and clock-event (throttle) reasons sampled every 2 ms through NVML while the timed region runs
+    (read-only queries); falls back to nvidia-smi -lms 200 when NVML is unavailable."""
 
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap",
+               0x80: "hw_power_brake_slowdown"}
     Q = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown," \
         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
 
     def __init__(self, index):
         self.index = index
+        self.sm, self.mx, self.reasons = [], None, set()
+        self.stop = threading.Event()
         self.proc = None
-        self.lines = []
+        self.t = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "200",
-                                          "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            import pynvml as N
+            N.nvmlInit()
+            h = N.nvmlDeviceGetHandleByIndex(self.index)
+            self.mx = float(N.nvmlDeviceGetMaxClockInfo(h, N.NVML_CLOCK_SM))
+            get_reasons = getattr(N, "nvmlDeviceGetCurrentClocksEventReasons", None) or N.nvmlDeviceGetCurrentClocksThrottleReasons
+
+            def poll():
+                while not self.stop.is_set():
+                    self._nvml_sample(N, h, get_reasons)
+                    time.sleep(0.002)
+                self._nvml_sample(N, h, get_reasons)
+
+            self.t = threading.Thread(target=poll, daemon=True)
             self.t.start()
-        except (OSError, FileNotFoundError):
-            self.proc = None
+        except Exception:
+            try:
+                self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "200",
+                                              "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self.t = threading.Thread(target=self._smi_read, daemon=True)
+                self.t.start()
+            except (OSError, FileNotFoundError):
+                self.proc = None
         return self
 
-    def _read(self):
+    def _nvml_sample(self, N, h, get_reasons):
+        try:
+            self.sm.append(float(N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM)))
+            r = int(get_reasons(h))
+            for bit, name in self.REASONS.items():
+                if r & bit:
+                    self.reasons.add(name)
+        except Exception:
+            pass
+
+    def _smi_read(self):
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.proc.stdout:
-            self.lines.append(ln.strip())
+            p = [x.strip() for x in ln.strip().split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                self.sm.append(float(p[1]))
+                self.mx = float(p[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, p[5:9]):
+                if v.lower() == "active":
+                    self.reasons.add(n)
 
     def __exit__(self, *a):
+        self.stop.set()
         if self.proc:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        if self.t:
+            self.t.join(timeout=5)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            p = [x.strip() for x in ln.split(",")]
-            if len(p) < 9:
-                continue
-            try:
-                sm.append(float(p[1]))
-                mx = float(p[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, p[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        if not self.sm:
+            return {"sm_mhz": None, "sm_max_mhz": self.mx, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(self.sm), "sm_max_mhz": self.mx, "reasons": sorted(self.reasons),
+                "samples": len(self.sm)}
+
+
+# DRAM bytes (read + write) of one call, from ncu captures of the same call (profiles/k_gemv_llama8b_gate_up.md)
+TRAFFIC_BYTES = {"gate+up": 31587840}
 
 
 def measured_peaks():
@@ -251,34 +288,47 @@ def run_b200(args, rank, world, local_rank):
     torch.cuda.synchronize()
     barrier()
     t_e2e = e2.elapsed_time(e3) / 1e3
-    # ---- roofline of the GEMV call: one eager pass with events around every call
-    evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * len(groups) * model["layers"])]
+    # ---- roofline per call type: the 32 calls of one group type (one per layer, distinct weights) captured as a
+    # graph and replayed; per-call duration = replay time / 32, against the call's algorithmic bytes
     dims = {nm: (rows, K) for nm, rows, K in shapes}
-    bytes_total = 0
-    i = 0
-    with torch.cuda.stream(stream):
-        x = buf["x"]
-        for ts in layers:
-            src = inputs(x)
-            for grp in groups:
-                evs[i].record(stream)
-                mul_mat_vec_group([ts[n] for n in grp], src[grp], outs=[buf[n] for n in grp], workspace=ws, stream=stream)
-                evs[i + 1].record(stream)
-                bytes_total += sum(algo_bytes_gemv(*dims[n]) for n in grp) - 4 * dims[grp[0]][1] * (len(grp) - 1)
-                i += 2
-    torch.cuda.synchronize()
-    call_s = sum(evs[j].elapsed_time(evs[j + 1]) for j in range(0, len(evs), 2)) / 1e3
-    ncalls = len(evs) // 2
+    reps = max(3, args.steps // 4)
+    per_group = {}
+    for gi, grp in enumerate(groups):
+        gg = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(gg, stream=stream):
+                for L, ts in enumerate(layers):
+                    src = inputs(buf["x"] if L == 0 else buf["down"])
+                    mul_mat_vec_group([ts[n] for n in grp], src[grp], outs=[buf[n] for n in grp], workspace=ws, stream=stream)
+            gg.replay()
+        torch.cuda.synchronize()
+        ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ea.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(reps):
+                gg.replay()
+        eb.record(stream)
+        torch.cuda.synchronize()
+        call_s = ea.elapsed_time(eb) / 1e3 / (reps * model["layers"])
+        nbytes = sum(algo_bytes_gemv(*dims[n]) for n in grp) - 4 * dims[grp[0]][1] * (len(grp) - 1)
+        per_group["+".join(grp)] = (call_s, nbytes)
+        del gg
     # ---- max over ranks
-    times = torch.tensor([t_dev, t_e2e, call_s], dtype=torch.float64, device=dev)
+    gnames = list(per_group)
+    times = torch.tensor([t_dev, t_e2e] + [per_group[g][0] for g in gnames], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    t_dev, t_e2e, call_s = times.tolist()
+    t_dev, t_e2e = times[0].item(), times[1].item()
+    for i, g in enumerate(gnames):
+        per_group[g] = (times[2 + i].item(), per_group[g][1])
     bytes_token = sum(algo_bytes_gemv(r, k) for _, r, k in shapes) * model["layers"]
     if rank != 0:
         return 0
     peak, peak_kind = measured_peaks()
-    achieved = bytes_total / call_s / 1e9
+    # dominant call type by device time per step
+    dom = max(gnames, key=lambda g: per_group[g][0])
+    dom_s, dom_bytes = per_group[dom]
+    achieved = dom_bytes / dom_s / 1e9
     tok_s = world * args.steps / t_dev
     line = {
         "metric": METRIC, "value": round(tok_s, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -288,9 +338,12 @@ def run_b200(args, rank, world, local_rank):
                    "batch": 1, "classes": "3", "parallelism": f"replicas{world}" if world > 1 else "single",
                    "weight_bytes_per_token": bytes_token, "l2": "inputs larger than L2 (1.80 GB of weights streamed per step)",
                    "hbm_gbs_step": round(bytes_token / (t_dev / args.steps) / 1e9, 1)},
-        "roofline": {"kernel": "p8_mul_mat_vec_group (k_act_prep + k_gemv)", "bound": "hbm", "achieved": round(achieved, 1),
-                     "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
-                     "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs", "calls": ncalls},
+        "roofline": {"kernel": f"p8_mul_mat_vec_group {dom} (k_act_prep + k_gemv)", "bound": "hbm", "achieved": round(achieved, 1),
+                     "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "traffic": TRAFFIC_BYTES.get(dom), "algorithmic_bytes": dom_bytes,
+                     "call_us": round(dom_s * 1e6, 3), "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs (burst copy)",
+                     "per_call_type": {g: {"us": round(per_group[g][0] * 1e6, 3),
+                                           "gbs": round(per_group[g][1] / per_group[g][0] / 1e9, 1)} for g in gnames}},
         "e2e": {"value": round(world * args.steps / t_e2e, 3), "unit": "tok/s", "h2d_bytes_per_step": 4 * h, "d2h_bytes_per_step": 4 * h},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),

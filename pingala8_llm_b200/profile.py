@@ -1,9 +1,12 @@
 """Run one grouped GEMV of a model shape repeatedly: a small, self-contained case for profilers (ncu) and timing.
 
-usage: python -m pingala8_llm_b200.profile [--group gate_up|qkv|o|down] [--iters N] [--copies C]
+usage: python -m pingala8_llm_b200.profile [--group gate_up|qkv|o|down] [--iters N] [--copies C] [--graph]
+                                            [--ncols N]
 
 Weights are seeded synthetic class-3 slots of the Llama-3.1-8B shapes. With --copies > 1 the calls rotate over
 distinct weight copies so repeated calls read DRAM rather than L2. Prints the mean time per call (CUDA events).
+--ncols N (N >= 8) runs the batched product (tcgen05 GEMM) of each tensor of the group on N tokens instead of the
+grouped batch-1 GEMV.
 """
 import argparse
 
@@ -26,8 +29,11 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--copies", type=int, default=1)
     ap.add_argument("--graph", action="store_true", help="capture the calls in a CUDA graph (no host launch overhead)")
+    ap.add_argument("--ncols", type=int, default=1, help="tokens per call; > 1 runs the batched product per tensor")
     a = ap.parse_args()
     shapes = GROUPS[a.group]
+    if a.ncols > 1:
+        return run_batched(a, shapes)
     copies = []
     for c in range(a.copies):
         copies.append([P8Tensor(synth.make_slot_device(r, k, seed=100 * c + i), k, r) for i, (r, k) in enumerate(shapes)])
@@ -60,6 +66,26 @@ def main():
     us = e0.elapsed_time(e1) * 1e3 / a.iters
     nbytes = sum((r // 32) * (k // 256) * (68 + 2048) for r, k in shapes)
     print(f"group {a.group}: {us:.2f} us/call, {nbytes / us / 1e3:.1f} GB/s (algorithmic, class 3)")
+
+
+def run_batched(a, shapes):
+    ts = [P8Tensor(synth.make_slot_device(r, k, seed=i), k, r) for i, (r, k) in enumerate(shapes)]
+    X = torch.randn(a.ncols, shapes[0][1], device="cuda")
+    outs = [torch.empty(a.ncols, r, device="cuda") for r, _ in shapes]
+    ws = [t.workspace(a.ncols) for t in ts]
+    for t, y, w in zip(ts, outs, ws):  # warm-up
+        t.mul_mat(X, out=y, workspace=w)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.iters):
+        for t, y, w in zip(ts, outs, ws):
+            t.mul_mat(X, out=y, workspace=w)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / a.iters
+    flop = sum(2.0 * r * k * a.ncols for r, k in shapes)
+    print(f"group {a.group} x {a.ncols} tokens: {us:.2f} us/call, {flop / us / 1e6:.1f} TFLOP/s")
 
 
 if __name__ == "__main__":
