@@ -1,0 +1,84 @@
+"""Tensor-parallel path on 2 GPUs (NCCL over NVLink): column- and row-parallel shards of real slots, run through the
+CUDA GEMV, gathered / all-reduced, against the oracle's full GEMV. Skips with fewer than 2 GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+    pytest.skip("needs 2 CUDA GPUs", allow_module_level=True)
+
+import torch.multiprocessing as mp  # noqa: E402
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank(rank, world, port, name, q):
+    import datetime
+    import sys
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        sys.path.insert(0, os.path.dirname(__file__))
+        from conftest import load_fixture
+
+        from pingala8_llm_b200 import tp
+        from pingala8_llm_b200.ops import device_error
+
+        f = load_fixture(name)
+        x = torch.from_numpy(f.x).cuda()
+        col = tp.ColumnParallel(f.slot, f.K, f.rows, world, rank, unit=32)
+        yc = col(x)
+        n = torch.tensor([yc.numel()], device="cuda")
+        ns = [torch.zeros_like(n) for _ in range(world)]
+        dist.all_gather(ns, n)
+        parts = [torch.zeros(int(v.item()), device="cuda") for v in ns]
+        dist.all_gather(parts, yc)
+        row = tp.RowParallel(f.slot, f.K, f.rows, world, rank)
+        yr = row(x[row.lo:row.hi].contiguous())
+        torch.cuda.synchronize()
+        q.put((rank, torch.cat(parts).cpu().numpy(), yr.cpu().numpy(), device_error()))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("name", ["c1_1024x2560_c3", "cls3_64x512"])
+def test_tp2_column_and_row_parallel(name):
+    import sys
+
+    sys.path.insert(0, os.path.dirname(__file__))
+    from conftest import load_fixture
+
+    f = load_fixture(name)
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_rank, args=(r, world, port, name, q)) for r in range(world)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(world)]
+    for p in ps:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    rel = lambda a: float(np.linalg.norm(a - f.y_ref) / np.linalg.norm(f.y_ref))
+    for rank, yc, yr, err in res:
+        assert err == 0
+        assert rel(yc) < 1e-5, (rank, rel(yc))
+        assert rel(yr) < 1e-5, (rank, rel(yr))
