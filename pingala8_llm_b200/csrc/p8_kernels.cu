@@ -267,13 +267,17 @@ __global__ void __launch_bounds__(256) k_act_prep(PrepArgs a) {
     const int b = blockIdx.x, fg = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
     pdl_launch_dependents();
     if (tid < 32) A_s[tid] = a.A[32 * fg + tid];
+    float4 i0 = make_float4(0.f, 0.f, 0.f, 0.f), i1 = i0;
+    if (tid < 32) {  // the column scales belong to the tensor, not to the previous kernel: loaded before the wait
+        const float *ic = a.ic + b * 256 + 8 * lane;
+        i0 = *reinterpret_cast<const float4 *>(ic);
+        i1 = *reinterpret_cast<const float4 *>(ic + 4);
+    }
     pdl_wait();  // x and the workspace belong to the previous kernel until it completes
     if (b == 0 && fg == 0 && tid == 0) *a.arrive = 0u;
     if (tid < 32) {
         const float *x = a.X + b * 256 + 8 * lane;
-        const float *ic = a.ic + b * 256 + 8 * lane;
         const float4 x0 = *reinterpret_cast<const float4 *>(x), x1 = *reinterpret_cast<const float4 *>(x + 4);
-        const float4 i0 = *reinterpret_cast<const float4 *>(ic), i1 = *reinterpret_cast<const float4 *>(ic + 4);
         float v[8] = {__fmul_rn(x0.x, i0.x), __fmul_rn(x0.y, i0.y), __fmul_rn(x0.z, i0.z), __fmul_rn(x0.w, i0.w),
                       __fmul_rn(x1.x, i1.x), __fmul_rn(x1.y, i1.y), __fmul_rn(x1.z, i1.z), __fmul_rn(x1.w, i1.w)};
         fwht256_warp(v, lane);
@@ -296,6 +300,8 @@ __global__ void __launch_bounds__(256) k_act_prep(PrepArgs a) {
             cx_s[tid] = cx;
         }
         __syncthreads();
+        // G[hs][grp][m] = sum over the set bits i of the nibble m of <c, q_t>, t = 4 grp + i. A 16-entry group table
+        // spans 16 banks, so the warp's lookups never conflict (equal m broadcast).
         const int hs = tid >> 7, grp = (tid >> 4) & 7, m = tid & 15;
         int gsum = 0;
 #pragma unroll
@@ -459,24 +465,30 @@ __device__ __forceinline__ int tensor_of(const GemvArgs &a, int rr) {
 // the warp's units of a CTA: per block b (segment), units rr = first + warp + 16 j of [rr_begin(b), rr_end(b)); a
 // unit is tile g = rr - g0 of tensor tensor_of(rr). Pure integer bookkeeping, no divisions.
 struct WarpCursor {
-    int b, rr;  // current unit; b > b_last: exhausted
+    int b, rr;  // current unit (256-column block, row tile of the group); exhausted once past the CTA's range
 };
 
 __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint64_t *bar = reinterpret_cast<uint64_t *>(g_smem + kSmemBar);
-    // contiguous, equal share of the block-major unit list
+    __shared__ unsigned int s_done[2];  // warps done with table buffer 0 / 1, counted over the kernel (monotonic)
+    __shared__ int s_issued;            // tables issued so far (segments 0 .. s_issued - 1)
+    __shared__ int s_ok;
+    // contiguous, equal share of the block-major unit list; warp w takes units u0 + w, u0 + w + W, ... in order, so
+    // the warps' shares differ by at most one unit and no warp waits for another at a block boundary
     const long long u0 = a.units * blockIdx.x / gridDim.x, u1 = a.units * (blockIdx.x + 1) / gridDim.x;
     const int b_first = (int)(u0 / a.ng_total), b_last = (int)((u1 - 1) / a.ng_total);
     const int rr_first = (int)(u0 - (long long)b_first * a.ng_total);             // first unit's rr in block b_first
     const int rr_last_end = (int)(u1 - (long long)b_last * a.ng_total);           // end rr in block b_last
-    auto rr_begin = [&](int b) { return b == b_first ? rr_first : 0; };
-    auto rr_end = [&](int b) { return b == b_last ? rr_last_end : a.ng_total; };
+    const int nseg = b_last - b_first + 1;
     pdl_launch_dependents();
     if (tid == 0) {
         mbar_init(bar, 1);
         mbar_init(bar + 1, 1);
         fence_mbar_init();
+        s_done[0] = 0u;
+        s_done[1] = 0u;
+        s_issued = 0;
     }
     uint32_t po[11];
 #pragma unroll
@@ -487,34 +499,36 @@ __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
             if (3 * q + i < 32) r |= (((uint32_t)(lane + 3 * q + i) & 31u) << 2) << (8 * i);
         po[q] = r;
     }
-    pdl_wait();  // tables and x come from the preceding prep kernel
-    __syncthreads();
-    auto issue_table = [&](int seg) {  // segment seg (block b_first + seg) -> buffer seg & 1
-        const int bb = b_first + seg, buf = seg & 1;
-        mbar_expect_tx(bar + buf, kTabBytes + 2 * kGInts * 4);
-        bulk_g2s(g_smem + (buf ? kSmemT1 : kSmemT0), a.T + (size_t)bb * kTabInts, kTabBytes, bar + buf);
-        bulk_g2s(g_smem + (buf ? kSmemG1 : kSmemG0), a.G + (size_t)2 * bb * kGInts, 2 * kGInts * 4, bar + buf);
-    };
-    if (tid == 0) {
-        issue_table(0);
-        if (b_last > b_first) issue_table(1);
+    // ---- reduce-phase split and the combining threads' row metadata (permutation, clamp-delta range): independent
+    // of the computation, loaded now so the dependent loads are off the tail of the kernel
+    const int r0 = (int)((long long)a.rows_total * blockIdx.x / gridDim.x), r1 = (int)((long long)a.rows_total * (blockIdx.x + 1) / gridDim.x);
+    const int n_rows = r1 - r0;
+    const int R = n_rows < kGemvThreads ? n_rows : kGemvThreads;
+    int S = R > 0 ? kGemvThreads / R : 1;
+    if (S > a.nb) S = a.nb;
+    const int rl = R > 0 ? tid % R : 0, sl = R > 0 ? tid / R : S;
+    int c_ti = 0, c_ro = 0, c_e0 = 0, c_e1 = 0;
+    if (tid < R) {
+        const int rt = r0 + tid;
+#pragma unroll
+        for (int i = 1; i < kMaxGroup; ++i)
+            if (i < a.ntensors && rt >= a.t[i].row0) c_ti = i;
+        const GemvTensor &T = a.t[c_ti];
+        c_ro = T.prm[rt - T.row0];
+        c_e0 = T.cp[c_ro];
+        c_e1 = T.cp[c_ro + 1];
     }
-    // cursor over this warp's units; the payload of the next unit is loaded while the current one computes
+    // ---- this warp's cursor (global order) and its first units' M words, payload and scale. The weights are not
+    // written by earlier kernels of the stream, so these loads are issued before the wait for the prep kernel.
+    auto in_range = [&](const WarpCursor &c) { return c.b < b_last || (c.b == b_last && c.rr < rr_last_end); };
     auto advance = [&](WarpCursor c) -> WarpCursor {
         c.rr += kGemvWarps;
-        while (c.b <= b_last && c.rr >= rr_end(c.b)) {
+        while (c.rr >= a.ng_total) {
+            c.rr -= a.ng_total;
             ++c.b;
-            c.rr = (c.b <= b_last ? rr_begin(c.b) : 0) + warp;
         }
         return c;
     };
-    // Three-deep cursor: the unit being computed, the next one (payload + scale in registers) and the one after
-    // (M word in a register). Every global load is issued one unit ahead of its first use.
-    WarpCursor nc = {b_first, rr_first + warp};
-    while (nc.b <= b_last && nc.rr >= rr_end(nc.b)) {
-        ++nc.b;
-        nc.rr = (nc.b <= b_last ? rr_begin(nc.b) : 0) + warp;
-    }
     auto m_of = [&](const WarpCursor &c) -> uint32_t {
         const int ti = tensor_of(a, c.rr);
         const uint32_t tile = (uint32_t)(c.rr - a.t[ti].g0) * (uint32_t)a.nb + (uint32_t)c.b;
@@ -530,118 +544,174 @@ __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
         if ((mt >> 29) == 3) load3(a.t[ti].D + (mt & 0x1FFFFFFFu), lane, nxt);
         s_n = __ldg(a.t[ti].S + (size_t)c.b * a.t[ti].rows + g * 32 + lane);
     };
+    WarpCursor nc = {b_first, rr_first + warp};
+    while (nc.rr >= a.ng_total) {
+        nc.rr -= a.ng_total;
+        ++nc.b;
+    }
     WarpCursor nc2 = nc;
-    if (nc.b <= b_last) {
+    if (in_range(nc)) {
         mt_n = m_of(nc);
         fetch(nc, mt_n);
         nc2 = advance(nc);
-        if (nc2.b <= b_last) mt_nn = m_of(nc2);
+        if (in_range(nc2)) mt_nn = m_of(nc2);
+    }
+    pdl_wait();  // tables and x come from the preceding prep kernel
+    __syncthreads();
+    auto issue_table = [&](int seg) {  // segment seg (block b_first + seg) -> buffer seg & 1
+        const int bb = b_first + seg, buf = seg & 1;
+        mbar_expect_tx(bar + buf, kTabBytes + 2 * kGInts * 4);
+        bulk_g2s(g_smem + (buf ? kSmemT1 : kSmemT0), a.T + (size_t)bb * kTabInts, kTabBytes, bar + buf);
+        bulk_g2s(g_smem + (buf ? kSmemG1 : kSmemG0), a.G + (size_t)2 * bb * kGInts, 2 * kGInts * 4, bar + buf);
+    };
+    if (tid == 0) {
+        issue_table(0);
+        if (nseg > 1) issue_table(1);
+        s_issued = nseg > 1 ? 2 : 1;
     }
     bool ok = true;
-    int seg = 0;
-    for (; b_first + seg <= b_last; ++seg) {
-        const int b = b_first + seg;
-        if (!mbar_wait_bounded(bar + (seg & 1), (uint32_t)((seg >> 1) & 1), kWaitPolls)) {
+    int waited = -1;    // the last segment whose table this warp has waited for
+    int signaled = 0;   // this warp is done with segments [0, signaled)
+    auto wait_table = [&](int sg) {
+        if (waited >= sg || !ok) return;
+        // warp-uniform outcome (every lane polls; a lane that gave up makes the whole warp take the error path)
+        const bool landed = __all_sync(0xffffffffu, mbar_wait_bounded(bar + (sg & 1), (uint32_t)((sg >> 1) & 1), kWaitPolls));
+        if (!landed) {
             if (lane == 0) atomicOr(&g_p8_device_error, 1u);
             ok = false;
-            break;
         }
-        const float d0 = a.d[2 * b], d1 = a.d[2 * b + 1];
-        while (nc.b == b) {
-            const int rr = nc.rr;
-            const uint32_t mt = mt_n;
-            const uint16_t sc = s_n;
-            uint32_t cur[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) cur[i] = nxt[i];
-            nc = nc2;
-            mt_n = mt_nn;
-            if (nc.b <= b_last) {
-                fetch(nc, mt_n);  // possibly in the next segment
-                nc2 = advance(nc);
-                if (nc2.b <= b_last) mt_nn = m_of(nc2);
-            }
-            const int ti = tensor_of(a, rr), g = rr - a.t[ti].g0;
-            const GemvTensor &T = a.t[ti];
-            const int c = (int)(mt >> 29);
-            float part;
-            if (c == 3) {
-                uint32_t w0[24], w1[24];
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    w0[2 * i] = cur[2 * i]; w0[2 * i + 1] = cur[2 * i + 1];
-                    w1[2 * i] = cur[8 + 2 * i]; w1[2 * i + 1] = cur[8 + 2 * i + 1];
+        waited = sg;
+    };
+    // Done with segments [signaled, end): a warp signals a segment only after its table arrived, so a buffer's count
+    // grows segment by segment; the warp that completes a segment's count refills its buffer with segment + 2.
+    auto signal_through = [&](int end) {
+        for (; signaled < end; ++signaled) {
+            const int sg = signaled;
+            wait_table(sg);
+            __syncwarp();
+            if (lane == 0) {
+                __threadfence_block();  // this warp's table reads are ordered before its count
+                const unsigned int old = atomicAdd(&s_done[sg & 1], 1u);
+                if (old + 1u == (unsigned int)((sg >> 1) + 1) * kGemvWarps && sg + 2 < nseg && ok) {
+                    __threadfence_block();
+                    fence_proxy_async();  // every warp's generic-proxy reads of the buffer before the bulk copy
+                    issue_table(sg + 2);
+                    atomicMax(&s_issued, sg + 3);
                 }
-#pragma unroll
-                for (int i = 8; i < 24; ++i) { w0[i] = 0; w1[i] = 0; }
-                part = (seg & 1) ? tile_row_dot_w<3, 1>(w0, w1, po, lane, d0, d1) : tile_row_dot_w<3, 0>(w0, w1, po, lane, d0, d1);
-            } else {
-                const uint32_t *p0 = T.D + (mt & 0x1FFFFFFFu);
-                part = (seg & 1) ? tile_row_other<1>(c, p0, po, lane, d0, d1) : tile_row_other<0>(c, p0, po, lane, d0, d1);
             }
-            const int r = g * 32 + lane;
-            T.part[(size_t)b * T.rows + r] = __fmul_rn(part, h2f(sc));
+            __syncwarp();
         }
-        __syncthreads();  // every warp is done with this segment's buffer
-        if (tid == 0 && b_first + seg + 2 <= b_last) {
-            fence_proxy_async();  // the buffer's generic-proxy reads are ordered before the bulk copy overwrites it
-            issue_table(seg + 2);
+    };
+    while (ok && in_range(nc)) {
+        const int seg = nc.b - b_first;
+        signal_through(seg);
+        wait_table(seg);
+        if (!ok) break;
+        const int b = nc.b, rr = nc.rr;
+        const float d0 = a.d[2 * b], d1 = a.d[2 * b + 1];
+        const uint32_t mt = mt_n;
+        const uint16_t sc = s_n;
+        uint32_t cur[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) cur[i] = nxt[i];
+        nc = nc2;
+        mt_n = mt_nn;
+        if (in_range(nc)) {
+            fetch(nc, mt_n);  // possibly in the next segment
+            nc2 = advance(nc);
+            if (in_range(nc2)) mt_nn = m_of(nc2);
         }
+        const int ti = tensor_of(a, rr), g = rr - a.t[ti].g0;
+        const GemvTensor &T = a.t[ti];
+        const int c = (int)(mt >> 29);
+        float part;
+        if (c == 3) {
+            uint32_t w0[24], w1[24];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                w0[2 * i] = cur[2 * i]; w0[2 * i + 1] = cur[2 * i + 1];
+                w1[2 * i] = cur[8 + 2 * i]; w1[2 * i + 1] = cur[8 + 2 * i + 1];
+            }
+#pragma unroll
+            for (int i = 8; i < 24; ++i) { w0[i] = 0; w1[i] = 0; }
+            part = (seg & 1) ? tile_row_dot_w<3, 1>(w0, w1, po, lane, d0, d1) : tile_row_dot_w<3, 0>(w0, w1, po, lane, d0, d1);
+        } else {
+            const uint32_t *p0 = T.D + (mt & 0x1FFFFFFFu);
+            part = (seg & 1) ? tile_row_other<1>(c, p0, po, lane, d0, d1) : tile_row_other<0>(c, p0, po, lane, d0, d1);
+        }
+        const int r = g * 32 + lane;
+        T.part[(size_t)b * T.rows + r] = __fmul_rn(part, h2f(sc));
     }
-    if (!ok && tid == 0) {  // copies in flight must land before the CTA's shared memory goes away
-        for (int s2 = seg; s2 <= seg + 1 && b_first + s2 <= b_last; ++s2)
-            mbar_wait_bounded(bar + (s2 & 1), (uint32_t)((s2 >> 1) & 1), kWaitPolls);
+    if (ok) signal_through(nseg);
+    __syncthreads();
+    if (!ok && tid == 0) {  // copies in flight must land before the CTA's shared memory is reused or goes away
+        for (int sg = s_issued - 2; sg < s_issued; ++sg)
+            if (sg >= 0) mbar_wait_bounded(bar + (sg & 1), (uint32_t)((sg >> 1) & 1), kWaitPolls);
     }
     // grid barrier (all CTAs are resident: one per SM; the prep kernel zeroed the counter), then every CTA reduces an
     // equal share of the rows: y[prm[r]] = sum_b part[b][r] (block order, deterministic) + sum_e val_e x[col_e]
-    __shared__ int s_ok;
     __syncthreads();
     if (tid == 0) {
         unsigned int n;  // release: this CTA's partial stores are visible before its arrival is counted
         asm volatile("atom.add.release.gpu.global.u32 %0, [%1], 1;" : "=r"(n) : "l"(a.arrive) : "memory");
         ++n;
         for (int spins = 0; n < gridDim.x && spins < (1 << 26); ++spins)
-            asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(n) : "l"(a.arrive) : "memory");
+            asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(n) : "l"(a.arrive) : "memory");
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");  // acquire: the other CTAs' partials are visible
         s_ok = n >= gridDim.x;
         if (!s_ok) atomicOr(&g_p8_device_error, 2u);
     }
     __syncthreads();
     if (!s_ok) return;
-    // 128 rows x 4 block slices per pass: each slice sums its blocks in order with four loads in flight, slice 0
-    // then adds the four slice sums in order
-    constexpr int kRedRows = 128, kRedSlices = kGemvThreads / kRedRows;
+    // R rows x S block slices per pass (R * S <= threads): slice j sums blocks [nb j / S, nb (j + 1) / S) of its row
+    // in block order with all of its loads in flight, then the first R threads add the S slice sums in slice order.
+    // The split depends only on the launch shape, so the result is deterministic.
     float *red = reinterpret_cast<float *>(g_smem + kSmemT0);  // the table buffers are free now
-    const int r0 = (int)((long long)a.rows_total * blockIdx.x / gridDim.x), r1 = (int)((long long)a.rows_total * (blockIdx.x + 1) / gridDim.x);
-    const int rl = tid % kRedRows, sl = tid / kRedRows;
-    const int b_lo = a.nb * sl / kRedSlices, b_hi = a.nb * (sl + 1) / kRedSlices;
-    for (int base = r0; base < r1; base += kRedRows) {
+    const int b_lo = a.nb * sl / S, b_hi = a.nb * (sl + 1) / S;
+    for (int base = r0; base < r1; base += R) {
         const int rt = base + rl;
-        int ti = 0;
         float s = 0.f;
-        if (rt < r1) {
+        if (sl < S && rt < r1) {
+            int ti = 0;
 #pragma unroll
             for (int i = 1; i < kMaxGroup; ++i)
                 if (i < a.ntensors && rt >= a.t[i].row0) ti = i;
             const GemvTensor &T = a.t[ti];
             const float *p = T.part + (rt - T.row0);
             int bb = b_lo;
-            for (; bb + 4 <= b_hi; bb += 4) {
-                const float p0 = __ldcg(p + (size_t)bb * T.rows), p1 = __ldcg(p + (size_t)(bb + 1) * T.rows);
-                const float p2 = __ldcg(p + (size_t)(bb + 2) * T.rows), p3 = __ldcg(p + (size_t)(bb + 3) * T.rows);
-                s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, p0), p1), p2), p3);
-            }
-            for (; bb < b_hi; ++bb) s = __fadd_rn(s, __ldcg(p + (size_t)bb * T.rows));
-        }
-        red[sl * kRedRows + rl] = s;
-        __syncthreads();
-        if (sl == 0 && rt < r1) {
-            float y = red[rl];
+            for (; bb + 8 <= b_hi; bb += 8) {
+                float v[8];
 #pragma unroll
-            for (int j = 1; j < kRedSlices; ++j) y = __fadd_rn(y, red[j * kRedRows + rl]);
-            const GemvTensor &T = a.t[ti];
-            const int ro = T.prm[rt - T.row0];
-            for (int e = T.cp[ro]; e < T.cp[ro + 1]; ++e) y = __fadd_rn(y, __fmul_rn(T.cv[e], a.X[T.cc[e]]));
-            T.Y[ro] = y;
+                for (int j = 0; j < 8; ++j) v[j] = __ldcg(p + (size_t)(bb + j) * T.rows);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) s = __fadd_rn(s, v[j]);
+            }
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = bb + j < b_hi ? __ldcg(p + (size_t)(bb + j) * T.rows) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (bb + j < b_hi) s = __fadd_rn(s, v[j]);
+        }
+        if (sl < S) red[sl * R + rl] = s;
+        __syncthreads();
+        if (tid < R && base + tid < r1) {
+            float y = red[tid];
+            for (int j = 1; j < S; ++j) y = __fadd_rn(y, red[j * R + tid]);
+            const int rt2 = base + tid;
+            if (base != r0) {  // rows past the first pass: metadata loaded here
+                c_ti = 0;
+#pragma unroll
+                for (int i = 1; i < kMaxGroup; ++i)
+                    if (i < a.ntensors && rt2 >= a.t[i].row0) c_ti = i;
+                const GemvTensor &T = a.t[c_ti];
+                c_ro = T.prm[rt2 - T.row0];
+                c_e0 = T.cp[c_ro];
+                c_e1 = T.cp[c_ro + 1];
+            }
+            const GemvTensor &T = a.t[c_ti];
+            for (int e = c_e0; e < c_e1; ++e) y = __fadd_rn(y, __fmul_rn(T.cv[e], a.X[T.cc[e]]));
+            T.Y[c_ro] = y;
         }
         __syncthreads();
     }
