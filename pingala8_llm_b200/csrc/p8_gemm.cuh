@@ -1,6 +1,6 @@
-// p8_gemm.cuh -- batched (prefill) Pingala-8 matmul on the 5th-generation tensor cores: tcgen05 MMA with the
-// accumulator in tensor memory (TMEM), operands in shared memory written by decoder warps (weights) and by bulk copies
-// (activations). Included by p8_kernels.cu, so it shares that file's device error word and launch helpers.
+// p8_gemm.cuh -- batched (prefill) Pingala-8 matmul on the 5th-generation tensor cores: tcgen05 MMA with the weight
+// operand and the accumulator in tensor memory (TMEM), the activation operand in shared memory. Included by
+// p8_kernels.cu, so it shares that file's device error word and launch helpers.
 //
 // The reference batch path (ggml_cuda_f44_mul_mat_q8, CU:1014-1054; the CPU batch path CP:1201-1262) computes
 //     Y[n][ro] = sum_k W[ro][k] X[n][k],   W = H256(int * S) / 16 * (sgn / c) + Delta        (vrc_dequant_f32)
@@ -20,27 +20,35 @@
 //   k_gx_prep  grid (Npad/8, nb/4 rounded up), 256 thr, warp = token: tau from the partial maxima; Xr as fp16 in the
 //              operand layout below ([half-slice][token group of 8][16 core matrices][8 tokens][8 columns]), so the
 //              GEMM moves one B stage with one bulk copy.
-//   k_gemm     grid (rows/128 rounded up, Npad/BN), 320 thr, 1 CTA per SM:
+//   k_gemm     grid (rows/128 rounded up, Npad/BN), 352 thr, 1 CTA per SM. One stage = one 128-column half-slice.
+//              warp 8     stages the packed payload: per stage, one bulk copy per row tile (NW words x 32 lanes of its
+//                         half-slice) into a ring of up to 8 shared-memory slots, several stages ahead of the decoders;
 //              warps 0-7  decoders: warp (q, hs) decodes half-slice hs of row tile q (32 rows) of every 256-column
-//                         block into the A stage as fp16 int * S * 2^sigma; then the epilogue (TMEM -> registers,
+//                         block from the staged words into a TMEM A slot (4 slots, 64 columns each) as fp16
+//                         int * S * 2^sigma with tcgen05.st (lane = row); then the epilogue (TMEM -> registers,
 //                         scales, clamp delta, y[n][prm[r]]);
-//              warp 8     one lane bulk-copies each B stage (BN tokens x 128 columns) onto the stage's mbarrier;
-//              warp 9     allocates TMEM; one lane issues 8 MMAs (M = 128, N = BN, K = 16) per stage and commits them to
-//                         the stage's 'empty' barrier, and after the last stage to the accumulator barrier.
-// One stage = one 128-column half-slice: A 128 x 128 fp16 (32 KB), B BN x 128 fp16. Shared-memory operand layout,
-// both operands (UMMA K-major, no swizzle): a core matrix is 8 rows x 8 fp16, 16 B per row, 128 B contiguous;
+//              warp 10    bulk-copies each B stage (BN tokens x 128 columns) into a shared-memory ring;
+//              warp 9     allocates TMEM; one lane issues 8 MMAs (M = 128, N = BN, K = 16, A from TMEM) per stage and
+//                         commits them to the stage's A-slot and B-slot 'empty' barriers, after the last stage to the
+//                         accumulator barrier.
+// The loader and MMA warps run their loops as whole warps (every lane polls, one or four lanes issue): a single active
+// lane with 31 parked at a warp barrier was starved behind the decoders' shared-memory traffic.
+// Keeping A in TMEM leaves shared-memory bandwidth to the B tile (written once by the copy, read once by the MMA). The
+// codebook lookup table is a lane-private copy (entry f of lane l at word 32 f + l), so a warp's lookups never share a
+// bank. B operand layout (UMMA K-major, no swizzle): a core matrix is 8 rows x 8 fp16, 16 B per row, 128 B contiguous;
 //     byte(row, col) = (row >> 3) * 2048 + (col >> 3) * 128 + (row & 7) * 16 + (col & 7) * 2
-// so descriptor LBO (next core matrix along K) = 128 B and SBO (next group of 8 rows) = 2048 B. A decoder lane owns
-// one row and writes 16 B (two 4-column chunks) per store; eight lanes cover the 32 banks, so stores are conflict-free.
+// so descriptor LBO (next core matrix along K) = 128 B and SBO (next group of 8 rows) = 2048 B.
 //
 // Every mbarrier wait is bounded; a wait that gives up sets bit 2 (value 4) of the device error word, the kernel
-// still drains its own copies and MMAs, frees its TMEM and returns (results of that launch are invalid).
+// drains its own copies and MMAs, frees its TMEM and returns (results of that launch are invalid).
 
-constexpr int kGemmThreads = 320;
-constexpr int kGemmStageA = 32768;                  // 128 rows x 128 columns fp16
-constexpr int kGemmOperandBudget = 196608;          // bytes of shared memory for the stage ring
-constexpr int kGemmMaxStages = 8;
-constexpr int kGemmAH = 512 * 8;                    // fp16 (codebook + h * coset) table for the one-stage classes
+constexpr int kGemmThreads = 352;                   // 8 decoder warps, payload loader, MMA, activation loader
+constexpr int kGemmCbk = 256 * 32 * 4;              // lane-private codebook copy (32 KB)
+constexpr int kGemmASlots = 4;                      // A operand stages in TMEM, 64 columns each
+constexpr int kGemmAColBase = 256;                  // TMEM columns [0, 256): accumulator; [256, 512): A stages
+constexpr uint32_t kGemmTmemCols = 512;
+constexpr int kGemmMaxB = 4, kGemmMaxP = 8;         // activation / payload ring depths
+constexpr int kGemmSmemMax = 227 * 1024;            // dynamic shared memory per CTA (sm_100 opt-in maximum)
 constexpr uint32_t kGemmPolls = 1u << 22;
 constexpr int kGemmMinCols = 8;                     // below this the per-column table GEMV is faster
 
@@ -58,7 +66,7 @@ struct GemmArgs {
     const float *tdown;    // per token 2^-tau
     long long ldx, ldy;
     uint32_t cs;
-    int rows, nb, ng, ncols, npad, bn, nst, ucls;
+    int rows, nb, ng, ncols, npad, bn, nbs, np, tileb, ucls;
 };
 
 struct GxArgs {
@@ -82,14 +90,6 @@ __device__ __forceinline__ void tmem_alloc(uint32_t *slot_smem, uint32_t ncols) 
 }
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-// D[tmem] (+)= A[smem] * B[smem]^T, both K-major; accumulate = 0 overwrites D
-__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accumulate) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem_d),
-        "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
-        : "memory");
 }
 // arrive on the mbarrier once every MMA this thread issued so far has completed
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
@@ -203,229 +203,346 @@ __global__ void __launch_bounds__(256) k_gx_prep(const GxArgs a) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// decoders: one lane = one row of a 32-row tile, one 128-column half-slice, written as fp16 into the A stage row
-// (arow = stage + row offset; chunk t = columns 4t..4t+3 lands at (t >> 1) * 128 + (t & 1) * 8).
+// decoders: one lane = one row of a 32-row tile, one 128-column half-slice, written as fp16 into the TMEM A slot of
+// the stage (row = TMEM lane, column c of the slot holds columns 2c, 2c + 1 of the half-slice as a half2).
+//
+// Chunk order: the payload stores chunk t of lane j at step k = (t - j) & 31, i.e. every field stream of the lane is
+// rotated by j fields. Reading the lane's words from shared memory with the word rotation applied at load time and
+// the bit rotation by a funnel shift puts chunk t's fields at static bit positions t * width, so each class decodes
+// straight into registers in chunk order, eight chunks (16 columns) per tcgen05.st.
 
-// One-stage class 3 (W1 = 8): the lane's 8 words are loaded with the byte stream rotated by j words' worth at load
-// time (word i <- stored word (i - j/4) & 7); the remaining j & 3 bytes are rotated in registers, after which byte t is
-// the field of chunk t (stored at step k = (t - j) & 31).
-__device__ __forceinline__ void load_c3_rotated(const uint32_t *p0, int hs, int j, uint32_t (&w)[24]) {
-    const uint32_t *q = p0 + (size_t)hs * 8 * 32 + 2 * j;
-    const int a = j >> 2;
+// lane words of one half-slice in the staging slot: word i of lane j at pw[(i >> 1) * 64 + 2 j + (i & 1)]
+__device__ __forceinline__ uint32_t slot_word(const uint32_t *pw, int lane, int i) { return pw[(i >> 1) * 64 + 2 * lane + (i & 1)]; }
+
+// the W-word stream at words [wbase, wbase + W) rotated left by rbits (< 32 W) bits: out bit p = stream bit p - rbits
+template <int W>
+__device__ __forceinline__ void rot_stream(const uint32_t *pw, int wbase, int lane, int rbits, uint32_t (&out)[W]) {
+    const int qw = rbits >> 5, o = rbits & 31;
+    uint32_t r[W];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int s = (i - a) & 7;
-        w[i] = __ldg(q + (s >> 1) * 64 + (s & 1));
+    for (int i = 0; i < W; ++i) {
+        int s = i - qw;
+        if (s < 0) s += W;
+        r[i] = slot_word(pw, lane, wbase + s);
     }
+#pragma unroll
+    for (int i = 0; i < W; ++i) out[i] = __funnelshift_l(r[(i + W - 1) % W], r[i], o);
 }
 
-__device__ __forceinline__ void decode_c3(const uint32_t (&w)[24], int j, const uint2 *AH, float sc, uint8_t *arow) {
+// width-bit field at static bit position pos of a word array
+template <int N>
+__device__ __forceinline__ uint32_t sfield(const uint32_t (&w)[N], int pos, int width) {
+    const int wi = pos >> 5, bb = pos & 31;
+    uint32_t v = w[wi] >> bb;
+    if (bb + width > 32) v |= w[wi + 1] << (32 - bb);
+    return v & ((1u << width) - 1u);
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16};\n" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// D[tmem] (+)= A[tmem] * B[smem]^T, B K-major; accumulate = 0 overwrites D
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(db), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+
+constexpr uint32_t kHalf2M1152 = 0xE480E480u;  // half2(-1152, -1152)
+
+// Class 3 (one 8-bit stage). The codebook copy holds A[f] ^ 0x80808080 (bytes a + 128). PRMT places two bytes u under
+// the fp16 exponent pattern 0x64 (giving 1024 + u exactly); adding -1152 (h = 0) or c_e - 1152 (h = 1) gives the exact
+// integer a + h c, and one multiply by the row scale rounds it to fp16 once.
+__device__ __forceinline__ void decode_c3_tmem(const uint32_t *pw, int lane, const uint32_t *cl, float sc, uint32_t dlo,
+                                               uint32_t dhi, uint32_t tA) {
     uint32_t rw[8];
-    const int sh = 8 * (j & 3);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) rw[i] = __funnelshift_l(w[(i + 7) & 7], w[i], sh);
+    rot_stream<8>(pw, 0, lane, 8 * lane, rw);
     const uint32_t H = pingala8_h(zbits<3>(rw));
     const __half2 s2 = __float2half2_rn(sc);
 #pragma unroll
-    for (int p = 0; p < 16; ++p) {
-        uint2 e[2];
+    for (int gq = 0; gq < 4; ++gq) {
+        uint32_t o[16];
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-            const int t = 2 * p + u;
+        for (int u = 0; u < 8; ++u) {
+            const int t = 8 * gq + u;
             const uint32_t f = (rw[t >> 2] >> (8 * (t & 3))) & 0xFFu;
-            e[u] = AH[(f << 1) | ((H >> t) & 1u)];
+            const uint32_t v = cl[f * 32];
+            const uint32_t hm = (uint32_t)((int32_t)(H << (31 - t)) >> 31);
+            const uint32_t lo = __byte_perm(v, 0x64646464u, 0x5140), hi = __byte_perm(v, 0x64646464u, 0x7362);
+            o[2 * u] = h2u(__hmul2(__hadd2(u2h(lo), u2h((hm & dlo) ^ kHalf2M1152)), s2));
+            o[2 * u + 1] = h2u(__hmul2(__hadd2(u2h(hi), u2h((hm & dhi) ^ kHalf2M1152)), s2));
         }
-        uint4 o;
-        o.x = h2u(__hmul2(u2h(e[0].x), s2));
-        o.y = h2u(__hmul2(u2h(e[0].y), s2));
-        o.z = h2u(__hmul2(u2h(e[1].x), s2));
-        o.w = h2u(__hmul2(u2h(e[1].y), s2));
-        *reinterpret_cast<uint4 *>(arow + p * 128) = o;
+        tmem_st16(tA + 16 * gq, o);
     }
 }
 
-// any class: exact integers per step (chunk_ints_step), then fp16(int * sc)
+// any class: exact integers sum_s (A[f_s] + h c) << SH_s per element, then fp16(int * sc)
 template <int C>
-__device__ __forceinline__ void decode_generic(const uint32_t (&w)[24], int j, const uint32_t *A_s, uint32_t cs, float sc,
-                                               uint8_t *arow) {
-    const uint32_t z = zbits<C>(w);
-    const uint32_t H = pingala8_h(__funnelshift_l(z, z, j));
+__device__ __forceinline__ void decode_gen_tmem(const uint32_t *pw, int lane, const uint32_t *cl, uint32_t cs, float sc,
+                                                uint32_t tA) {
+    constexpr int w1 = W1(C), w2 = W2(C), w3 = W3(C);
+    constexpr int n1 = w1 == 8 ? 8 : w1 - 1;
+    uint32_t s1[n1], s2[w2 > 0 ? w2 : 1], s3[8], z;
+    if constexpr (w1 == 8) {
+        rot_stream<8>(pw, 0, lane, 8 * lane, s1);
+        z = zbits<3>(s1);
+    } else {
+        uint32_t m0[1];
+        rot_stream<1>(pw, 0, lane, lane, m0);  // stage-1 MSB word: bit k = z of step k
+        z = m0[0];
+        rot_stream<n1>(pw, 1, lane, n1 * lane, s1);
+    }
+    if constexpr (w2 > 0) rot_stream<(w2 > 0 ? w2 : 1)>(pw, w1, lane, w2 * lane, s2);
+    if constexpr (w3 > 0) rot_stream<8>(pw, w1 + w2, lane, 8 * lane, s3);
+    const uint32_t H = pingala8_h(z);
 #pragma unroll
-    for (int k = 0; k < 32; ++k) {
-        const int t = (j + k) & 31;
-        int v[4];
-        chunk_ints_step<C>(w, A_s, cs, H, k, t, v);
-        uint2 o;
-        o.x = h2u(__floats2half2_rn(__fmul_rn((float)v[0], sc), __fmul_rn((float)v[1], sc)));
-        o.y = h2u(__floats2half2_rn(__fmul_rn((float)v[2], sc), __fmul_rn((float)v[3], sc)));
-        *reinterpret_cast<uint2 *>(arow + (t >> 1) * 128 + (t & 1) * 8) = o;
+    for (int gq = 0; gq < 4; ++gq) {
+        uint32_t o[16];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int t = 8 * gq + u;
+            uint32_t f1;
+            if constexpr (w1 == 8) f1 = (s1[t >> 2] >> (8 * (t & 3))) & 0xFFu;
+            else f1 = sfield(s1, (w1 - 1) * t, w1 - 1) | (((z >> t) & 1u) << (w1 - 1));
+            const uint32_t a1 = cl[f1 * 32] ^ 0x80808080u;
+            uint32_t a2 = 0, a3 = 0;
+            if constexpr (w2 > 0) a2 = cl[sfield(s2, w2 * t, w2) * 32] ^ 0x80808080u;
+            if constexpr (w3 > 0) a3 = cl[((s3[t >> 2] >> (8 * (t & 3))) & 0xFFu) * 32] ^ 0x80808080u;
+            const int h = (H >> t) & 1u;
+            float v[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int ce = h ? (int)(int8_t)(cs >> (8 * e)) : 0;
+                int x = ((int)(int8_t)(a1 >> (8 * e)) + ce) * (1 << SH1(C));
+                if (w2 > 0) x += ((int)(int8_t)(a2 >> (8 * e)) + ce) * (1 << SH2(C));
+                if (w3 > 0) x += (int)(int8_t)(a3 >> (8 * e)) + ce;
+                v[e] = __fmul_rn((float)x, sc);
+            }
+            o[2 * u] = h2u(__floats2half2_rn(v[0], v[1]));
+            o[2 * u + 1] = h2u(__floats2half2_rn(v[2], v[3]));
+        }
+        tmem_st16(tA + 16 * gq, o);
     }
 }
 
-__device__ __forceinline__ void load_tile_words(int c, const uint32_t *p0, int hs, int j, uint32_t (&w)[24]) {
+__device__ __forceinline__ void decode_tile_tmem(int c, const uint32_t *pw, int lane, const uint32_t *cl, uint32_t cs, float sc,
+                                                 uint32_t dlo, uint32_t dhi, uint32_t tA) {
     switch (c) {
-        case 0: break;
-        case 1: load_lane_words<1>(p0, hs, j, w); break;
-        case 2: load_lane_words<2>(p0, hs, j, w); break;
-        case 3: load_c3_rotated(p0, hs, j, w); break;
-        case 4: load_lane_words<4>(p0, hs, j, w); break;
-        case 5: load_lane_words<5>(p0, hs, j, w); break;
-        case 6: load_lane_words<6>(p0, hs, j, w); break;
-        default: load_lane_words<7>(p0, hs, j, w); break;
-    }
-}
-
-__device__ __forceinline__ void decode_tile(int c, const uint32_t (&w)[24], int j, const uint2 *AH, const uint32_t *A_s,
-                                            uint32_t cs, float sc, uint8_t *arow) {
-    switch (c) {
-        case 0:
+        case 0: {
+            uint32_t o[16];
 #pragma unroll
-            for (int p = 0; p < 16; ++p) *reinterpret_cast<uint4 *>(arow + p * 128) = make_uint4(0u, 0u, 0u, 0u);
+            for (int i = 0; i < 16; ++i) o[i] = 0u;
+#pragma unroll
+            for (int gq = 0; gq < 4; ++gq) tmem_st16(tA + 16 * gq, o);
             break;
-        case 1: decode_generic<1>(w, j, A_s, cs, sc, arow); break;
-        case 2: decode_generic<2>(w, j, A_s, cs, sc, arow); break;
-        case 3: decode_c3(w, j, AH, sc, arow); break;
-        case 4: decode_generic<4>(w, j, A_s, cs, sc, arow); break;
-        case 5: decode_generic<5>(w, j, A_s, cs, sc, arow); break;
-        case 6: decode_generic<6>(w, j, A_s, cs, sc, arow); break;
-        default: decode_generic<7>(w, j, A_s, cs, sc, arow); break;
+        }
+        case 1: decode_gen_tmem<1>(pw, lane, cl, cs, sc, tA); break;
+        case 2: decode_gen_tmem<2>(pw, lane, cl, cs, sc, tA); break;
+        case 3: decode_c3_tmem(pw, lane, cl, sc, dlo, dhi, tA); break;
+        case 4: decode_gen_tmem<4>(pw, lane, cl, cs, sc, tA); break;
+        case 5: decode_gen_tmem<5>(pw, lane, cl, cs, sc, tA); break;
+        case 6: decode_gen_tmem<6>(pw, lane, cl, cs, sc, tA); break;
+        default: decode_gen_tmem<7>(pw, lane, cl, cs, sc, tA); break;
     }
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// shared-memory layout of k_gemm (bytes from the dynamic base), shared by host and device
+struct GemmSmem {
+    int cbk, B, P, Mw, bars, tslot, total;
+};
+__host__ __device__ inline GemmSmem gemm_smem_layout(int bn, int nbs, int np, int tileb, int nb) {
+    GemmSmem L;
+    L.cbk = 0;
+    L.B = kGemmCbk;
+    L.P = L.B + nbs * bn * 256;
+    L.Mw = L.P + np * 4 * tileb;
+    L.bars = L.Mw + 16 * nb;  // 4 tiles x nb words
+    L.tslot = L.bars + 8 * (2 * kGemmMaxP + 2 * kGemmMaxB + 2 * kGemmASlots + 1);
+    L.total = L.tslot + 16;
+    return L;
+}
+
 __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant__ GemmArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nst = a.nst, bn = a.bn;
-    const int stageB = bn * 256;
-    uint8_t *sA = g_smem;
-    uint8_t *sB = g_smem + (size_t)nst * kGemmStageA;
-    uint2 *AH = reinterpret_cast<uint2 *>(sB + (size_t)nst * stageB);
-    uint32_t *A_s = reinterpret_cast<uint32_t *>(reinterpret_cast<uint8_t *>(AH) + kGemmAH);
-    uint64_t *full_a = reinterpret_cast<uint64_t *>(A_s + 256);
-    uint64_t *full_b = full_a + kGemmMaxStages;
-    uint64_t *empty = full_b + kGemmMaxStages;
-    uint64_t *acc_bar = empty + kGemmMaxStages;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_bar + 1);
-    const uint32_t tcols = bn < 32 ? 32u : (uint32_t)bn;
+    const int bn = a.bn, nbs = a.nbs, np = a.np;
+    const int stageB = bn * 256, stageP = 4 * a.tileb;
+    const GemmSmem L = gemm_smem_layout(bn, nbs, np, a.tileb, a.nb);
+    uint32_t *cbk = reinterpret_cast<uint32_t *>(g_smem + L.cbk);
+    uint8_t *sB = g_smem + L.B;
+    uint8_t *sP = g_smem + L.P;
+    uint32_t *sM = reinterpret_cast<uint32_t *>(g_smem + L.Mw);
+    uint64_t *p_full = reinterpret_cast<uint64_t *>(g_smem + L.bars);
+    uint64_t *p_empty = p_full + kGemmMaxP, *b_full = p_empty + kGemmMaxP, *b_empty = b_full + kGemmMaxB;
+    uint64_t *a_full = b_empty + kGemmMaxB, *a_empty = a_full + kGemmASlots, *acc_bar = a_empty + kGemmASlots;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(g_smem + L.tslot);
     const int nhs = 2 * a.nb;  // stages = half-slices
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < nst; ++i) {
-            mbar_init(full_a + i, 4);  // the four decoder warps of the stage's half-slice
-            mbar_init(full_b + i, 1);
-            mbar_init(empty + i, 1);   // tcgen05.commit
+        for (int i = 0; i < np; ++i) {
+            mbar_init(p_full + i, 1);   // payload bytes arrived (expect_tx arrive)
+            mbar_init(p_empty + i, 4);  // the four decoder warps of the stage have read the slot
+        }
+        for (int i = 0; i < nbs; ++i) {
+            mbar_init(b_full + i, 1);
+            mbar_init(b_empty + i, 1);  // tcgen05.commit
+        }
+        for (int i = 0; i < kGemmASlots; ++i) {
+            mbar_init(a_full + i, 4);
+            mbar_init(a_empty + i, 1);
         }
         mbar_init(acc_bar, 1);
         fence_mbar_init();
     }
-    if (warp == 9) tmem_alloc(tmem_slot, tcols);
+    if (warp == 9) tmem_alloc(tmem_slot, kGemmTmemCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     pdl_wait();  // everything below may read memory written by earlier work in the stream
-    for (int i = threadIdx.x; i < 512; i += kGemmThreads) {  // (codebook + h * coset) as fp16, exact (|v| <= 256)
-        const uint32_t av = a.A[i >> 1];
-        const int h = i & 1;
-        int v[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) v[e] = (int)(int8_t)(av >> (8 * e)) + (h ? (int)(int8_t)(a.cs >> (8 * e)) : 0);
-        AH[i] = make_uint2(h2u(__halves2half2(__int2half_rn(v[0]), __int2half_rn(v[1]))),
-                           h2u(__halves2half2(__int2half_rn(v[2]), __int2half_rn(v[3]))));
+    // lane-private codebook (entry f of lane l at word 32 f + l: a warp's lookups never share a bank), bytes + 128
+    for (int i = threadIdx.x; i < 256 * 32; i += kGemmThreads) cbk[i] = a.A[i >> 5] ^ 0x80808080u;
+    // M words of the CTA's four row tiles (arithmetic for uniform single-class layouts)
+    for (int i = threadIdx.x; i < 4 * a.nb; i += kGemmThreads) {
+        const int q = i / a.nb, b = i - q * a.nb, g = blockIdx.x * 4 + q;
+        uint32_t m = 0u;
+        if (g < a.ng) {
+            const size_t ti = (size_t)g * a.nb + b;
+            m = a.ucls ? ((uint32_t)(ti * 64 * NW(a.ucls)) | ((uint32_t)a.ucls << 29)) : __ldg(a.M + ti);
+        }
+        sM[i] = m;
     }
-    for (int i = threadIdx.x; i < 256; i += kGemmThreads) A_s[i] = a.A[i];
     __syncthreads();
 
     bool ok = true;
     if (warp < 8) {
         // ------------------------------------------------------------------ decoders
         const int q = warp & 3, hs = warp >> 2;
-        const int R = q * 32 + lane;
         const int g = blockIdx.x * 4 + q;
         const bool tile = g < a.ng;
         const int r = g * 32 + lane;
-        uint8_t *arow0 = sA + (R >> 3) * 2048 + (R & 7) * 16;
         const float up = tile ? a.rsc[r].x : 0.f;
-        auto mword = [&](int b) -> uint32_t {
-            if (!tile) return 0u;
-            const size_t ti = (size_t)g * a.nb + b;
-            if (a.ucls) return (uint32_t)(ti * 64 * NW(a.ucls)) | ((uint32_t)a.ucls << 29);
-            return __ldg(a.M + ti);
-        };
-        uint32_t w[24], wn[24];
-        uint32_t m_cur = mword(0), m_next = a.nb > 1 ? mword(1) : 0u;
-        load_tile_words((int)(m_cur >> 29), a.D + (m_cur & 0x1FFFFFFFu), hs, lane, w);
-        float s_cur = tile ? h2f(a.S[r]) : 0.f;
-        for (int b = 0; b < a.nb; ++b) {
-            // prefetch: payload and scale of block b + 1, M word of block b + 2
-            float s_next = 0.f;
-            uint32_t m_n2 = 0u;
-            if (b + 1 < a.nb) {
-                load_tile_words((int)(m_next >> 29), a.D + (m_next & 0x1FFFFFFFu), hs, lane, wn);
-                if (tile) s_next = h2f(a.S[(size_t)(b + 1) * a.rows + r]);
-                if (b + 2 < a.nb) m_n2 = mword(b + 2);
+        const int c0 = (int)(int8_t)a.cs, c1 = (int)(int8_t)(a.cs >> 8), c2 = (int)(int8_t)(a.cs >> 16), c3 = (int)(int8_t)(a.cs >> 24);
+        const uint32_t dlo = h2u(__floats2half2_rn((float)(c0 - 1152), (float)(c1 - 1152))) ^ kHalf2M1152;
+        const uint32_t dhi = h2u(__floats2half2_rn((float)(c2 - 1152), (float)(c3 - 1152))) ^ kHalf2M1152;
+        const uint32_t *cl = cbk + lane;
+        const uint32_t tA0 = tmem + ((uint32_t)(q * 32) << 16) + kGemmAColBase;
+        float s_next = tile ? h2f(a.S[r]) : 0.f;
+        for (int b = 0; b < a.nb && ok; ++b) {
+            const int s = 2 * b + hs;
+            const float s_cur = s_next;
+            if (tile && b + 1 < a.nb) s_next = h2f(a.S[(size_t)(b + 1) * a.rows + r]);
+            const int ps = s % np, as = s & (kGemmASlots - 1);
+            bool w = mbar_wait_bounded(p_full + ps, (uint32_t)(s / np) & 1u, kGemmPolls);
+            w = mbar_wait_bounded(a_empty + as, ((uint32_t)(s / kGemmASlots) & 1u) ^ 1u, kGemmPolls) && w;
+            if (!__all_sync(0xffffffffu, w)) {
+                ok = false;
+                break;
             }
-            const int s = 2 * b + hs, slot = s % nst;
-            const uint32_t ph = (uint32_t)(s / nst) & 1u;
-            if (!mbar_wait_bounded(empty + slot, ph ^ 1u, kGemmPolls)) ok = false;
-            decode_tile((int)(m_cur >> 29), w, lane, AH, A_s, a.cs, __fmul_rn(s_cur, up), arow0 + (size_t)slot * kGemmStageA);
-            fence_proxy_async();
+            tc_fence_after();
+            const uint32_t m = sM[q * a.nb + b];
+            const uint32_t *pw = reinterpret_cast<const uint32_t *>(sP + (size_t)ps * stageP + q * a.tileb);
+            decode_tile_tmem((int)(m >> 29), pw, lane, cl, a.cs, __fmul_rn(s_cur, up), dlo, dhi, tA0 + 64 * as);
+            tmem_wait_st();
+            tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(full_a + slot);
-#pragma unroll
-            for (int i = 0; i < 24; ++i) w[i] = wn[i];
-            s_cur = s_next;
-            m_cur = m_next;
-            m_next = m_n2;
+            if (lane == 0) {
+                mbar_arrive(p_empty + ps);
+                mbar_arrive(a_full + as);
+            }
         }
     } else if (warp == 8) {
-        // ------------------------------------------------------------------ activation tiles
-        if (lane == 0) {
-            const uint8_t *src = a.Xh + (size_t)blockIdx.y * stageB;
-            const size_t panel = (size_t)a.npad * 256;
-            for (int s = 0; s < nhs; ++s) {
-                const int slot = s % nst;
-                const uint32_t ph = (uint32_t)(s / nst) & 1u;
-                if (!mbar_wait_bounded(empty + slot, ph ^ 1u, kGemmPolls)) ok = false;
-                mbar_expect_tx(full_b + slot, (uint32_t)stageB);
-                bulk_g2s(sB + (size_t)slot * stageB, src + (size_t)s * panel, (uint32_t)stageB, full_b + slot);
+        // ------------------------------------------------------------------ payload staging (bulk copies, deep ring)
+        // The whole warp runs the loop (no lane parked on a divergent path behind the decoders' shared-memory traffic):
+        // every lane polls the barrier, lanes 0-3 each own one row tile's copy, lane 0 posts the byte count.
+        int last = -1;
+        for (int s = 0; s < nhs; ++s) {
+            const int b = s >> 1, hs = s & 1, ps = s % np;
+            const bool w = mbar_wait_bounded(p_empty + ps, ((uint32_t)(s / np) & 1u) ^ 1u, kGemmPolls);
+            if (!__all_sync(0xffffffffu, w)) {
+                ok = false;
+                break;
             }
-            // drain: every copy issued has landed before the CTA may exit
-            for (int s = nhs - nst < 0 ? 0 : nhs - nst; s < nhs; ++s)
-                if (!mbar_wait_bounded(full_b + s % nst, (uint32_t)(s / nst) & 1u, kGemmPolls)) ok = false;
+            const uint32_t m = lane < 4 ? sM[lane * a.nb + b] : 0u;
+            const int nw = NW((int)(m >> 29));
+            uint32_t bytes = (uint32_t)nw * 128u;
+            bytes += __shfl_xor_sync(0xffffffffu, bytes, 1);
+            bytes += __shfl_xor_sync(0xffffffffu, bytes, 2);
+            if (lane == 0) {
+                if (bytes) mbar_expect_tx(p_full + ps, bytes);
+                else mbar_arrive(p_full + ps);
+            }
+            __syncwarp();
+            if (lane < 4 && nw)
+                bulk_g2s(sP + (size_t)ps * stageP + lane * a.tileb, a.D + (m & 0x1FFFFFFFu) + (size_t)hs * nw * 32,
+                         (uint32_t)nw * 128u, p_full + ps);
+            last = s;
         }
-        __syncwarp();
+        for (int s = last - np + 1 < 0 ? 0 : last - np + 1; s <= last; ++s)  // drain: every copy has landed
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(p_full + s % np, (uint32_t)(s / np) & 1u, kGemmPolls))) ok = false;
+    } else if (warp == 10) {
+        // ------------------------------------------------------------------ activation tiles (whole warp, lane 0 copies)
+        const uint8_t *src = a.Xh + (size_t)blockIdx.y * stageB;
+        const size_t panel = (size_t)a.npad * 256;
+        int last = -1;
+        for (int s = 0; s < nhs; ++s) {
+            const int bs = s % nbs;
+            const bool w = mbar_wait_bounded(b_empty + bs, ((uint32_t)(s / nbs) & 1u) ^ 1u, kGemmPolls);
+            if (!__all_sync(0xffffffffu, w)) {
+                ok = false;
+                break;
+            }
+            if (lane == 0) {
+                mbar_expect_tx(b_full + bs, (uint32_t)stageB);
+                bulk_g2s(sB + (size_t)bs * stageB, src + (size_t)s * panel, (uint32_t)stageB, b_full + bs);
+            }
+            __syncwarp();
+            last = s;
+        }
+        for (int s = last - nbs + 1 < 0 ? 0 : last - nbs + 1; s <= last; ++s)
+            if (!__all_sync(0xffffffffu, mbar_wait_bounded(b_full + s % nbs, (uint32_t)(s / nbs) & 1u, kGemmPolls))) ok = false;
     } else {
-        // ------------------------------------------------------------------ MMA issue
-        if (lane == 0) {
-            const uint32_t idesc = umma_idesc_f16(bn);
-            for (int s = 0; s < nhs; ++s) {
-                const int slot = s % nst;
-                const uint32_t ph = (uint32_t)(s / nst) & 1u;
-                bool st_ok = mbar_wait_bounded(full_a + slot, ph, kGemmPolls);
-                st_ok = mbar_wait_bounded(full_b + slot, ph, kGemmPolls) && st_ok;
-                tc_fence_after();
-                if (st_ok) {
-                    const uint64_t da = smem_desc(smem_u32(sA + (size_t)slot * kGemmStageA));
-                    const uint64_t db = smem_desc(smem_u32(sB + (size_t)slot * stageB));
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)  // K = 16 per MMA: two core matrices (256 B) further along K
-                        umma_f16(tmem, da + (uint64_t)(16 * kk), db + (uint64_t)(16 * kk), idesc, (s | kk) != 0);
-                } else {
-                    ok = false;
-                }
-                umma_commit(empty + slot);
+        // ------------------------------------------------------------------ MMA issue (warp 9; lane 0 issues)
+        const uint32_t idesc = umma_idesc_f16(bn);
+        for (int s = 0; s < nhs; ++s) {
+            const int as = s & (kGemmASlots - 1), bs = s % nbs;
+            bool st = mbar_wait_bounded(a_full + as, (uint32_t)(s / kGemmASlots) & 1u, kGemmPolls);
+            st = mbar_wait_bounded(b_full + bs, (uint32_t)(s / nbs) & 1u, kGemmPolls) && st;
+            tc_fence_after();
+            if (!__all_sync(0xffffffffu, st)) {
+                ok = false;
+                break;
             }
-            umma_commit(acc_bar);
-            if (!mbar_wait_bounded(acc_bar, 0, kGemmPolls)) ok = false;  // own MMAs done before TMEM is freed
+            if (lane == 0) {
+                const uint64_t db = smem_desc(smem_u32(sB + (size_t)bs * stageB));
+                const uint32_t ta = tmem + kGemmAColBase + 64 * as;
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk)  // K = 16 per MMA: 8 TMEM columns of A, two core matrices (256 B) of B
+                    umma_f16_ts(tmem, ta + 8 * kk, db + (uint64_t)(16 * kk), idesc, (s | kk) != 0);
+                umma_commit(a_empty + as);
+                umma_commit(b_empty + bs);
+            }
+            __syncwarp();
         }
+        if (lane == 0) umma_commit(acc_bar);
         __syncwarp();
+        // own MMAs done before TMEM is freed
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(acc_bar, 0, kGemmPolls))) ok = false;
     }
 
     if (warp < 8) {
         // ------------------------------------------------------------------ epilogue
         pdl_launch_dependents();
-        bool acc_ok = mbar_wait_bounded(acc_bar, 0, kGemmPolls);
+        bool acc_ok = ok && mbar_wait_bounded(acc_bar, 0, kGemmPolls);
         acc_ok = __all_sync(0xffffffffu, acc_ok);
         tc_fence_after();
         if (!acc_ok) ok = false;
@@ -437,13 +554,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
         const int e0 = row ? a.cp[ro] : 0, e1 = row ? a.cp[ro + 1] : 0;
         const int n0 = blockIdx.y * bn;
         const int cw = bn >> 1;
-        for (int c0 = half * cw; acc_ok && c0 < (half + 1) * cw; c0 += 16) {
+        for (int cc0 = half * cw; acc_ok && cc0 < (half + 1) * cw; cc0 += 16) {
             uint32_t v[16];
-            tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+            tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)cc0, v);
             if (row) {
 #pragma unroll
                 for (int i = 0; i < 16; ++i) {
-                    const int n = n0 + c0 + i;
+                    const int n = n0 + cc0 + i;
                     if (n < a.ncols) {
                         float y = __fmul_rn(__fmul_rn(__uint_as_float(v[i]), down), a.tdown[n]);
                         const float *xn = a.X + (size_t)n * a.ldx;
@@ -460,23 +577,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
     __syncthreads();
     if (warp == 9) {
         tc_fence_after();
-        tmem_dealloc(tmem, tcols);
+        tmem_dealloc(tmem, kGemmTmemCols);
     }
 }
 
 // ---------------------------------------------------------------------------------------------------------------
 // host side
 struct GemmPlan {
-    int bn, nst, npad, nkc, mt, nnt;
+    int bn, nbs, np, tileb, npad, nkc, mt, nnt;
     size_t xh, pmax, tdown, total, smem;
 };
 
-static int gemm_stages(int bn) {
-    const int s = kGemmOperandBudget / (kGemmStageA + bn * 256);
-    return s > kGemmMaxStages ? kGemmMaxStages : s;
-}
-static size_t gemm_smem(int bn) {
-    return (size_t)gemm_stages(bn) * (kGemmStageA + bn * 256) + kGemmAH + 1024 + 8 * (3 * kGemmMaxStages + 1) + 16;
+static int gemm_tile_bytes(const p8_tensor *t) {  // staging bytes of one tile's half-slice: the largest class present
+    int m = 1;
+    for (int c = 1; c < 8; ++c)
+        if (((t->class_mask >> c) & 1u) && NW(c) > m) m = NW(c);
+    return m * 128;
 }
 
 static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols) {
@@ -493,7 +609,12 @@ static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols) {
         if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = bn; }
     }
     p.bn = best;
-    p.nst = gemm_stages(best);
+    p.tileb = gemm_tile_bytes(t);
+    p.nbs = best >= 256 ? 2 : best >= 128 ? 3 : kGemmMaxB;
+    p.np = kGemmMaxP;
+    while (p.np > 2 && gemm_smem_layout(p.bn, p.nbs, p.np, p.tileb, t->nb).total > kGemmSmemMax) --p.np;
+    while (p.nbs > 2 && gemm_smem_layout(p.bn, p.nbs, p.np, p.tileb, t->nb).total > kGemmSmemMax) --p.nbs;
+    p.smem = (size_t)gemm_smem_layout(p.bn, p.nbs, p.np, p.tileb, t->nb).total;
     p.nnt = (int)((ncols + best - 1) / best);
     p.npad = p.nnt * best;
     p.nkc = (t->K + 2047) / 2048;
@@ -501,12 +622,12 @@ static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols) {
     p.pmax = al256((size_t)t->K * p.npad * 2);
     p.tdown = p.pmax + al256((size_t)p.npad * p.nkc * 4);
     p.total = p.tdown + al256((size_t)p.npad * 4);
-    p.smem = gemm_smem(best);
     return p;
 }
 
 bool gemm_supported(const p8_tensor *t, int64_t ncols) {
-    return ncols >= kGemmMinCols && t->K <= 65536 && t->rsc != nullptr;
+    return ncols >= kGemmMinCols && t->K <= 65536 && t->rsc != nullptr &&
+           (size_t)gemm_plan(t, ncols).smem <= (size_t)kGemmSmemMax;
 }
 
 size_t gemm_workspace(const p8_tensor *t, int64_t ncols) { return gemm_plan(t, ncols).total; }
@@ -515,13 +636,13 @@ p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t
                       size_t ws_bytes, cudaStream_t st) {
     const GemmPlan p = gemm_plan(t, ncols);
     if (!ws || ws_bytes < p.total || ((uintptr_t)ws & 255)) return P8_ERR_WORKSPACE;
+    if (p.smem > (size_t)kGemmSmemMax) return P8_ERR_UNSUPPORTED;
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        size_t mx = 0;
-        for (int bn = 32; bn <= 256; bn <<= 1) mx = gemm_smem(bn) > mx ? gemm_smem(bn) : mx;
-        if (cudaFuncSetAttribute(k_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)mx) != cudaSuccess) return P8_ERR_CUDA;
+        if (cudaFuncSetAttribute(k_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemMax) != cudaSuccess)
+            return P8_ERR_CUDA;
         attr_set[dev] = true;
     }
     uint8_t *w = static_cast<uint8_t *>(ws);
@@ -539,8 +660,8 @@ p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t
     GemmArgs ga;
     ga.A = t->A; ga.M = t->M; ga.D = t->D; ga.S = t->S; ga.prm = t->prm; ga.rsc = t->rsc; ga.cp = t->cp; ga.cc = t->cc;
     ga.cv = t->cv; ga.X = X; ga.Y = Y; ga.Xh = xa.Xh; ga.tdown = xa.tdown; ga.ldx = ldx; ga.ldy = ldy; ga.cs = t->cs;
-    ga.rows = t->rows; ga.nb = t->nb; ga.ng = t->ng; ga.ncols = (int)ncols; ga.npad = p.npad; ga.bn = p.bn; ga.nst = p.nst;
-    ga.ucls = t->uniform_class;
+    ga.rows = t->rows; ga.nb = t->nb; ga.ng = t->ng; ga.ncols = (int)ncols; ga.npad = p.npad; ga.bn = p.bn; ga.nbs = p.nbs;
+    ga.np = p.np; ga.tileb = p.tileb; ga.ucls = t->uniform_class;
     void *args[] = {&ga};
     if (launch_pdl((const void *)k_gemm, dim3(p.mt, p.nnt), dim3(kGemmThreads), p.smem, st, args) != cudaSuccess)
         return P8_ERR_CUDA;
