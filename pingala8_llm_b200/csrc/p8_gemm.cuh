@@ -389,7 +389,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < np; ++i) {
-            mbar_init(p_full + i, 1);   // payload bytes arrived (expect_tx arrive)
+            mbar_init(p_full + i, 4);   // one arrival (with its byte count) per row tile, then the bytes
             mbar_init(p_empty + i, 4);  // the four decoder warps of the stage have read the slot
         }
         for (int i = 0; i < nbs; ++i) {
@@ -463,8 +463,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
     } else if (warp == 8) {
         // ------------------------------------------------------------------ payload staging (bulk copies, deep ring)
         // The whole warp runs the loop (no lane parked on a divergent path behind the decoders' shared-memory traffic):
-        // every lane polls the barrier, lanes 0-3 each own one row tile's copy, lane 0 posts the byte count.
+        // every lane polls the barrier; lanes 0-3 each own one row tile: each arrives on the stage's barrier with its
+        // own byte count (count 4) and issues its copy, with no cross-lane step. The M word of the next stage is read
+        // one iteration ahead.
         int last = -1;
+        uint32_t m = lane < 4 ? sM[lane * a.nb] : 0u;
         for (int s = 0; s < nhs; ++s) {
             const int b = s >> 1, hs = s & 1, ps = s % np;
             const bool w = mbar_wait_bounded(p_empty + ps, ((uint32_t)(s / np) & 1u) ^ 1u, kGemmPolls);
@@ -472,19 +475,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
                 ok = false;
                 break;
             }
-            const uint32_t m = lane < 4 ? sM[lane * a.nb + b] : 0u;
             const int nw = NW((int)(m >> 29));
-            uint32_t bytes = (uint32_t)nw * 128u;
-            bytes += __shfl_xor_sync(0xffffffffu, bytes, 1);
-            bytes += __shfl_xor_sync(0xffffffffu, bytes, 2);
-            if (lane == 0) {
-                if (bytes) mbar_expect_tx(p_full + ps, bytes);
-                else mbar_arrive(p_full + ps);
+            if (lane < 4) {
+                if (nw) {
+                    mbar_expect_tx(p_full + ps, (uint32_t)nw * 128u);
+                    bulk_g2s(sP + (size_t)ps * stageP + lane * a.tileb, a.D + (m & 0x1FFFFFFFu) + (size_t)hs * nw * 32,
+                             (uint32_t)nw * 128u, p_full + ps);
+                } else {
+                    mbar_arrive(p_full + ps);
+                }
             }
-            __syncwarp();
-            if (lane < 4 && nw)
-                bulk_g2s(sP + (size_t)ps * stageP + lane * a.tileb, a.D + (m & 0x1FFFFFFFu) + (size_t)hs * nw * 32,
-                         (uint32_t)nw * 128u, p_full + ps);
+            if (hs && lane < 4 && b + 1 < a.nb) m = sM[lane * a.nb + b + 1];
             last = s;
         }
         for (int s = last - np + 1 < 0 ? 0 : last - np + 1; s <= last; ++s)  // drain: every copy has landed
