@@ -126,6 +126,20 @@ def test_full_size_gemv_vs_oracle(label, rows, K):
     assert r < TIGHT, r
 
 
+@pytest.mark.parametrize("rows,K", [(256, 49152), (256, 65280)])
+def test_gemv_table_refills_long_rows(rows, K):
+    """Few rows and long K: a CTA's units span three 256-column blocks, so a table buffer is refilled (by the last warp
+    done with it) while other warps still work on the previous block. K = 65280 is the largest K a slot can hold."""
+    s = synth.make_slot(rows, K, seed=rows + K, nd=7)
+    t = P8Tensor(s, K, rows)
+    o = Oracle(s, rows, K)
+    x = np.random.default_rng(rows).normal(0, 1, K).astype(np.float32)
+    y1 = t.mul_mat_vec(torch.from_numpy(x).cuda()).cpu().numpy()
+    y2 = t.mul_mat_vec(torch.from_numpy(x).cuda()).cpu().numpy()
+    assert rel(y1, o.mul_mat(x)[0]) < TIGHT
+    assert np.array_equal(y1, y2)
+
+
 @pytest.mark.parametrize("label,rows,K", SHAPES[:3])
 def test_full_size_unit_vector_property(label, rows, K):
     """Size-independent property: W e_k is column k of W. x16 quantises a Hadamard-rotated unit vector exactly, so
