@@ -48,9 +48,10 @@ constexpr int kGemmASlots = 4;                      // A operand stages in TMEM,
 constexpr int kGemmAColBase = 256;                  // TMEM columns [0, 256): accumulator; [256, 512): A stages
 constexpr uint32_t kGemmTmemCols = 512;
 constexpr int kGemmMaxB = 4, kGemmMaxP = 8;         // activation / payload ring depths
-constexpr int kGemmSmemMax = 227 * 1024;            // dynamic shared memory per CTA (sm_100 opt-in maximum)
+constexpr int kGemmSmemMax = 227 * 1024;            // shared memory per CTA (sm_100 opt-in maximum)
+constexpr int kGemmSmemDyn = kGemmSmemMax - 1024;   // dynamic part (the kernel's static shared memory takes 1 KB)
 constexpr uint32_t kGemmPolls = 1u << 22;
-constexpr int kGemmMinCols = 8;                     // below this the per-column table GEMV is faster
+constexpr int kGemmMinCols = 4;                     // below this the per-column table GEMV is faster (measured crossover)
 
 struct GemmArgs {
     const uint32_t *A, *M, *D;
@@ -67,6 +68,9 @@ struct GemmArgs {
     long long ldx, ldy;
     uint32_t cs;
     int rows, nb, ng, ncols, npad, bn, nbs, np, tileb, ucls;
+    int ksplit, mtr;       // split-K: CTAs per output tile along K; padded rows of the partials
+    float *kpart;          // split-K partial accumulators [ksplit][npad][mtr] (raw fp32)
+    unsigned int *kcnt;    // split-K arrivals per output tile (zeroed by k_gx_max)
 };
 
 struct GxArgs {
@@ -77,6 +81,8 @@ struct GxArgs {
     float *tdown;
     long long ldx;
     int K, nb, ncols, npad, nkc;
+    unsigned int *kcnt;    // split-K tile counters to zero (or null)
+    int ncnt;
 };
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -142,6 +148,10 @@ __global__ void __launch_bounds__(256) k_gx_max(const GxArgs a) {
     pdl_launch_dependents();
     pdl_wait();
     __shared__ float red[8];
+    if (a.kcnt) {  // the GEMM's split-K tile counters start each call at zero
+        for (int i = (blockIdx.y * gridDim.x + blockIdx.x) * 256 + threadIdx.x; i < a.ncnt; i += gridDim.x * gridDim.y * 256)
+            a.kcnt[i] = 0u;
+    }
     const int n = blockIdx.x, col = blockIdx.y * 2048 + threadIdx.x * 8;
     float m = 0.f;
     if (n < a.ncols && col < a.K) {
@@ -385,7 +395,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
     uint64_t *p_empty = p_full + kGemmMaxP, *b_full = p_empty + kGemmMaxP, *b_empty = b_full + kGemmMaxB;
     uint64_t *a_full = b_empty + kGemmMaxB, *a_empty = a_full + kGemmASlots, *acc_bar = a_empty + kGemmASlots;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(g_smem + L.tslot);
-    const int nhs = 2 * a.nb;  // stages = half-slices
+    // split-K: this CTA's 256-column blocks [b0, b1); local stage ls = 2 (b - b0) + hs indexes every ring
+    const int b0 = a.nb * (int)blockIdx.z / a.ksplit, b1 = a.nb * ((int)blockIdx.z + 1) / a.ksplit;
+    const int nls = 2 * (b1 - b0);
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < np; ++i) {
@@ -436,11 +448,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
         const uint32_t dhi = h2u(__floats2half2_rn((float)(c2 - 1152), (float)(c3 - 1152))) ^ kHalf2M1152;
         const uint32_t *cl = cbk + lane;
         const uint32_t tA0 = tmem + ((uint32_t)(q * 32) << 16) + kGemmAColBase;
-        float s_next = tile ? h2f(a.S[r]) : 0.f;
-        for (int b = 0; b < a.nb && ok; ++b) {
-            const int s = 2 * b + hs;
+        float s_next = tile ? h2f(a.S[(size_t)b0 * a.rows + r]) : 0.f;
+        for (int b = b0; b < b1 && ok; ++b) {
+            const int s = 2 * (b - b0) + hs;
             const float s_cur = s_next;
-            if (tile && b + 1 < a.nb) s_next = h2f(a.S[(size_t)(b + 1) * a.rows + r]);
+            if (tile && b + 1 < b1) s_next = h2f(a.S[(size_t)(b + 1) * a.rows + r]);
             const int ps = s % np, as = s & (kGemmASlots - 1);
             bool w = mbar_wait_bounded(p_full + ps, (uint32_t)(s / np) & 1u, kGemmPolls);
             w = mbar_wait_bounded(a_empty + as, ((uint32_t)(s / kGemmASlots) & 1u) ^ 1u, kGemmPolls) && w;
@@ -467,9 +479,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
         // own byte count (count 4) and issues its copy, with no cross-lane step. The M word of the next stage is read
         // one iteration ahead.
         int last = -1;
-        uint32_t m = lane < 4 ? sM[lane * a.nb] : 0u;
-        for (int s = 0; s < nhs; ++s) {
-            const int b = s >> 1, hs = s & 1, ps = s % np;
+        uint32_t m = lane < 4 ? sM[lane * a.nb + b0] : 0u;
+        for (int s = 0; s < nls; ++s) {
+            const int b = b0 + (s >> 1), hs = s & 1, ps = s % np;
             const bool w = mbar_wait_bounded(p_empty + ps, ((uint32_t)(s / np) & 1u) ^ 1u, kGemmPolls);
             if (!__all_sync(0xffffffffu, w)) {
                 ok = false;
@@ -485,7 +497,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
                     mbar_arrive(p_full + ps);
                 }
             }
-            if (hs && lane < 4 && b + 1 < a.nb) m = sM[lane * a.nb + b + 1];
+            if (hs && lane < 4 && b + 1 < b1) m = sM[lane * a.nb + b + 1];
             last = s;
         }
         for (int s = last - np + 1 < 0 ? 0 : last - np + 1; s <= last; ++s)  // drain: every copy has landed
@@ -495,7 +507,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
         const uint8_t *src = a.Xh + (size_t)blockIdx.y * stageB;
         const size_t panel = (size_t)a.npad * 256;
         int last = -1;
-        for (int s = 0; s < nhs; ++s) {
+        for (int s = 0; s < nls; ++s) {
             const int bs = s % nbs;
             const bool w = mbar_wait_bounded(b_empty + bs, ((uint32_t)(s / nbs) & 1u) ^ 1u, kGemmPolls);
             if (!__all_sync(0xffffffffu, w)) {
@@ -504,7 +516,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
             }
             if (lane == 0) {
                 mbar_expect_tx(b_full + bs, (uint32_t)stageB);
-                bulk_g2s(sB + (size_t)bs * stageB, src + (size_t)s * panel, (uint32_t)stageB, b_full + bs);
+                bulk_g2s(sB + (size_t)bs * stageB, src + (size_t)(2 * b0 + s) * panel, (uint32_t)stageB, b_full + bs);
             }
             __syncwarp();
             last = s;
@@ -514,7 +526,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
     } else {
         // ------------------------------------------------------------------ MMA issue (warp 9; lane 0 issues)
         const uint32_t idesc = umma_idesc_f16(bn);
-        for (int s = 0; s < nhs; ++s) {
+        for (int s = 0; s < nls; ++s) {
             const int as = s & (kGemmASlots - 1), bs = s % nbs;
             bool st = mbar_wait_bounded(a_full + as, (uint32_t)(s / kGemmASlots) & 1u, kGemmPolls);
             st = mbar_wait_bounded(b_full + bs, (uint32_t)(s / nbs) & 1u, kGemmPolls) && st;
@@ -555,7 +567,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
         const int e0 = row ? a.cp[ro] : 0, e1 = row ? a.cp[ro + 1] : 0;
         const int n0 = blockIdx.y * bn;
         const int cw = bn >> 1;
-        for (int cc0 = half * cw; acc_ok && cc0 < (half + 1) * cw; cc0 += 16) {
+        if (a.ksplit > 1) {  // raw accumulators of this K range -> partials (the tile's last CTA finishes below)
+            const int rp = blockIdx.x * 128 + q * 32 + lane;
+            for (int cc0 = half * cw; acc_ok && cc0 < (half + 1) * cw; cc0 += 16) {
+                uint32_t v[16];
+                tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)cc0, v);
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    a.kpart[((size_t)blockIdx.z * a.npad + n0 + cc0 + i) * a.mtr + rp] = __uint_as_float(v[i]);
+            }
+        }
+        for (int cc0 = half * cw; acc_ok && a.ksplit == 1 && cc0 < (half + 1) * cw; cc0 += 16) {
             uint32_t v[16];
             tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)cc0, v);
             if (row) {
@@ -574,6 +596,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
     }
     ok = __all_sync(0xffffffffu, ok);
     if (!ok && lane == 0) atomicOr(&g_p8_device_error, 4u);
+    if (a.ksplit > 1) {
+        // split-K fixup: the last CTA of the output tile sums the partials in split order (deterministic), then
+        // scales, adds the clamp delta and scatters y
+        __shared__ int s_last;
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) s_last = atomicAdd(a.kcnt + blockIdx.y * gridDim.x + blockIdx.x, 1u) == (unsigned)a.ksplit - 1;
+        __syncthreads();
+        if (s_last && warp < 8) {
+            __threadfence();
+            const int q = warp & 3, half = warp >> 2;
+            const int r = blockIdx.x * 128 + q * 32 + lane;
+            if (r < a.rows) {
+                const int ro = a.prm[r];
+                const float down = a.rsc[r].y;
+                const int e0 = a.cp[ro], e1 = a.cp[ro + 1];
+                const int cw = bn >> 1, n0 = blockIdx.y * bn;
+                for (int c = half * cw; c < (half + 1) * cw; ++c) {
+                    const int n = n0 + c;
+                    if (n >= a.ncols) break;
+                    float acc = 0.f;
+                    for (int z = 0; z < a.ksplit; ++z) acc = __fadd_rn(acc, __ldcg(a.kpart + ((size_t)z * a.npad + n) * a.mtr + r));
+                    float y = __fmul_rn(__fmul_rn(acc, down), a.tdown[n]);
+                    const float *xn = a.X + (size_t)n * a.ldx;
+                    for (int e = e0; e < e1; ++e) y = __fadd_rn(y, __fmul_rn(a.cv[e], xn[a.cc[e]]));
+                    a.Y[(size_t)n * a.ldy + ro] = y;
+                }
+            }
+        }
+    }
     tc_fence_before();
     __syncthreads();
     if (warp == 9) {
@@ -585,8 +637,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
 // ---------------------------------------------------------------------------------------------------------------
 // host side
 struct GemmPlan {
-    int bn, nbs, np, tileb, npad, nkc, mt, nnt;
-    size_t xh, pmax, tdown, total, smem;
+    int bn, nbs, np, tileb, npad, nkc, mt, nnt, ks;
+    size_t xh, pmax, tdown, kpart, kcnt, total, smem;
 };
 
 static int gemm_tile_bytes(const p8_tensor *t) {  // staging bytes of one tile's half-slice: the largest class present
@@ -613,22 +665,33 @@ static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols) {
     p.tileb = gemm_tile_bytes(t);
     p.nbs = best >= 256 ? 2 : best >= 128 ? 3 : kGemmMaxB;
     p.np = kGemmMaxP;
-    while (p.np > 2 && gemm_smem_layout(p.bn, p.nbs, p.np, p.tileb, t->nb).total > kGemmSmemMax) --p.np;
-    while (p.nbs > 2 && gemm_smem_layout(p.bn, p.nbs, p.np, p.tileb, t->nb).total > kGemmSmemMax) --p.nbs;
+    while (p.np > 2 && gemm_smem_layout(p.bn, p.nbs, p.np, p.tileb, t->nb).total > kGemmSmemDyn) --p.np;
+    while (p.nbs > 2 && gemm_smem_layout(p.bn, p.nbs, p.np, p.tileb, t->nb).total > kGemmSmemDyn) --p.nbs;
     p.smem = (size_t)gemm_smem_layout(p.bn, p.nbs, p.np, p.tileb, t->nb).total;
     p.nnt = (int)((ncols + best - 1) / best);
     p.npad = p.nnt * best;
     p.nkc = (t->K + 2047) / 2048;
+    // split-K when the output tiles leave at least half the SMs idle (small batches): CTAs per tile along K, at
+    // least two 256-column blocks each
+    p.ks = 1;
+    const int base = p.mt * p.nnt;
+    if (2 * base <= nsm) {
+        p.ks = nsm / base;
+        const int kmax = t->nb / 2 > 1 ? t->nb / 2 : 1;
+        if (p.ks > kmax) p.ks = kmax;
+    }
     p.xh = 0;
     p.pmax = al256((size_t)t->K * p.npad * 2);
     p.tdown = p.pmax + al256((size_t)p.npad * p.nkc * 4);
-    p.total = p.tdown + al256((size_t)p.npad * 4);
+    p.kpart = p.tdown + al256((size_t)p.npad * 4);
+    p.kcnt = p.kpart + (p.ks > 1 ? al256((size_t)p.ks * p.npad * p.mt * 128 * 4) : 0);
+    p.total = p.kcnt + (p.ks > 1 ? al256((size_t)base * 4) : 0);
     return p;
 }
 
 bool gemm_supported(const p8_tensor *t, int64_t ncols) {
     return ncols >= kGemmMinCols && t->K <= 65536 && t->rsc != nullptr &&
-           (size_t)gemm_plan(t, ncols).smem <= (size_t)kGemmSmemMax;
+           (size_t)gemm_plan(t, ncols).smem <= (size_t)kGemmSmemDyn;
 }
 
 size_t gemm_workspace(const p8_tensor *t, int64_t ncols) { return gemm_plan(t, ncols).total; }
@@ -637,12 +700,12 @@ p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t
                       size_t ws_bytes, cudaStream_t st) {
     const GemmPlan p = gemm_plan(t, ncols);
     if (!ws || ws_bytes < p.total || ((uintptr_t)ws & 255)) return P8_ERR_WORKSPACE;
-    if (p.smem > (size_t)kGemmSmemMax) return P8_ERR_UNSUPPORTED;
+    if (p.smem > (size_t)kGemmSmemDyn) return P8_ERR_UNSUPPORTED;
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        if (cudaFuncSetAttribute(k_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemMax) != cudaSuccess)
+        if (cudaFuncSetAttribute(k_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemDyn) != cudaSuccess)
             return P8_ERR_CUDA;
         attr_set[dev] = true;
     }
@@ -652,6 +715,8 @@ p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t
     xa.Xh = w + p.xh;
     xa.pmax = reinterpret_cast<float *>(w + p.pmax);
     xa.tdown = reinterpret_cast<float *>(w + p.tdown);
+    xa.kcnt = p.ks > 1 ? reinterpret_cast<unsigned int *>(w + p.kcnt) : nullptr;
+    xa.ncnt = p.mt * p.nnt;
     {
         void *args[] = {&xa};
         if (launch_pdl((const void *)k_gx_max, dim3(p.npad, p.nkc), dim3(256), 0, st, args) != cudaSuccess) return P8_ERR_CUDA;
@@ -663,8 +728,11 @@ p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t
     ga.cv = t->cv; ga.X = X; ga.Y = Y; ga.Xh = xa.Xh; ga.tdown = xa.tdown; ga.ldx = ldx; ga.ldy = ldy; ga.cs = t->cs;
     ga.rows = t->rows; ga.nb = t->nb; ga.ng = t->ng; ga.ncols = (int)ncols; ga.npad = p.npad; ga.bn = p.bn; ga.nbs = p.nbs;
     ga.np = p.np; ga.tileb = p.tileb; ga.ucls = t->uniform_class;
+    ga.ksplit = p.ks; ga.mtr = p.mt * 128;
+    ga.kpart = reinterpret_cast<float *>(w + p.kpart);
+    ga.kcnt = xa.kcnt;
     void *args[] = {&ga};
-    if (launch_pdl((const void *)k_gemm, dim3(p.mt, p.nnt), dim3(kGemmThreads), p.smem, st, args) != cudaSuccess)
+    if (launch_pdl((const void *)k_gemm, dim3(p.mt, p.nnt, p.ks), dim3(kGemmThreads), p.smem, st, args) != cudaSuccess)
         return P8_ERR_CUDA;
     return P8_OK;
 }

@@ -5,7 +5,7 @@ usage: python -m pingala8_llm_b200.profile [--group gate_up|qkv|o|down] [--iters
 
 Weights are seeded synthetic class-3 slots of the Llama-3.1-8B shapes. With --copies > 1 the calls rotate over
 distinct weight copies so repeated calls read DRAM rather than L2. Prints the mean time per call (CUDA events).
---ncols N (N >= 8) runs the batched product (tcgen05 GEMM) of each tensor of the group on N tokens instead of the
+--ncols N (N >= 4) runs the batched product (tcgen05 GEMM) of each tensor of the group on N tokens instead of the
 grouped batch-1 GEMV.
 """
 import argparse
