@@ -15,6 +15,8 @@ CUDA graph and replayed per step. Attention, norms and the LM head are not part 
             duration, timed with CUDA events around a graph of that call type's 32 per-layer calls, against
             MEASURED_PEAKS.json hbm_gbs; traffic = DRAM bytes of the same call from an ncu capture
   cpu_baseline  the reference's own CPU core (oracle/_ref, x16 vrc_tg) on one layer's 7 GEMVs, all host threads
+  prefill   (1 GPU) the batched product: 512 tokens through all 224 projections (tcgen05 GEMM), TFLOP/s against
+            MEASURED_PEAKS.json bf16_tflops
 
 usage: python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 """
@@ -142,6 +144,13 @@ class ClockSampler:
 
 # DRAM bytes (read + write) of one call, from ncu captures of the same call (profiles/k_gemv_llama8b_gate_up.md)
 TRAFFIC_BYTES = {"gate+up": 31587840}
+
+
+def measured_bf16_tflops():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return json.load(open(p)).get("bf16_tflops", 1590.0)
+    return 1590.0
 
 
 def measured_peaks():
@@ -331,6 +340,38 @@ def run_b200(args, rank, world, local_rank):
         nbytes = sum(algo_bytes_gemv(*dims[n]) for n in grp) - 4 * dims[grp[0]][1] * (len(grp) - 1)
         per_group["+".join(grp)] = (call_s, nbytes)
         del gg
+    # ---- prefill (batched product, tcgen05 GEMM) at 1 GPU: 512 tokens through every projection of all 32 layers
+    # (1.80 GB of weights per pass, larger than L2), one CUDA graph per pass, device-timed
+    prefill = None
+    if world == 1 and not args.no_prefill:
+        ntok = 512
+        pws = torch.empty(max(ts[n].workspace_size(ntok) for ts in layers for n in ts), dtype=torch.uint8, device=dev)
+        Xp = {K: torch.randn(ntok, K, device=dev) for K in {k for _, _, k in shapes}}
+        Yp = {n: torch.empty(ntok, r, device=dev) for n, (r, k) in local.items()}
+        gp = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            for ts in layers[:1]:
+                for n, tt in ts.items():
+                    tt.mul_mat(Xp[tt.K], out=Yp[n], workspace=pws, stream=stream)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(gp, stream=stream):
+                for ts in layers:
+                    for n, tt in ts.items():
+                        tt.mul_mat(Xp[tt.K], out=Yp[n], workspace=pws, stream=stream)
+        gp.replay()
+        torch.cuda.synchronize()
+        ep0, ep1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        npass = 3
+        ep0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(npass):
+                gp.replay()
+        ep1.record(stream)
+        torch.cuda.synchronize()
+        t_pass = ep0.elapsed_time(ep1) / 1e3 / npass
+        flop = sum(2.0 * r * k * ntok for _, r, k in shapes) * model["layers"]
+        prefill = (ntok, t_pass, flop)
+        del gp
     # ---- max over ranks
     gnames = list(per_group)
     times = torch.tensor([t_dev, t_e2e] + [per_group[g][0] for g in gnames], dtype=torch.float64, device=dev)
@@ -370,6 +411,15 @@ def run_b200(args, rank, world, local_rank):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),
     }
+    if prefill is not None:
+        ntok, t_pass, flop = prefill
+        bf16_peak = measured_bf16_tflops()
+        line["prefill"] = {"tokens": ntok, "ms": round(t_pass * 1e3, 3), "tok_s": round(ntok / t_pass, 1),
+                           "kernel": "p8_mul_mat (k_gx_max + k_gx_prep + k_gemm, tcgen05 kind::f16, fp32 accumulate)",
+                           "tflops": round(flop / t_pass / 1e12, 1), "bound": "tensor", "peak_tflops": bf16_peak,
+                           "frac": round(flop / t_pass / 1e12 / bf16_peak, 4),
+                           "peak_source": "MEASURED_PEAKS.json bf16_tflops (cuBLAS bf16 burst; the GEMM runs fp16 operands at the same rate)",
+                           "config": "512 tokens x 224 projections (32 layers), distinct weights, inputs resident"}
     if world == 1 and not args.no_cpu:
         layer_s, cores, isa = cpu_reference_layer(model, reps=5, warmup=1)
         line["cpu_baseline"] = {"value": round(1.0 / (model["layers"] * layer_s), 4), "unit": "tok/s", "cores": cores, "kind": "reference",
@@ -385,6 +435,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the batched-product (prefill) measurement")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
