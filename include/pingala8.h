@@ -40,7 +40,9 @@ typedef enum p8_status {
     P8_ERR_NOT_PREPARED = -12, /* tensor handle unknown / released (reference: GGML_ABORT, CU:3172) */
     P8_ERR_UNSUPPORTED = -13,  /* valid request this build does not serve */
     P8_ERR_TIMEOUT = -14,   /* a bounded device-side wait gave up (kernel returned early, results invalid) */
-    P8_ERR_SLOT = -15       /* no slot type is large enough (loader: "no slot type fits", CU:3498) */
+    P8_ERR_SLOT = -15,      /* no slot type is large enough (loader: "no slot type fits", CU:3498) */
+    P8_ERR_FILE = -16,      /* model file: I/O error, not a GGUF file (v2/v3), or a malformed container */
+    P8_ERR_MODEL = -17      /* model file: Pingala-8 keys or tensors missing or inconsistent (vr_native_init) */
 } p8_status;
 
 typedef struct p8_tensor p8_tensor;
@@ -150,6 +152,26 @@ p8_status p8_tp_shard_rows(const uint8_t *slot, size_t nbytes, int64_t K, int64_
  * slot; every rank keeps all rows, partial outputs are summed by an all-reduce. */
 p8_status p8_tp_shard_cols(const uint8_t *slot, size_t nbytes, int64_t K, int64_t rows, int64_t b0, int64_t b1,
                            uint8_t *out, size_t out_cap, size_t *out_n);
+
+/* ---------------------------------------------------------------- model files (GGUF) ---------------------------- */
+
+/* A GGUF file holding a Pingala-8 ("VR native") model, opened and checked as llama_model_loader::vr_native_init does
+ * (CU:3411-3508): KV vr.format, vr.ns = 108, vr.trl = 2, vr.n_linear (= 7 x <arch>.block_count when present),
+ * vr.layout 2 (kernel bytes + vr_prm) or 3 (VR3 file tensors, natural rows); per linear <base>.weight (I8),
+ * <base>.vr_c (F16 [K]), <base>.vr_prm (I16 [rows], layout 2), optional <base>.vr_didx (I16 [nd, 2]) and
+ * <base>.vr_dval (F32 [nd]); vr.had_signs (I8 [256]). Host memory only; one handle is not safe for concurrent use. */
+typedef struct p8_gguf p8_gguf;
+p8_status p8_gguf_open(const char *path, p8_gguf **out);
+void p8_gguf_close(p8_gguf *g);
+/* linears in name order */
+int64_t p8_gguf_n_linear(const p8_gguf *g);
+p8_status p8_gguf_linear_info(const p8_gguf *g, int64_t i, const char **name, int64_t *K, int64_t *rows, int64_t *nd,
+                              size_t *slot_nbytes, int *layout);
+/* Linear i as the slot the reference builds in device memory (vr_native_load, CU:3527-3580): kernel bytes (VR3
+ * expanded), c16, permutation (identity for VR3) and its inverse, clamp delta, signs and trailer, assembled in `out`
+ * (slot_nbytes bytes) with every loader check; every linear must carry the first one's codebook and coset. Upload
+ * the bytes and p8_prepare them. */
+p8_status p8_gguf_load_linear(p8_gguf *g, int64_t i, uint8_t *out, size_t out_cap, size_t *out_n);
 
 /* 1 if a kernel since the last call gave up on a bounded device-side wait (that launch's results are invalid), then
  * clears the flag. Synchronises the device. */

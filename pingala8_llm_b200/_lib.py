@@ -15,6 +15,7 @@ P8_STATUS = {
     0: "P8_OK", -1: "P8_ERR_ARG", -2: "P8_ERR_TRAILER", -3: "P8_ERR_HEADER", -4: "P8_ERR_PAYLOAD", -5: "P8_ERR_PERM",
     -6: "P8_ERR_DELTA", -7: "P8_ERR_SIGNS", -8: "P8_ERR_TABLES", -9: "P8_ERR_SHAPE", -10: "P8_ERR_CUDA",
     -11: "P8_ERR_WORKSPACE", -12: "P8_ERR_NOT_PREPARED", -13: "P8_ERR_UNSUPPORTED", -14: "P8_ERR_TIMEOUT", -15: "P8_ERR_SLOT",
+    -16: "P8_ERR_FILE", -17: "P8_ERR_MODEL",
 }
 
 
@@ -56,6 +57,12 @@ _SIGS = {
     "p8_vr3_expand": (C.c_int, [_vp, _sz, _sz, _sz, _vp, _sz]),
     "p8_tp_shard_rows": (C.c_int, [_vp, _sz, _i64, _i64, _i64, _i64, _vp, _sz, C.POINTER(_sz), _vp]),
     "p8_tp_shard_cols": (C.c_int, [_vp, _sz, _i64, _i64, _i64, _i64, _vp, _sz, C.POINTER(_sz)]),
+    "p8_gguf_open": (C.c_int, [C.c_char_p, C.POINTER(_vp)]),
+    "p8_gguf_close": (None, [_vp]),
+    "p8_gguf_n_linear": (_i64, [_vp]),
+    "p8_gguf_linear_info": (C.c_int, [_vp, _i64, C.POINTER(C.c_char_p), C.POINTER(_i64), C.POINTER(_i64), C.POINTER(_i64),
+                                      C.POINTER(_sz), C.POINTER(C.c_int)]),
+    "p8_gguf_load_linear": (C.c_int, [_vp, _i64, _vp, _sz, C.POINTER(_sz)]),
     "p8_device_error": (C.c_int, []),
     "p8_status_str": (C.c_char_p, [C.c_int]),
     "p8_build_info": (C.c_char_p, []),

@@ -419,6 +419,8 @@ const char *p8_status_str(p8_status s) {
         case P8_ERR_UNSUPPORTED: return "unsupported request";
         case P8_ERR_TIMEOUT: return "device wait timed out";
         case P8_ERR_SLOT: return "no slot type fits";
+        case P8_ERR_FILE: return "model file unreadable, not GGUF v2/v3, or malformed";
+        case P8_ERR_MODEL: return "model file: Pingala-8 keys or tensors missing or inconsistent";
     }
     return "unknown status";
 }
