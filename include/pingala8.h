@@ -153,6 +153,40 @@ p8_status p8_tp_shard_rows(const uint8_t *slot, size_t nbytes, int64_t K, int64_
 p8_status p8_tp_shard_cols(const uint8_t *slot, size_t nbytes, int64_t K, int64_t rows, int64_t b0, int64_t b1,
                            uint8_t *out, size_t out_cap, size_t *out_n);
 
+/* Fused row-parallel product: y = sum over ranks of (rank's column shard) x (rank's slice of x), computed by one GEMV
+ * launch per rank whose epilogue exchanges the partial rows over peer memory (NVLink stores, no collective library):
+ * each rank stores its partial y into every peer's exchange buffer, polls its own buffer for the peers' partials and
+ * sums the ranks' values in rank order, so every rank gets the same bits. A wait is bounded by the communicator's
+ * timeout; past it the launch gives up, p8_device_error reports bit 3 (8), the result is invalid and every rank must
+ * p8_tp_comm_reset its communicator (between steps, then a host barrier) before the next call. An entry whose tag
+ * names another row count (the ranks called different tensors) sets bit 4 (16).
+ *
+ * Exchange buffer of rank r: 2 * world * max_rows u64 entries; entry (parity s, source rank q, output row i) at index
+ * (s * world + q) * max_rows + i holds ((0x80000000 | rows) << 32) | float bits of rank q's partial y[i]; 0 = empty.
+ * Parity s = the communicator's call count & 1 (the first call is 1). Peers' buffers must have the same world and
+ * max_rows. All ranks make the same sequence of p8_tp_gemv_allreduce calls on their communicators, each with its
+ * column shard of one tensor (same rows); a rank with no columns cannot take part (use a collective instead). */
+typedef struct p8_tp_comm p8_tp_comm;
+#define P8_IPC_HANDLE_BYTES 64
+/* rank of world (1..8) on the current device, up to max_rows output rows per call, waits bounded by timeout_ms */
+p8_status p8_tp_comm_create(int rank, int world, int64_t max_rows, uint32_t timeout_ms, p8_tp_comm **out);
+p8_status p8_tp_comm_destroy(p8_tp_comm *c);
+/* CUDA IPC handle (P8_IPC_HANDLE_BYTES) of this rank's exchange buffer, for the other processes' p8_tp_comm_open_peer */
+p8_status p8_tp_comm_ipc_handle(const p8_tp_comm *c, void *handle, size_t handle_bytes);
+/* map peer q's exchange buffer from its IPC handle (one process per GPU) */
+p8_status p8_tp_comm_open_peer(p8_tp_comm *c, int q, const void *handle, size_t handle_bytes);
+/* or attach it by device pointer (one process driving several GPUs, peer access enabled by the caller) */
+p8_status p8_tp_comm_set_peer(p8_tp_comm *c, int q, void *dev_buffer);
+p8_status p8_tp_comm_buffer(const p8_tp_comm *c, void **dev_buffer, size_t *nbytes);
+/* calls made so far (synchronous device read) */
+p8_status p8_tp_comm_epoch(const p8_tp_comm *c, uint32_t *epoch);
+/* zero the exchange buffer and the call count (enqueued on stream) */
+p8_status p8_tp_comm_reset(p8_tp_comm *c, void *stream);
+/* the fused call: t = this rank's column shard (p8_tp_shard_cols), x its input slice, y [rows]; workspace as
+ * p8_workspace_size(t, 1). Enqueues on stream, capturable into a CUDA graph (the call count lives on the device). */
+p8_status p8_tp_gemv_allreduce(const p8_tensor *t, const float *x, float *y, p8_tp_comm *c, void *workspace,
+                               size_t workspace_bytes, void *stream);
+
 /* ---------------------------------------------------------------- model files (GGUF) ---------------------------- */
 
 /* A GGUF file holding a Pingala-8 ("VR native") model, opened and checked as llama_model_loader::vr_native_init does
@@ -173,8 +207,9 @@ p8_status p8_gguf_linear_info(const p8_gguf *g, int64_t i, const char **name, in
  * the bytes and p8_prepare them. */
 p8_status p8_gguf_load_linear(p8_gguf *g, int64_t i, uint8_t *out, size_t out_cap, size_t *out_n);
 
-/* 1 if a kernel since the last call gave up on a bounded device-side wait (that launch's results are invalid), then
- * clears the flag. Synchronises the device. */
+/* Non-zero if a kernel since the last call gave up (that launch's results are invalid), then clears the word. Bits:
+ * 1 GEMV table wait, 2 GEMV grid barrier, 4 GEMM pipeline wait timed out; 8 row-parallel exchange wait timed out,
+ * 16 exchange entry with a foreign tag. Synchronises the device. */
 int p8_device_error(void);
 
 const char *p8_status_str(p8_status s);

@@ -63,6 +63,15 @@ _SIGS = {
     "p8_gguf_linear_info": (C.c_int, [_vp, _i64, C.POINTER(C.c_char_p), C.POINTER(_i64), C.POINTER(_i64), C.POINTER(_i64),
                                       C.POINTER(_sz), C.POINTER(C.c_int)]),
     "p8_gguf_load_linear": (C.c_int, [_vp, _i64, _vp, _sz, C.POINTER(_sz)]),
+    "p8_tp_comm_create": (C.c_int, [C.c_int, C.c_int, _i64, _u32, C.POINTER(_vp)]),
+    "p8_tp_comm_destroy": (C.c_int, [_vp]),
+    "p8_tp_comm_ipc_handle": (C.c_int, [_vp, _vp, _sz]),
+    "p8_tp_comm_open_peer": (C.c_int, [_vp, C.c_int, _vp, _sz]),
+    "p8_tp_comm_set_peer": (C.c_int, [_vp, C.c_int, _vp]),
+    "p8_tp_comm_buffer": (C.c_int, [_vp, C.POINTER(_vp), C.POINTER(_sz)]),
+    "p8_tp_comm_epoch": (C.c_int, [_vp, C.POINTER(_u32)]),
+    "p8_tp_comm_reset": (C.c_int, [_vp, _vp]),
+    "p8_tp_gemv_allreduce": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "p8_device_error": (C.c_int, []),
     "p8_status_str": (C.c_char_p, [C.c_int]),
     "p8_build_info": (C.c_char_p, []),

@@ -65,6 +65,24 @@ p8_status launch_gemv_group(const p8_tensor *const *ts, int nt, const float *X, 
                             const int64_t *ldys, void *ws, size_t ws_bytes, cudaStream_t st);
 p8_status launch_gemv(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy, void *ws,
                       size_t ws_bytes, cudaStream_t st);
+// Fused row-parallel exchange of the GEMV epilogue (one-shot all-reduce over peer memory). Every rank owns an exchange
+// buffer of u64 entries: entry (parity s, source rank q, output row r) at index (s * world + q) * cap + r holds
+// (tag << 32) | float bits of rank q's partial y[r], 0 when empty. A rank stores its partials into every peer's buffer
+// (plain 8-byte stores over NVLink), then polls its own buffer for the peers' partials (bounded by timeout_ns), sums
+// the ranks' values in rank order and clears the entries it consumed. The parity s = epoch & 1 alternates per call, so
+// a rank one call ahead writes the other half while a slow peer still reads this one.
+constexpr int kTpMaxWorld = 8;
+struct TpExchange {
+    unsigned long long *peer[kTpMaxWorld];  // each rank's exchange buffer as mapped here (peer[rank] = own)
+    const unsigned int *epoch;              // this rank's call counter, advanced by the call's prep kernel
+    long long cap;                          // output rows per (parity, rank) section
+    unsigned long long timeout_ns;
+    unsigned int tag;                       // 0x80000000 | rows: an entry with another non-zero tag is a mismatch
+    int rank, world;
+};
+p8_status launch_gemv_tp(const p8_tensor *t, const float *x, float *y, const TpExchange &tp, unsigned int *epoch, void *ws,
+                         size_t ws_bytes, cudaStream_t st);
+
 size_t gemm_workspace(const p8_tensor *t, int64_t ncols);
 p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy, void *ws,
                       size_t ws_bytes, cudaStream_t st);

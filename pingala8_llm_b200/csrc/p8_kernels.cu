@@ -10,7 +10,8 @@
 
 namespace p8 {
 
-// device-side error word: bit 0 = a bounded wait timed out (that launch's results are invalid)
+// device-side error word (that launch's results are invalid): bit 0 GEMV table wait, bit 1 GEMV grid barrier, bit 2 GEMM
+// pipeline wait timed out; bit 3 row-parallel exchange wait timed out, bit 4 exchange entry with a foreign tag
 __device__ unsigned int g_p8_device_error = 0;
 
 // ================================================================================================================
@@ -258,6 +259,7 @@ struct PrepArgs {
     int *G;     // [nsl][128]
     float *d;   // [nsl]
     unsigned int *arrive;  // the GEMV's grid-barrier counter
+    unsigned int *epoch;   // row-parallel exchange: the call counter to advance (nullptr without an exchange)
 };
 
 __global__ void __launch_bounds__(256) k_act_prep(PrepArgs a) {
@@ -274,7 +276,10 @@ __global__ void __launch_bounds__(256) k_act_prep(PrepArgs a) {
         i1 = *reinterpret_cast<const float4 *>(ic + 4);
     }
     pdl_wait();  // x and the workspace belong to the previous kernel until it completes
-    if (b == 0 && fg == 0 && tid == 0) *a.arrive = 0u;
+    if (b == 0 && fg == 0 && tid == 0) {
+        *a.arrive = 0u;
+        if (a.epoch) *a.epoch += 1u;  // the GEMV reads it after this kernel completes
+    }
     if (tid < 32) {
         const float *x = a.X + b * 256 + 8 * lane;
         const float4 x0 = *reinterpret_cast<const float4 *>(x), x1 = *reinterpret_cast<const float4 *>(x + 4);
@@ -331,9 +336,58 @@ struct GemvArgs {
     const float *X;
     int nb, nsl, ng_total;
     long long units;  // nb * ng_total
+    TpExchange tp;    // row-parallel exchange (tp.world > 1), single tensor only
 };
 
 extern __shared__ __align__(1024) uint8_t g_smem[];
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_sys(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Row-parallel exchange of one output row (layout and protocol: TpExchange). Each 8-byte entry carries the value and
+// its tag in one single-copy-atomic store, so an entry that reads as tagged holds its value: no flag, no fence. Returns
+// the sum over ranks in rank order (the same bits on every rank); on a wait past the deadline or a mismatched tag it
+// sets the device error word (bit 3 / bit 4) and the row's result is invalid.
+__device__ __forceinline__ float tp_exchange_row(const TpExchange &x, unsigned int par, int row, float y,
+                                                 unsigned long long deadline, bool &ok) {
+    const unsigned long long v = ((unsigned long long)x.tag << 32) | __float_as_uint(y);
+    const long long sec = (long long)par * x.world;
+    for (int q = 0; q < x.world; ++q)
+        if (q != x.rank) st_relaxed_sys(x.peer[q] + (sec + x.rank) * x.cap + row, v);
+    float s = 0.f;
+    for (int q = 0; q < x.world; ++q) {
+        float yq = y;
+        if (q != x.rank) {
+            unsigned long long *p = x.peer[x.rank] + (sec + q) * x.cap + row;
+            unsigned long long e = ok ? ld_relaxed_sys(p) : 0ull;
+            while (ok && (unsigned int)(e >> 32) == 0u) {
+                if (global_ns() > deadline) {
+                    atomicOr(&g_p8_device_error, 8u);
+                    ok = false;
+                    break;
+                }
+                __nanosleep(32);
+                e = ld_relaxed_sys(p);
+            }
+            if (ok && (unsigned int)(e >> 32) != x.tag) atomicOr(&g_p8_device_error, 16u);
+            if (ok) *p = 0ull;  // consumed; the peer writes this half again two calls later
+            yq = __uint_as_float((unsigned int)e);
+        }
+        s = q == 0 ? yq : __fadd_rn(s, yq);
+    }
+    return s;
+}
 
 // table byte address of the chunk at step k: PRMT places the field byte (k % 4 of word k / 4) in bits 8-15 and the
 // lane's rotated chunk offset ((lane + k) & 31) * 4 (byte k % 3 of po[k / 3]; po byte 3 is zero) in bits 0-7.
@@ -667,6 +721,10 @@ __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
     // in block order with all of its loads in flight, then the first R threads add the S slice sums in slice order.
     // The split depends only on the launch shape, so the result is deterministic.
     float *red = reinterpret_cast<float *>(g_smem + kSmemT0);  // the table buffers are free now
+    const bool tpx = a.tp.world > 1;
+    const unsigned int par = tpx ? (__ldcg(a.tp.epoch) & 1u) : 0u;  // advanced by the prep kernel of this call
+    const unsigned long long deadline = tpx ? global_ns() + a.tp.timeout_ns : 0ull;
+    bool tp_ok = true;
     const int b_lo = a.nb * sl / S, b_hi = a.nb * (sl + 1) / S;
     for (int base = r0; base < r1; base += R) {
         const int rt = base + rl;
@@ -711,6 +769,7 @@ __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
             }
             const GemvTensor &T = a.t[c_ti];
             for (int e = c_e0; e < c_e1; ++e) y = __fadd_rn(y, __fmul_rn(T.cv[e], a.X[T.cc[e]]));
+            if (tpx) y = tp_exchange_row(a.tp, par, c_ro, y, deadline, tp_ok);
             T.Y[c_ro] = y;
         }
         __syncthreads();
@@ -768,7 +827,7 @@ static int sm_count() {
 
 // one column: prep + persistent GEMV over the group
 static p8_status launch_gemv_col(const p8_tensor *const *ts, int nt, const float *x, float *const *Ys, void *ws, size_t ws_bytes,
-                                 cudaStream_t st) {
+                                 cudaStream_t st, const TpExchange *tp = nullptr, unsigned int *epoch = nullptr) {
     const p8_tensor *t0 = ts[0];
     const GemvWs L = gemv_ws_layout(ts, nt);
     if (!ws || ws_bytes < L.total) return P8_ERR_WORKSPACE;
@@ -781,8 +840,10 @@ static p8_status launch_gemv_col(const p8_tensor *const *ts, int nt, const float
     pa.G = reinterpret_cast<int *>(w + L.G);
     pa.d = reinterpret_cast<float *>(w + L.d);
     pa.arrive = reinterpret_cast<unsigned int *>(w + L.arrive);
+    pa.epoch = tp ? epoch : nullptr;
     GemvArgs ga;
     memset(&ga, 0, sizeof(ga));
+    if (tp) ga.tp = *tp;
     ga.ntensors = nt; ga.T = pa.T; ga.G = pa.G; ga.d = pa.d; ga.X = x; ga.nb = t0->nb; ga.nsl = t0->nsl;
     ga.arrive = pa.arrive;
     size_t poff = L.part;
@@ -830,6 +891,13 @@ p8_status launch_gemv_group(const p8_tensor *const *ts, int nt, const float *X, 
 p8_status launch_gemv(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy, void *ws, size_t ws_bytes,
                       cudaStream_t st) {
     return launch_gemv_group(&t, 1, X, ncols, ldx, &Y, &ldy, ws, ws_bytes, st);
+}
+
+p8_status launch_gemv_tp(const p8_tensor *t, const float *x, float *y, const TpExchange &tp, unsigned int *epoch, void *ws,
+                         size_t ws_bytes, cudaStream_t st) {
+    (void)sm_count();
+    if (tp.world < 2) return launch_gemv_col(&t, 1, x, &y, ws, ws_bytes, st);
+    return launch_gemv_col(&t, 1, x, &y, ws, ws_bytes, st, &tp, epoch);
 }
 
 unsigned int read_and_clear_device_error() {

@@ -71,6 +71,19 @@ class P8Tensor:
         check(lib().p8_mul_mat_vec(self.handle, _ptr(x), _ptr(y), _ptr(ws), ws.numel(), _stream(stream)), "p8_mul_mat_vec")
         return y
 
+    def mul_mat_vec_allreduce(self, x, comm, out=None, workspace=None, stream=None):
+        """y = sum over the ranks of comm of (rank's shard) x (rank's x): this tensor is the rank's row-parallel shard
+        (p8_tp_shard_cols), x its input slice; the partial rows are exchanged inside the GEMV (p8_tp_gemv_allreduce).
+        Every rank gets the same y (sum in rank order)."""
+        x = x.contiguous()
+        if x.dtype != torch.float32 or x.numel() != self.K or not x.is_cuda:
+            raise ValueError("x must be float32 CUDA with K elements")
+        y = out if out is not None else torch.empty(self.rows, dtype=torch.float32, device=x.device)
+        ws = workspace if workspace is not None else self.workspace(1)
+        check(lib().p8_tp_gemv_allreduce(self.handle, _ptr(x), _ptr(y), comm.handle, _ptr(ws), ws.numel(), _stream(stream)),
+              "p8_tp_gemv_allreduce")
+        return y
+
     def mul_mat(self, X, out=None, workspace=None, stream=None):
         """Y = X W^T: X float32 [ncols, K] -> Y float32 [ncols, rows] (ggml dst [rows, ncols]).
 

@@ -7,13 +7,16 @@ between the two projections of a pair:
                                        (p8_tp_shard_rows: rows re-tiled, lane rotation remapped); its output is the
                                        rank's slice of y, consumed locally (attention heads, SwiGLU).
   row-parallel    (o, down)            rank i holds the 256-column blocks of its input slice (p8_tp_shard_cols); its
-                                       output is a partial y over all rows, summed over ranks by an all-reduce
-                                       (NCCL over NVLink on the GPU path).
+                                       output is a partial y over all rows, summed over ranks either inside the GEMV
+                                       (TpComm: p8_tp_gemv_allreduce, the epilogue stores the partial rows into the
+                                       peers' exchange buffers over NVLink and sums the ranks' rows in rank order) or
+                                       by an NCCL all-reduce after it.
 
 Split units keep the pairs consistent: q and o's input in units of two heads (256 columns, o's K-shards must be
 whole 256-column blocks), k/v in single KV heads (query heads of rank i use KV heads of rank i under GQA), gate/up
 and down's input in 256-row units. Uneven counts are spread by a balanced contiguous split.
 """
+import ctypes as C
 from dataclasses import dataclass
 
 import numpy as np
@@ -112,6 +115,113 @@ def reduce_partials(y, group=None):
     return y
 
 
+class TpComm:
+    """This rank's exchange buffer for fused row-parallel calls (p8_tp_comm_*): rank of world (<= 8) on the current
+    device, up to max_rows output rows per call, device waits bounded by timeout_ms. connect() makes one per rank of a
+    process group and maps every peer's buffer (CUDA IPC handles exchanged through the group)."""
+
+    def __init__(self, rank, world, max_rows, timeout_ms=1000):
+        from ._lib import check, lib
+
+        h = C.c_void_p()
+        check(lib().p8_tp_comm_create(rank, world, max_rows, timeout_ms, C.byref(h)), "p8_tp_comm_create")
+        self._h = h
+        self.rank, self.world, self.max_rows, self.timeout_ms = rank, world, max_rows, timeout_ms
+
+    @classmethod
+    def connect(cls, max_rows, group=None, timeout_ms=1000):
+        import torch.distributed as dist
+
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        c = cls(rank, world, max_rows, timeout_ms)
+        info = [None] * world
+        dist.all_gather_object(info, (world, max_rows, c.ipc_handle()), group=group)
+        if any(w != world or m != max_rows for w, m, _ in info):
+            c.close()
+            raise ValueError("TpComm.connect: ranks asked for different world sizes or max_rows")
+        for q, (_, _, hnd) in enumerate(info):
+            if q != rank:
+                c.open_peer(q, hnd)
+        return c
+
+    @property
+    def handle(self):
+        from ._lib import P8Error
+
+        if self._h is None:
+            raise P8Error(-1, "TpComm closed")
+        return self._h
+
+    def ipc_handle(self):
+        from ._lib import check, lib
+
+        buf = C.create_string_buffer(64)
+        check(lib().p8_tp_comm_ipc_handle(self.handle, buf, 64), "p8_tp_comm_ipc_handle")
+        return buf.raw
+
+    def open_peer(self, q, ipc_handle):
+        from ._lib import check, lib
+
+        check(lib().p8_tp_comm_open_peer(self.handle, q, C.c_char_p(bytes(ipc_handle)), len(ipc_handle)),
+              "p8_tp_comm_open_peer")
+
+    def set_peer(self, q, dev_ptr):
+        """attach peer q's buffer by device address (one process, or a local stand-in buffer)"""
+        from ._lib import check, lib
+
+        check(lib().p8_tp_comm_set_peer(self.handle, q, C.c_void_p(int(dev_ptr))), "p8_tp_comm_set_peer")
+
+    def buffer(self):
+        """this rank's exchange buffer as an int64 CUDA tensor [2, world, max_rows] (entry layout: p8_tp_gemv_allreduce)"""
+        import torch
+
+        from ._lib import check, lib
+
+        p, n = C.c_void_p(), C.c_size_t()
+        check(lib().p8_tp_comm_buffer(self.handle, C.byref(p), C.byref(n)), "p8_tp_comm_buffer")
+        shape = (2, self.world, self.max_rows)
+        owner = self
+
+        class _View:
+            __cuda_array_interface__ = {"shape": shape, "typestr": "<i8", "data": (p.value, False), "version": 3}
+            keep = owner
+
+        return torch.as_tensor(_View(), device="cuda")
+
+    def epoch(self):
+        """fused calls made so far on this communicator"""
+        from ._lib import check, lib
+
+        e = C.c_uint32()
+        check(lib().p8_tp_comm_epoch(self.handle, C.byref(e)), "p8_tp_comm_epoch")
+        return e.value
+
+    def reset(self, stream=None):
+        """zero the buffer and the call count (after a failed exchange: every rank, between steps)"""
+        from ._lib import check, lib
+        from .ops import _stream
+
+        check(lib().p8_tp_comm_reset(self.handle, _stream(stream)), "p8_tp_comm_reset")
+
+    def close(self):
+        if getattr(self, "_h", None) is not None:
+            from ._lib import lib
+
+            lib().p8_tp_comm_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def entry_tag(rows):
+    """high word of a filled exchange entry for a tensor of `rows` rows"""
+    return 0x80000000 | int(rows)
+
+
 class ColumnParallel:
     """this rank's rows of a column-parallel projection: y_local = W[lo:hi] x"""
 
@@ -133,9 +243,12 @@ class ColumnParallel:
 
 
 class RowParallel:
-    """this rank's input columns of a row-parallel projection: y = all_reduce_sum(W[:, lo:hi] x[lo:hi])"""
+    """this rank's input columns of a row-parallel projection: y = all_reduce_sum(W[:, lo:hi] x[lo:hi]).
 
-    def __init__(self, slot, K, rows, world, rank, unit=256, device="cuda", group=None):
+    With comm (a TpComm of the group) the sum happens inside the GEMV (p8_tp_gemv_allreduce); every rank must then
+    hold input columns (world <= K / unit), else the NCCL all-reduce after the GEMV is used on every rank."""
+
+    def __init__(self, slot, K, rows, world, rank, unit=256, device="cuda", group=None, comm=None):
         import torch
 
         from .ops import P8Tensor
@@ -144,8 +257,12 @@ class RowParallel:
         self.lo, self.hi = self.shard.lo, self.shard.hi
         self.group = group
         self.t = P8Tensor(torch.from_numpy(self.shard.slot).to(device), self.shard.K, rows) if self.shard.K else None
+        # the same decision on every rank: it depends only on K, unit and world
+        self.comm = comm if comm is not None and world <= K // unit and world > 1 else None
 
     def __call__(self, x_local, out=None, workspace=None, stream=None):
+        if self.comm is not None:
+            return self.t.mul_mat_vec_allreduce(x_local, self.comm, out=out, workspace=workspace, stream=stream)
         if self.t is None:  # no input columns on this rank: contribute zeros to the sum
             import torch
 

@@ -187,3 +187,17 @@ def test_synthetic_slots_valid_and_decodable():
         o = Oracle(s, rows, K)
         W = o.dequant()
         assert np.isfinite(W).all() and o.nd == 5
+
+
+def test_tp_comm_create_checks_arguments_before_touching_the_device():
+    """p8_tp_comm_create refuses bad rank / world / rows / timeout with P8_ERR_ARG (no CUDA call is made for them)."""
+    from pingala8_llm_b200._lib import lib
+
+    h = C.c_void_p()
+    for rank, world, rows, tmo in [(0, 0, 64, 100), (0, 9, 64, 100), (2, 2, 64, 100), (-1, 2, 64, 100), (0, 2, 0, 100),
+                                   (0, 2, 1 << 25, 100), (0, 2, 64, 0), (0, 2, 64, 600001)]:
+        assert lib().p8_tp_comm_create(rank, world, rows, tmo, C.byref(h)) == -1, (rank, world, rows, tmo)
+        assert not h.value
+    assert lib().p8_tp_comm_create(0, 2, 64, 100, None) == -1
+    assert lib().p8_tp_comm_destroy(None) == -1
+    assert lib().p8_tp_gemv_allreduce(None, None, None, None, None, 0, None) == -12
