@@ -233,7 +233,9 @@ def run_b200(args, rank, world, local_rank):
         ts = {}
         for i, (nm, _, _) in enumerate(shapes):
             rows, K = local[nm]
-            slot = synth.make_slot_device(rows, K, seed=1000 * L + 17 * i + 7919 * rank, device=dev)
+            # a row-parallel shard keeps its tensor's row order on every rank (as p8_tp_shard_cols shards do)
+            perm_seed = 1000 * L + 17 * i + 31 if plan[nm][0] == "row" else None
+            slot = synth.make_slot_device(rows, K, seed=1000 * L + 17 * i + 7919 * rank, device=dev, perm_seed=perm_seed)
             ts[nm] = P8Tensor(slot, K, rows)
         layers.append(ts)
     groups = [("q", "k", "v"), ("o",), ("gate", "up"), ("down",)]  # tensors of a group read the same x
@@ -283,6 +285,10 @@ def run_b200(args, rank, world, local_rank):
     torch.cuda.synchronize()
 
     def barrier():
+        # the device is idle before the collective: a collective kernel that waits for other ranks must never share
+        # the GPU with the persistent GEMV (its CTAs could keep a GEMV CTA from becoming resident while that GEMV's
+        # peers wait for it in the fused exchange)
+        torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()

@@ -159,13 +159,18 @@ p8_status p8_tp_shard_cols(const uint8_t *slot, size_t nbytes, int64_t K, int64_
  * sums the ranks' values in rank order, so every rank gets the same bits. A wait is bounded by the communicator's
  * timeout; past it the launch gives up, p8_device_error reports bit 3 (8), the result is invalid and every rank must
  * p8_tp_comm_reset its communicator (between steps, then a host barrier) before the next call. An entry whose tag
- * names another row count (the ranks called different tensors) sets bit 4 (16).
+ * names another row count or another original row (the ranks called different tensors, or shards whose row order
+ * differs) sets bit 4 (16).
  *
- * Exchange buffer of rank r: 2 * world * max_rows u64 entries; entry (parity s, source rank q, output row i) at index
- * (s * world + q) * max_rows + i holds ((0x80000000 | rows) << 32) | float bits of rank q's partial y[i]; 0 = empty.
+ * Exchange buffer of rank r: 2 * world * max_rows u64 entries; entry (parity s, source rank q, sorted row i) at index
+ * (s * world + q) * max_rows + i holds (tag << 32) | float bits of rank q's partial y[prm[i]], tag = 0x80000000 |
+ * prm[i] << 16 | rows / 32 (prm: the slot's row permutation, sorted -> original row); 0 = empty.
  * Parity s = the communicator's call count & 1 (the first call is 1). Peers' buffers must have the same world and
  * max_rows. All ranks make the same sequence of p8_tp_gemv_allreduce calls on their communicators, each with its
- * column shard of one tensor (same rows); a rank with no columns cannot take part (use a collective instead). */
+ * column shard of one tensor (same rows); a rank with no columns cannot take part (use a collective instead).
+ * The GEMV is a persistent kernel (one CTA per SM, all resident): while a fused call may be in flight, run no other
+ * kernel on the GPU that waits for other ranks (an NCCL collective on another stream): its CTAs can keep a GEMV CTA
+ * from becoming resident while the peers' GEMVs wait for this rank. Synchronise the device before such a collective. */
 typedef struct p8_tp_comm p8_tp_comm;
 #define P8_IPC_HANDLE_BYTES 64
 /* rank of world (1..8) on the current device, up to max_rows output rows per call, waits bounded by timeout_ms */

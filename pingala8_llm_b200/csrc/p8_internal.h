@@ -66,8 +66,10 @@ p8_status launch_gemv_group(const p8_tensor *const *ts, int nt, const float *X, 
 p8_status launch_gemv(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy, void *ws,
                       size_t ws_bytes, cudaStream_t st);
 // Fused row-parallel exchange of the GEMV epilogue (one-shot all-reduce over peer memory). Every rank owns an exchange
-// buffer of u64 entries: entry (parity s, source rank q, output row r) at index (s * world + q) * cap + r holds
-// (tag << 32) | float bits of rank q's partial y[r], 0 when empty. A rank stores its partials into every peer's buffer
+// buffer of u64 entries: entry (parity s, source rank q, sorted row i) at index (s * world + q) * cap + i holds
+// (tag << 32) | float bits of rank q's partial y[prm[i]], 0 when empty; tag = 0x80000000 | prm[i] << 16 | rows / 32.
+// Indexing by sorted row keeps a warp's 32 entries contiguous (one coalesced write per peer), and the original row in
+// the tag checks that the ranks' shards share the row order. A rank stores its partials into every peer's buffer
 // (plain 8-byte stores over NVLink), then polls its own buffer for the peers' partials (bounded by timeout_ns), sums
 // the ranks' values in rank order and clears the entries it consumed. The parity s = epoch & 1 alternates per call, so
 // a rank one call ahead writes the other half while a slow peer still reads this one.
@@ -77,7 +79,7 @@ struct TpExchange {
     const unsigned int *epoch;              // this rank's call counter, advanced by the call's prep kernel
     long long cap;                          // output rows per (parity, rank) section
     unsigned long long timeout_ns;
-    unsigned int tag;                       // 0x80000000 | rows: an entry with another non-zero tag is a mismatch
+    unsigned int tag_rows;                  // rows / 32 (tag bits 0-15); an entry with another non-zero tag is a mismatch
     int rank, world;
 };
 p8_status launch_gemv_tp(const p8_tensor *t, const float *x, float *y, const TpExchange &tp, unsigned int *epoch, void *ws,

@@ -356,33 +356,52 @@ __device__ __forceinline__ unsigned long long global_ns() {
 }
 
 // Row-parallel exchange of one output row (layout and protocol: TpExchange). Each 8-byte entry carries the value and
-// its tag in one single-copy-atomic store, so an entry that reads as tagged holds its value: no flag, no fence. Returns
-// the sum over ranks in rank order (the same bits on every rank); on a wait past the deadline or a mismatched tag it
-// sets the device error word (bit 3 / bit 4) and the row's result is invalid.
-__device__ __forceinline__ float tp_exchange_row(const TpExchange &x, unsigned int par, int row, float y,
+// its tag in one single-copy-atomic store, so an entry that reads as tagged holds its value: no flag, no fence. The
+// peers' entries are loaded together (one round trip for all ranks) and only the missing ones are polled again.
+// Returns the sum over ranks in rank order (the same bits on every rank); on a wait past the deadline or a mismatched
+// tag it sets the device error word (bit 3 / bit 4) and the row's result is invalid.
+__device__ __forceinline__ float tp_exchange_row(const TpExchange &x, unsigned int par, int row, int orig_row, float y,
                                                  unsigned long long deadline, bool &ok) {
-    const unsigned long long v = ((unsigned long long)x.tag << 32) | __float_as_uint(y);
+    const unsigned int tag = 0x80000000u | ((unsigned int)orig_row << 16) | x.tag_rows;
+    const unsigned long long v = ((unsigned long long)tag << 32) | __float_as_uint(y);
     const long long sec = (long long)par * x.world;
-    for (int q = 0; q < x.world; ++q)
-        if (q != x.rank) st_relaxed_sys(x.peer[q] + (sec + x.rank) * x.cap + row, v);
+#pragma unroll
+    for (int q = 0; q < kTpMaxWorld; ++q)
+        if (q < x.world && q != x.rank) st_relaxed_sys(x.peer[q] + (sec + x.rank) * x.cap + row, v);
+    unsigned long long *own = x.peer[x.rank] + sec * x.cap + row;
+    unsigned long long e[kTpMaxWorld];
+    unsigned int missing = 0;  // bit q: rank q's entry not seen yet
+#pragma unroll
+    for (int q = 0; q < kTpMaxWorld; ++q) {
+        e[q] = 0ull;
+        if (ok && q < x.world && q != x.rank) e[q] = ld_relaxed_sys(own + q * x.cap);
+    }
+#pragma unroll
+    for (int q = 0; q < kTpMaxWorld; ++q)
+        if (q < x.world && q != x.rank && (unsigned int)(e[q] >> 32) == 0u) missing |= 1u << q;
+    while (ok && missing) {
+        if (global_ns() > deadline) {
+            atomicOr(&g_p8_device_error, 8u);
+            ok = false;
+            break;
+        }
+        __nanosleep(32);
+#pragma unroll
+        for (int q = 0; q < kTpMaxWorld; ++q)
+            if ((missing >> q) & 1u) {
+                e[q] = ld_relaxed_sys(own + q * x.cap);
+                if ((unsigned int)(e[q] >> 32) != 0u) missing &= ~(1u << q);
+            }
+    }
     float s = 0.f;
-    for (int q = 0; q < x.world; ++q) {
+#pragma unroll
+    for (int q = 0; q < kTpMaxWorld; ++q) {
+        if (q >= x.world) break;
         float yq = y;
         if (q != x.rank) {
-            unsigned long long *p = x.peer[x.rank] + (sec + q) * x.cap + row;
-            unsigned long long e = ok ? ld_relaxed_sys(p) : 0ull;
-            while (ok && (unsigned int)(e >> 32) == 0u) {
-                if (global_ns() > deadline) {
-                    atomicOr(&g_p8_device_error, 8u);
-                    ok = false;
-                    break;
-                }
-                __nanosleep(32);
-                e = ld_relaxed_sys(p);
-            }
-            if (ok && (unsigned int)(e >> 32) != x.tag) atomicOr(&g_p8_device_error, 16u);
-            if (ok) *p = 0ull;  // consumed; the peer writes this half again two calls later
-            yq = __uint_as_float((unsigned int)e);
+            if (ok && (unsigned int)(e[q] >> 32) != tag) atomicOr(&g_p8_device_error, 16u);
+            if (ok) own[q * x.cap] = 0ull;  // consumed; the peer writes this half again two calls later
+            yq = __uint_as_float((unsigned int)e[q]);
         }
         s = q == 0 ? yq : __fadd_rn(s, yq);
     }
@@ -522,6 +541,8 @@ struct WarpCursor {
     int b, rr;  // current unit (256-column block, row tile of the group); exhausted once past the CTA's range
 };
 
+// TPX: the row-parallel exchange in the epilogue (a separate instantiation, so the plain GEMV carries none of it)
+template <bool TPX>
 __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint64_t *bar = reinterpret_cast<uint64_t *>(g_smem + kSmemBar);
@@ -721,7 +742,7 @@ __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
     // in block order with all of its loads in flight, then the first R threads add the S slice sums in slice order.
     // The split depends only on the launch shape, so the result is deterministic.
     float *red = reinterpret_cast<float *>(g_smem + kSmemT0);  // the table buffers are free now
-    const bool tpx = a.tp.world > 1;
+    constexpr bool tpx = TPX;
     const unsigned int par = tpx ? (__ldcg(a.tp.epoch) & 1u) : 0u;  // advanced by the prep kernel of this call
     const unsigned long long deadline = tpx ? global_ns() + a.tp.timeout_ns : 0ull;
     bool tp_ok = true;
@@ -769,7 +790,7 @@ __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
             }
             const GemvTensor &T = a.t[c_ti];
             for (int e = c_e0; e < c_e1; ++e) y = __fadd_rn(y, __fmul_rn(T.cv[e], a.X[T.cc[e]]));
-            if (tpx) y = tp_exchange_row(a.tp, par, c_ro, y, deadline, tp_ok);
+            if (tpx) y = tp_exchange_row(a.tp, par, rt2, c_ro, y, deadline, tp_ok);
             T.Y[c_ro] = y;
         }
         __syncthreads();
@@ -820,7 +841,8 @@ static int sm_count() {
         int v = 0;
         cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
         n[dev] = v > 0 ? v : 148;
-        cudaFuncSetAttribute(k_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
+        cudaFuncSetAttribute(k_gemv<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
+        cudaFuncSetAttribute(k_gemv<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
     }
     return n[dev];
 }
@@ -867,7 +889,8 @@ static p8_status launch_gemv_col(const p8_tensor *const *ts, int nt, const float
     }
     const unsigned grid = (unsigned)(ga.units < nsm ? ga.units : nsm);
     void *args[] = {&ga};
-    if (launch_pdl((const void *)k_gemv, dim3(grid), dim3(kGemvThreads), kGemvSmem, st, args) != cudaSuccess) return P8_ERR_CUDA;
+    const void *fn = tp ? (const void *)k_gemv<true> : (const void *)k_gemv<false>;
+    if (launch_pdl(fn, dim3(grid), dim3(kGemvThreads), kGemvSmem, st, args) != cudaSuccess) return P8_ERR_CUDA;
     return P8_OK;
 }
 

@@ -135,7 +135,7 @@ p8_status p8_tp_gemv_allreduce(const p8_tensor *t, const float *x, float *y, p8_
     tp.epoch = c->epoch;
     tp.cap = c->cap;
     tp.timeout_ns = c->timeout_ns;
-    tp.tag = 0x80000000u | (uint32_t)t->rows;
+    tp.tag_rows = (uint32_t)t->rows >> 5;
     tp.rank = c->rank;
     tp.world = c->world;
     return launch_gemv_tp(t, x, y, tp, c->epoch, workspace, workspace_bytes, (cudaStream_t)stream);

@@ -61,11 +61,12 @@ def make_slot(rows, K, classes=3, seed=0, nd=0, permute=True, c16=None, sigma=0.
     return fmt.assemble_slot(kb, rows, K, c16, prm, drow, dcol, dval, SIGNS)
 
 
-def make_slot_device(rows, K, classes=3, seed=0, device="cuda", nd=0, permute=True):
+def make_slot_device(rows, K, classes=3, seed=0, device="cuda", nd=0, permute=True, perm_seed=None):
     """Like make_slot, but the random payload is drawn on the GPU (fast for model-size tensors).
 
     The header, M, S and side data are built on the host from a payload-free copy and the payload words are filled
-    on the device, so a 15 MB tensor costs ~1 ms of host work.
+    on the device, so a 15 MB tensor costs ~1 ms of host work. perm_seed (optional) draws the row permutation from its
+    own seed, so slots made with different seeds can share a row order (the column shards of one tensor do).
     """
     import torch
 
@@ -78,6 +79,8 @@ def make_slot_device(rows, K, classes=3, seed=0, device="cuda", nd=0, permute=Tr
     od = fmt.off_d(rows, K)
     kb[od:] = 0
     prm = rng.permutation(rows).astype(np.int16) if permute else None
+    if permute and perm_seed is not None:
+        prm = np.random.default_rng(perm_seed).permutation(rows).astype(np.int16)
     if nd:
         flat = np.sort(rng.choice(rows * K, size=nd, replace=False))
         drow, dcol = (flat // K).astype(np.uint16), (flat % K).astype(np.uint16)

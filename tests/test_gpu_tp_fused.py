@@ -15,20 +15,23 @@ pytestmark = pytest.mark.gpu
 if not torch.cuda.is_available():
     pytest.skip("needs a CUDA GPU", allow_module_level=True)
 
-from pingala8_llm_b200 import synth, tp  # noqa: E402
+from pingala8_llm_b200 import fmt, synth, tp  # noqa: E402
 from pingala8_llm_b200.ops import P8Tensor, device_error  # noqa: E402
 from oracle.oracle import Oracle  # noqa: E402
 
 
+PRM = {}
+
+
 def _entries(y, rows):
-    """exchange entries (int64 bit patterns) of partial rows y"""
-    bits = y.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
-    tag = (tp.entry_tag(rows) << 32) - (1 << 64)  # the same 64 bits as a signed int64
-    return bits | tag
+    """exchange entries (sorted-row order, int64 bit patterns) of partial output y of the tensor set up last"""
+    return tp.exchange_entries(y, PRM["prm"], rows)
 
 
 def _setup(rows, K, world, seed=3, nd=11):
     slot = synth.make_slot(rows, K, seed=seed, nd=nd)
+    PRM["prm"] = fmt.split_kernel_bytes(slot, K, rows)[2]  # shards keep the tensor's row order
+    assert sorted(PRM["prm"].tolist()) == list(range(rows)) and PRM["prm"].tolist() != list(range(rows))
     x = np.random.default_rng(seed).normal(0, 1, K).astype(np.float32)
     shards = [tp.row_shard(slot, K, rows, world, q) for q in range(world)]
     ts = [P8Tensor(s.slot, s.K, rows) for s in shards]
@@ -143,6 +146,12 @@ def test_fused_foreign_tag_is_reported():
     peer1 = torch.zeros(2, world, rows + 32, dtype=torch.int64, device="cuda")
     comm.set_peer(1, peer1.data_ptr())
     comm.buffer()[1, 1, :rows] = _entries(parts[1], rows + 32)  # written for a tensor of another row count
+    ts[0].mul_mat_vec_allreduce(xs[0], comm)
+    torch.cuda.synchronize()
+    assert device_error() & 16
+    comm.reset()
+    e = _entries(parts[1], rows)
+    comm.buffer()[1, 1, :rows] = torch.roll(e, 1)  # a peer whose shard has another row order
     ts[0].mul_mat_vec_allreduce(xs[0], comm)
     torch.cuda.synchronize()
     assert device_error() & 16
