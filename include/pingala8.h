@@ -82,6 +82,26 @@ size_t p8_workspace_size_group(const p8_tensor *const *ts, int n, int64_t ncols)
 p8_status p8_mul_mat_vec_group(const p8_tensor *const *ts, int n, const float *x, float *const *ys, void *workspace,
                                size_t workspace_bytes, void *stream);
 
+/* Activation prologue fused into the GEMV's activation prep, for the op that produces a projection's input in a
+ * llama-style layer (each a separate ggml op, and kernel, in the reference):
+ *   P8_PROLOGUE_RMSNORM  x' = (x * scale) * w, scale = 1 / sqrt(sum(x^2) / K + eps)   (ggml rms_norm, then mul by the
+ *                        norm weight w[K]; the q/k/v and gate/up inputs)
+ *   P8_PROLOGUE_SWIGLU   x' = x / (1 + exp(-x)) * x2                                    (ggml swiglu: silu(gate) * up
+ *                        with x = gate, x2 = up[K]; the down projection's input)
+ * x' is computed in fp32 and is what the GEMV multiplies (clamp-delta term included); it is not written back. The
+ * stock llama.cpp fuses the GLU into its own quantized GEMV (ggml_cuda_should_fuse_mul_mat_vec_q); the reference turns
+ * that off for Pingala-8 tensors (CU:1319-1321). */
+typedef enum p8_prologue_kind { P8_PROLOGUE_NONE = 0, P8_PROLOGUE_RMSNORM = 1, P8_PROLOGUE_SWIGLU = 2 } p8_prologue_kind;
+typedef struct p8_prologue {
+    int kind;          /* p8_prologue_kind */
+    const float *w;    /* RMSNORM: norm weight [K] (16-byte aligned) */
+    const float *x2;   /* SWIGLU: up [K] (16-byte aligned) */
+    float eps;         /* RMSNORM */
+} p8_prologue;
+/* p8_mul_mat_vec_group with a prologue (pro NULL or kind NONE: the plain call); workspace as p8_workspace_size_group */
+p8_status p8_mul_mat_vec_group_ex(const p8_tensor *const *ts, int n, const float *x, const p8_prologue *pro, float *const *ys,
+                                  void *workspace, size_t workspace_bytes, void *stream);
+
 /* y = W x like p8_mul_mat_vec, but with no workspace argument and no allocation: the scratch is a fixed 6 MiB device
  * array inside the library, for callers that cannot allocate device memory at call time and have no buffer to lend
  * (e.g. a host framework that plans all device memory up front). No counterpart in the reference (its GEMV takes

@@ -32,6 +32,14 @@ class P8Error(RuntimeError):
 _LIB = None
 
 _vp, _sz, _i64, _u32 = C.c_void_p, C.c_size_t, C.c_int64, C.c_uint32
+
+
+class Prologue(C.Structure):
+    """p8_prologue: activation prologue of p8_mul_mat_vec_group_ex (kind 0 none, 1 RMSNorm with w and eps, 2 SwiGLU
+    with x2 = up)"""
+    _fields_ = [("kind", C.c_int), ("w", C.c_void_p), ("x2", C.c_void_p), ("eps", C.c_float)]
+
+
 _SIGS = {
     "p8_prepare": (C.c_int, [_vp, _sz, _i64, _i64, _vp, C.POINTER(_vp)]),
     "p8_release": (C.c_int, [_vp]),
@@ -41,6 +49,7 @@ _SIGS = {
     "p8_mul_mat_vec": (C.c_int, [_vp, _vp, _vp, _vp, _sz, _vp]),
     "p8_workspace_size_group": (_sz, [_vp, C.c_int, _i64]),
     "p8_mul_mat_vec_group": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, _sz, _vp]),
+    "p8_mul_mat_vec_group_ex": (C.c_int, [_vp, C.c_int, _vp, C.POINTER(Prologue), _vp, _vp, _sz, _vp]),
     "p8_noalloc_scratch_bytes": (_sz, []),
     "p8_mul_mat_vec_noalloc": (C.c_int, [_vp, _vp, _vp, _vp]),
     "p8_mul_mat": (C.c_int, [_vp, _vp, _i64, _i64, _vp, _i64, _vp, _sz, _vp]),

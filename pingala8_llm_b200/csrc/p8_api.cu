@@ -218,6 +218,25 @@ p8_status p8_mul_mat_vec_group(const p8_tensor *const *ts, int n, const float *x
     return launch_gemv_group(ts, n, x, 1, ts[0]->K, ys, ld, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
+p8_status p8_mul_mat_vec_group_ex(const p8_tensor *const *ts, int n, const float *x, const p8_prologue *pro, float *const *ys,
+                                  void *workspace, size_t workspace_bytes, void *stream) {
+    if (!ts || !ys || n < 1 || n > 4 || !x || ((uintptr_t)x & 15)) return P8_ERR_ARG;
+    for (int i = 0; i < n; ++i) {
+        if (!valid(ts[i])) return P8_ERR_NOT_PREPARED;
+        if (!ys[i]) return P8_ERR_ARG;
+    }
+    if (pro) {
+        if (pro->kind == P8_PROLOGUE_RMSNORM) {
+            if (!pro->w || ((uintptr_t)pro->w & 15) || !(pro->eps >= 0.f)) return P8_ERR_ARG;
+        } else if (pro->kind == P8_PROLOGUE_SWIGLU) {
+            if (!pro->x2 || ((uintptr_t)pro->x2 & 15)) return P8_ERR_ARG;
+        } else if (pro->kind != P8_PROLOGUE_NONE) {
+            return P8_ERR_ARG;
+        }
+    }
+    return launch_gemv_group_pro(ts, n, x, pro, ys, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
 p8_status p8_mul_mat(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy, void *workspace,
                      size_t workspace_bytes, void *stream) {
     if (!valid(t)) return P8_ERR_NOT_PREPARED;

@@ -65,6 +65,8 @@ p8_status launch_gemv_group(const p8_tensor *const *ts, int nt, const float *X, 
                             const int64_t *ldys, void *ws, size_t ws_bytes, cudaStream_t st);
 p8_status launch_gemv(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy, void *ws,
                       size_t ws_bytes, cudaStream_t st);
+p8_status launch_gemv_group_pro(const p8_tensor *const *ts, int nt, const float *x, const p8_prologue *pro, float *const *Ys,
+                                void *ws, size_t ws_bytes, cudaStream_t st);
 // Fused row-parallel exchange of the GEMV epilogue (one-shot all-reduce over peer memory). Every rank owns an exchange
 // buffer of u64 entries: entry (parity s, source rank q, sorted row i) at index (s * world + q) * cap + i holds
 // (tag << 32) | float bits of rank q's partial y[prm[i]], 0 when empty; tag = 0x80000000 | prm[i] << 16 | rows / 32.

@@ -260,12 +260,42 @@ struct PrepArgs {
     float *d;   // [nsl]
     unsigned int *arrive;  // the GEMV's grid-barrier counter
     unsigned int *epoch;   // row-parallel exchange: the call counter to advance (nullptr without an exchange)
+    // activation prologue (PRO != P8_PROLOGUE_NONE): x' from x and w (RMSNorm weight) or x2 (SwiGLU up), written to xv
+    const float *pw, *x2;
+    float eps;
+    float *xv;
 };
 
+// x'[i] = (x[i] * scale) * w[i], scale = 1 / sqrt(mean(x^2) + eps): ggml's rms_norm (sum of squares, mean by float
+// division, 1 / sqrtf) followed by the weight multiply. Every CTA sums the whole vector in the same fixed order
+// (per-thread strided float4 sums, then a shared-memory tree), so all CTAs get the same scale.
+__device__ __forceinline__ float rms_scale(const float *x, int K, float eps, float *red) {
+    const int tid = threadIdx.x;
+    float ss = 0.f;
+    for (int k = 4 * tid; k < K; k += 4 * 256) {
+        const float4 v = *reinterpret_cast<const float4 *>(x + k);
+        ss = __fmaf_rn(v.x, v.x, ss);
+        ss = __fmaf_rn(v.y, v.y, ss);
+        ss = __fmaf_rn(v.z, v.z, ss);
+        ss = __fmaf_rn(v.w, v.w, ss);
+    }
+    red[tid] = ss;
+    __syncthreads();
+#pragma unroll
+    for (int h = 128; h > 0; h >>= 1) {
+        if (tid < h) red[tid] = __fadd_rn(red[tid], red[tid + h]);
+        __syncthreads();
+    }
+    const float mean = __fdiv_rn(red[0], (float)K);
+    return __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, eps)));
+}
+
+template <int PRO>
 __global__ void __launch_bounds__(256) k_act_prep(PrepArgs a) {
     __shared__ int q_s[256];
     __shared__ uint32_t A_s[32];
     __shared__ int cx_s[64];
+    __shared__ float red_s[PRO == P8_PROLOGUE_RMSNORM ? 256 : 1];
     const int b = blockIdx.x, fg = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
     pdl_launch_dependents();
     if (tid < 32) A_s[tid] = a.A[32 * fg + tid];
@@ -280,9 +310,29 @@ __global__ void __launch_bounds__(256) k_act_prep(PrepArgs a) {
         *a.arrive = 0u;
         if (a.epoch) *a.epoch += 1u;  // the GEMV reads it after this kernel completes
     }
+    float scale = 1.f;
+    if (PRO == P8_PROLOGUE_RMSNORM) scale = rms_scale(a.X, a.K, a.eps, red_s);
     if (tid < 32) {
         const float *x = a.X + b * 256 + 8 * lane;
-        const float4 x0 = *reinterpret_cast<const float4 *>(x), x1 = *reinterpret_cast<const float4 *>(x + 4);
+        float4 x0 = *reinterpret_cast<const float4 *>(x), x1 = *reinterpret_cast<const float4 *>(x + 4);
+        if (PRO == P8_PROLOGUE_RMSNORM) {
+            const float4 w0 = *reinterpret_cast<const float4 *>(a.pw + b * 256 + 8 * lane);
+            const float4 w1 = *reinterpret_cast<const float4 *>(a.pw + b * 256 + 8 * lane + 4);
+            x0 = make_float4(__fmul_rn(__fmul_rn(x0.x, scale), w0.x), __fmul_rn(__fmul_rn(x0.y, scale), w0.y),
+                             __fmul_rn(__fmul_rn(x0.z, scale), w0.z), __fmul_rn(__fmul_rn(x0.w, scale), w0.w));
+            x1 = make_float4(__fmul_rn(__fmul_rn(x1.x, scale), w1.x), __fmul_rn(__fmul_rn(x1.y, scale), w1.y),
+                             __fmul_rn(__fmul_rn(x1.z, scale), w1.z), __fmul_rn(__fmul_rn(x1.w, scale), w1.w));
+        } else if (PRO == P8_PROLOGUE_SWIGLU) {  // silu(gate) * up = gate / (1 + exp(-gate)) * up
+            const float4 u0 = *reinterpret_cast<const float4 *>(a.x2 + b * 256 + 8 * lane);
+            const float4 u1 = *reinterpret_cast<const float4 *>(a.x2 + b * 256 + 8 * lane + 4);
+            auto sw = [](float g, float u) { return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u); };
+            x0 = make_float4(sw(x0.x, u0.x), sw(x0.y, u0.y), sw(x0.z, u0.z), sw(x0.w, u0.w));
+            x1 = make_float4(sw(x1.x, u1.x), sw(x1.y, u1.y), sw(x1.z, u1.z), sw(x1.w, u1.w));
+        }
+        if (PRO != P8_PROLOGUE_NONE && fg == 0) {  // x' for the GEMV's clamp-delta term
+            *reinterpret_cast<float4 *>(a.xv + b * 256 + 8 * lane) = x0;
+            *reinterpret_cast<float4 *>(a.xv + b * 256 + 8 * lane + 4) = x1;
+        }
         float v[8] = {__fmul_rn(x0.x, i0.x), __fmul_rn(x0.y, i0.y), __fmul_rn(x0.z, i0.z), __fmul_rn(x0.w, i0.w),
                       __fmul_rn(x1.x, i1.x), __fmul_rn(x1.y, i1.y), __fmul_rn(x1.z, i1.z), __fmul_rn(x1.w, i1.w)};
         fwht256_warp(v, lane);
@@ -799,7 +849,7 @@ __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
 
 // workspace layout (bytes, each part 256-aligned): T | G | d | partials ([nb][rows] per tensor)
 struct GemvWs {
-    size_t T, G, d, arrive, part, total;
+    size_t T, G, d, arrive, xv, part, total;
 };
 static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
 static GemvWs gemv_ws_layout(const p8_tensor *const *ts, int nt) {
@@ -811,7 +861,8 @@ static GemvWs gemv_ws_layout(const p8_tensor *const *ts, int nt) {
     w.G = w.T + al256((size_t)t->nb * kTabBytes);
     w.d = w.G + al256((size_t)t->nsl * kGInts * 4);
     w.arrive = w.d + al256((size_t)t->nsl * 4);
-    w.part = w.arrive + 256;
+    w.xv = w.arrive + 256;
+    w.part = w.xv + al256((size_t)t->K * 4);
     w.total = w.part + part;
     return w;
 }
@@ -849,7 +900,8 @@ static int sm_count() {
 
 // one column: prep + persistent GEMV over the group
 static p8_status launch_gemv_col(const p8_tensor *const *ts, int nt, const float *x, float *const *Ys, void *ws, size_t ws_bytes,
-                                 cudaStream_t st, const TpExchange *tp = nullptr, unsigned int *epoch = nullptr) {
+                                 cudaStream_t st, const TpExchange *tp = nullptr, unsigned int *epoch = nullptr,
+                                 const p8_prologue *pro = nullptr) {
     const p8_tensor *t0 = ts[0];
     const GemvWs L = gemv_ws_layout(ts, nt);
     if (!ws || ws_bytes < L.total) return P8_ERR_WORKSPACE;
@@ -863,10 +915,18 @@ static p8_status launch_gemv_col(const p8_tensor *const *ts, int nt, const float
     pa.d = reinterpret_cast<float *>(w + L.d);
     pa.arrive = reinterpret_cast<unsigned int *>(w + L.arrive);
     pa.epoch = tp ? epoch : nullptr;
+    const int pk = pro ? pro->kind : P8_PROLOGUE_NONE;
+    if (pk != P8_PROLOGUE_NONE) {
+        pa.pw = pro->w;
+        pa.x2 = pro->x2;
+        pa.eps = pro->eps;
+        pa.xv = reinterpret_cast<float *>(w + L.xv);
+    }
     GemvArgs ga;
     memset(&ga, 0, sizeof(ga));
     if (tp) ga.tp = *tp;
-    ga.ntensors = nt; ga.T = pa.T; ga.G = pa.G; ga.d = pa.d; ga.X = x; ga.nb = t0->nb; ga.nsl = t0->nsl;
+    ga.ntensors = nt; ga.T = pa.T; ga.G = pa.G; ga.d = pa.d; ga.X = pk != P8_PROLOGUE_NONE ? pa.xv : x; ga.nb = t0->nb;
+    ga.nsl = t0->nsl;
     ga.arrive = pa.arrive;
     size_t poff = L.part;
     int g0 = 0;
@@ -885,7 +945,10 @@ static p8_status launch_gemv_col(const p8_tensor *const *ts, int nt, const float
     ga.units = (long long)g0 * t0->nb;
     {
         void *args[] = {&pa};
-        if (launch_pdl((const void *)k_act_prep, dim3(t0->nb, 8), dim3(256), 0, st, args) != cudaSuccess) return P8_ERR_CUDA;
+        const void *fn = pk == P8_PROLOGUE_RMSNORM ? (const void *)k_act_prep<P8_PROLOGUE_RMSNORM>
+                         : pk == P8_PROLOGUE_SWIGLU  ? (const void *)k_act_prep<P8_PROLOGUE_SWIGLU>
+                                                     : (const void *)k_act_prep<P8_PROLOGUE_NONE>;
+        if (launch_pdl(fn, dim3(t0->nb, 8), dim3(256), 0, st, args) != cudaSuccess) return P8_ERR_CUDA;
     }
     const unsigned grid = (unsigned)(ga.units < nsm ? ga.units : nsm);
     void *args[] = {&ga};
@@ -909,6 +972,15 @@ p8_status launch_gemv_group(const p8_tensor *const *ts, int nt, const float *X, 
         if (s) return s;
     }
     return P8_OK;
+}
+
+p8_status launch_gemv_group_pro(const p8_tensor *const *ts, int nt, const float *x, const p8_prologue *pro, float *const *Ys,
+                                void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (nt < 1 || nt > kMaxGroup) return P8_ERR_ARG;
+    for (int i = 0; i < nt; ++i)
+        if (ts[i]->K != ts[0]->K || ts[i]->act_hash != ts[0]->act_hash) return P8_ERR_ARG;
+    (void)sm_count();
+    return launch_gemv_col(ts, nt, x, Ys, ws, ws_bytes, st, nullptr, nullptr, pro);
 }
 
 p8_status launch_gemv(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy, void *ws, size_t ws_bytes,

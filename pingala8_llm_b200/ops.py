@@ -140,19 +140,34 @@ def group_workspace_size(tensors, ncols=1):
     return int(lib().p8_workspace_size_group(arr, len(tensors), ncols))
 
 
-def mul_mat_vec_group(tensors, x, outs=None, workspace=None, stream=None):
-    """y_i = W_i x for tensors sharing x (q/k/v, gate/up): one prepared activation, one launch (<= 4 tensors)."""
+def mul_mat_vec_group(tensors, x, outs=None, workspace=None, stream=None, norm_weight=None, eps=1e-5, up=None):
+    """y_i = W_i x for tensors sharing x (q/k/v, gate/up): one prepared activation, one launch (<= 4 tensors).
+
+    Fused activation prologue (p8_mul_mat_vec_group_ex): norm_weight -> the tensors multiply RMSNorm(x) * norm_weight
+    (eps as ggml's rms_norm); up -> they multiply silu(x) * up (x = the gate output)."""
     x = x.contiguous()
     if x.dtype != torch.float32 or not x.is_cuda or x.numel() != tensors[0].K:
         raise ValueError("x must be float32 CUDA with K elements")
+    if norm_weight is not None and up is not None:
+        raise ValueError("one prologue per call: norm_weight or up")
     outs = outs if outs is not None else [torch.empty(t.rows, dtype=torch.float32, device=x.device) for t in tensors]
     n = len(tensors)
     arr = (C.c_void_p * n)(*[t.handle.value for t in tensors])
     ys = (C.c_void_p * n)(*[o.data_ptr() for o in outs])
     if workspace is None:
         workspace = torch.empty(max(group_workspace_size(tensors), 256), dtype=torch.uint8, device=x.device)
-    check(lib().p8_mul_mat_vec_group(arr, n, _ptr(x), ys, _ptr(workspace), workspace.numel(), _stream(stream)),
-          "p8_mul_mat_vec_group")
+    if norm_weight is None and up is None:
+        check(lib().p8_mul_mat_vec_group(arr, n, _ptr(x), ys, _ptr(workspace), workspace.numel(), _stream(stream)),
+              "p8_mul_mat_vec_group")
+        return outs
+    from ._lib import Prologue
+
+    extra = norm_weight if norm_weight is not None else up
+    if extra.dtype != torch.float32 or not extra.is_cuda or not extra.is_contiguous() or extra.numel() != tensors[0].K:
+        raise ValueError("norm_weight / up must be contiguous float32 CUDA with K elements")
+    pro = Prologue(1, extra.data_ptr(), None, float(eps)) if norm_weight is not None else Prologue(2, None, extra.data_ptr(), 0.0)
+    check(lib().p8_mul_mat_vec_group_ex(arr, n, _ptr(x), C.byref(pro), ys, _ptr(workspace), workspace.numel(),
+                                        _stream(stream)), "p8_mul_mat_vec_group_ex")
     return outs
 
 
