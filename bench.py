@@ -352,6 +352,59 @@ def run_b200(args, rank, world, local_rank):
         nbytes = sum(algo_bytes_gemv(*dims[n]) for n in grp) - 4 * dims[grp[0]][1] * (len(grp) - 1)
         per_group["+".join(grp)] = (call_s, nbytes)
         del gg
+    # ---- (1 GPU) the projections with the elementwise ops that produce their inputs in a llama layer: RMSNorm x
+    # weight -> q/k/v, o, RMSNorm x weight -> gate/up, SwiGLU -> down; fused into the GEMV's activation prep
+    # (p8_mul_mat_vec_group_ex) vs the same ops as separate torch kernels before the plain GEMV. One graph per variant.
+    layer = None
+    if world == 1 and not args.no_layer:
+        eps = 1e-5
+        nw = [torch.rand(h, device=dev) + 0.5 for _ in range(2)]
+
+        def layer_fused(stream):
+            x = buf["x"]
+            for ts in layers:
+                mul_mat_vec_group([ts[n] for n in ("q", "k", "v")], x, outs=[buf[n] for n in ("q", "k", "v")], workspace=ws,
+                                  stream=stream, norm_weight=nw[0], eps=eps)
+                mul_mat_vec_group([ts["o"]], buf["q"], outs=[buf["o"]], workspace=ws, stream=stream)
+                mul_mat_vec_group([ts["gate"], ts["up"]], buf["o"], outs=[buf["gate"], buf["up"]], workspace=ws,
+                                  stream=stream, norm_weight=nw[1], eps=eps)
+                mul_mat_vec_group([ts["down"]], buf["gate"], outs=[buf["down"]], workspace=ws, stream=stream, up=buf["up"])
+                x = buf["down"]
+
+        def layer_torch(stream):
+            x = buf["x"]
+            for ts in layers:
+                xn = (x * torch.rsqrt(torch.mean(x * x) + eps)) * nw[0]
+                mul_mat_vec_group([ts[n] for n in ("q", "k", "v")], xn, outs=[buf[n] for n in ("q", "k", "v")], workspace=ws,
+                                  stream=stream)
+                mul_mat_vec_group([ts["o"]], buf["q"], outs=[buf["o"]], workspace=ws, stream=stream)
+                on = (buf["o"] * torch.rsqrt(torch.mean(buf["o"] * buf["o"]) + eps)) * nw[1]
+                mul_mat_vec_group([ts["gate"], ts["up"]], on, outs=[buf["gate"], buf["up"]], workspace=ws, stream=stream)
+                mul_mat_vec_group([ts["down"]], torch.nn.functional.silu(buf["gate"]) * buf["up"], outs=[buf["down"]],
+                                  workspace=ws, stream=stream)
+                x = buf["down"]
+
+        layer = {}
+        for name, fn in (("fused", layer_fused), ("torch_ops", layer_torch)):
+            gl = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                fn(stream)
+                torch.cuda.synchronize()
+                with torch.cuda.graph(gl, stream=stream):
+                    fn(stream)
+            for _ in range(3):
+                gl.replay()
+            torch.cuda.synchronize()
+            el0, el1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            nrep = max(10, args.steps // 2)
+            el0.record(stream)
+            with torch.cuda.stream(stream):
+                for _ in range(nrep):
+                    gl.replay()
+            el1.record(stream)
+            torch.cuda.synchronize()
+            layer[name] = el0.elapsed_time(el1) / 1e3 / nrep
+            del gl
     # ---- prefill (batched product, tcgen05 GEMM) at 1 GPU: 512 tokens through every projection of all 32 layers
     # (1.80 GB of weights per pass, larger than L2), one CUDA graph per pass, device-timed
     prefill = None
@@ -432,6 +485,12 @@ def run_b200(args, rank, world, local_rank):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),
     }
+    if layer is not None:
+        line["layer_prologues"] = {
+            "ops": "RMSNorm*w -> q,k,v; o; RMSNorm*w -> gate,up; SwiGLU -> down (x 32 layers, graph-replayed, device-timed)",
+            "fused_tok_s": round(1.0 / layer["fused"], 1), "torch_ops_tok_s": round(1.0 / layer["torch_ops"], 1),
+            "fused": "p8_mul_mat_vec_group_ex (prologue in k_act_prep)",
+            "torch_ops": "separate torch elementwise/reduction kernels, then p8_mul_mat_vec_group"}
     if prefill is not None:
         ntok, t_pass, flop = prefill
         bf16_peak = measured_bf16_tflops()
@@ -457,6 +516,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-prefill", action="store_true", help="skip the batched-product (prefill) measurement")
+    ap.add_argument("--no-layer", action="store_true", help="skip the fused-prologue layer measurement")
     ap.add_argument("--tp-exchange", default="fused", choices=["fused", "nccl"],
                     help="row-parallel sum for N > 1: inside the GEMV over peer memory, or an NCCL all-reduce after it")
     args = ap.parse_args()
