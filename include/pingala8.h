@@ -212,6 +212,27 @@ p8_status p8_tp_comm_reset(p8_tp_comm *c, void *stream);
 p8_status p8_tp_gemv_allreduce(const p8_tensor *t, const float *x, float *y, p8_tp_comm *c, void *workspace,
                                size_t workspace_bytes, void *stream);
 
+/* ---------------------------------------------------------------- offline encoder ------------------------------- */
+
+/* One 128-column slice of the trellis encoder (the reference's LDLQ Viterbi, research/detail/r48k.py encode / vit_k /
+ * best_cw / zero_ldlq, r48k.py:33-120, trellis mode with 8 states) for all rows, on the GPU. Device pointers unless
+ * noted; row r of each array at base + r * ld:
+ *   X    [rows][128] f32   the slice of the FWHT-domain weights after the earlier slices' error feedback
+ *   Hb   [128][128]  f32   the slice's diagonal block of the upper Cholesky factor Uc (Hi = Uc^T Uc)
+ *   A4   [32][4][4]  f32   inverses of Hb's diagonal 4 x 4 blocks (row-major)
+ *   codebook [256][4] i8   the codebook A (header bytes 0..1023); coset: 4 i8 in HOST memory
+ *   cls  u8 per row (stride ldc), S f32 per row (stride lds): the class and scale of the row's 256-column block
+ *   Q    [rows][128] f32   out: quantised values (integer codeword x S); E [rows][128] f32 out: the errors in the
+ *        A4-transformed metric (the caller subtracts E @ Uc[slice, later columns] from the later columns)
+ *   IDX  [rows][32][3] u8  out: (f1, f2, f3) per 4-weight step (rows of class 0 are not written)
+ * workspace: p8_encode_workspace() bytes (16-byte aligned). Rows are independent and the result is deterministic;
+ * codes equal the reference's except where two candidates' metrics differ only in their last bits. */
+size_t p8_encode_workspace(void);
+p8_status p8_encode_slice(const float *X, int64_t ldx, const float *Hb, int64_t ldh, const float *A4, const int8_t *codebook,
+                          const int8_t *coset, const uint8_t *cls, int64_t ldc, const float *S, int64_t lds, int64_t rows, float *Q,
+                          int64_t ldq, float *E, int64_t lde, uint8_t *IDX, int64_t ldi, void *workspace, size_t workspace_bytes,
+                          void *stream);
+
 /* ---------------------------------------------------------------- model files (GGUF) ---------------------------- */
 
 /* A GGUF file holding a Pingala-8 ("VR native") model, opened and checked as llama_model_loader::vr_native_init does

@@ -81,6 +81,9 @@ _SIGS = {
     "p8_tp_comm_epoch": (C.c_int, [_vp, C.POINTER(_u32)]),
     "p8_tp_comm_reset": (C.c_int, [_vp, _vp]),
     "p8_tp_gemv_allreduce": (C.c_int, [_vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "p8_encode_workspace": (_sz, []),
+    "p8_encode_slice": (C.c_int, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i64, _vp,
+                                  _i64, _vp, _sz, _vp]),
     "p8_device_error": (C.c_int, []),
     "p8_status_str": (C.c_char_p, [C.c_int]),
     "p8_build_info": (C.c_char_p, []),

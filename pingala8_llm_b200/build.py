@@ -10,7 +10,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libpingala8_b200.so")
-SOURCES = ["p8_host.cpp", "p8_gguf.cpp", "p8_api.cu", "p8_kernels.cu", "p8_noalloc.cu", "p8_tp.cu"]
+SOURCES = ["p8_host.cpp", "p8_gguf.cpp", "p8_api.cu", "p8_kernels.cu", "p8_noalloc.cu", "p8_tp.cu", "p8_encode.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
