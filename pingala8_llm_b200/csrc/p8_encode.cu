@@ -102,6 +102,7 @@ __device__ __forceinline__ void best_cw(const float (&xa)[4], const float *TAt, 
     if (NST(C) == 1) {
         float best = INFINITY;
         int bi = H * hs;
+#pragma unroll 8
         for (int m = 0; m < hs; ++m) {
             const int i = H * hs + m;
             const float d = dist4(xa, ta_at(TAt, i), sc1);
@@ -113,6 +114,7 @@ __device__ __forceinline__ void best_cw(const float (&xa)[4], const float *TAt, 
     }
     float v1[4] = {INFINITY, INFINITY, INFINITY, INFINITY};
     int t1i[4] = {H * hs, H * hs, H * hs, H * hs};
+#pragma unroll 8
     for (int m = 0; m < hs; ++m) {
         const int i = H * hs + m;
         top4_insert(v1, t1i, dist4(xa, ta_at(TAt, i), sc1), i);
@@ -128,6 +130,7 @@ __device__ __forceinline__ void best_cw(const float (&xa)[4], const float *TAt, 
         if (NST(C) == 2) {
             float c2 = INFINITY;
             int j2 = 0;
+#pragma unroll 8
             for (int i = 0; i < K2; ++i) {
                 const float d = dist4(r1, ta_at(TAt, i), sc2);
                 if (d < c2) { c2 = d; j2 = i; }
@@ -136,6 +139,7 @@ __device__ __forceinline__ void best_cw(const float (&xa)[4], const float *TAt, 
         } else {
             float v2[4] = {INFINITY, INFINITY, INFINITY, INFINITY};
             int t2i[4] = {0, 0, 0, 0};
+#pragma unroll 8
             for (int i = 0; i < K2; ++i) top4_insert(v2, t2i, dist4(r1, ta_at(TAt, i), sc2), i);
             constexpr int K3 = 1 << W3(C);
 #pragma unroll 1
@@ -145,6 +149,7 @@ __device__ __forceinline__ void best_cw(const float (&xa)[4], const float *TAt, 
                                      __fsub_rn(r1[2], __fmul_rn(sc2, b.z)), __fsub_rn(r1[3], __fmul_rn(sc2, b.w))};
                 float c3 = INFINITY;
                 int j3 = 0;
+#pragma unroll 8
                 for (int i = 0; i < K3; ++i) {
                     const float d = dist4(r2, ta_at(TAt, i), 1.f);
                     if (d < c3) { c3 = d; j3 = i; }
