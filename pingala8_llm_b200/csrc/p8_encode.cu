@@ -408,10 +408,12 @@ p8_status p8_encode_slice(const float *X, int64_t ldx, const float *Hb, int64_t 
     a.lds = lds; a.rows = (int)rows; a.Q = Q; a.ldq = ldq; a.E = E; a.lde = lde; a.IDX = IDX; a.ldi = ldi;
     for (int k = 0; k < 4; ++k) a.cvec[k] = (float)coset[k];
     const size_t smem = sizeof(RowSmem) * kVitRowsPerCta;
-    static bool attr = false;
-    if (!attr) {
+    static bool attr[64] = {false};  // the attribute is per device
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return P8_ERR_CUDA;
+    if (dev < 0 || dev >= 64 || !attr[dev]) {
         if (cudaFuncSetAttribute(k_vit, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return P8_ERR_CUDA;
-        attr = true;
+        if (dev >= 0 && dev < 64) attr[dev] = true;
     }
     const unsigned grid = (unsigned)((rows + kVitRowsPerCta - 1) / kVitRowsPerCta);
     k_vit<<<grid, 128, smem, st>>>(a);
