@@ -101,6 +101,12 @@ typedef struct p8_prologue {
 /* p8_mul_mat_vec_group with a prologue (pro NULL or kind NONE: the plain call); workspace as p8_workspace_size_group */
 p8_status p8_mul_mat_vec_group_ex(const p8_tensor *const *ts, int n, const float *x, const p8_prologue *pro, float *const *ys,
                                   void *workspace, size_t workspace_bytes, void *stream);
+/* p8_mul_mat (prefill / batched) with a prologue applied to every token: RMSNORM per token (its own sum of squares)
+ * with the shared weight w[K]; SWIGLU with up rows at pro->x2 + n * ldx. Workspace p8_workspace_size_ex(t, ncols, kind)
+ * (the tcgen05 path keeps x' [ncols][K] f32 for the clamp-delta term). */
+size_t p8_workspace_size_ex(const p8_tensor *t, int64_t ncols, int kind);
+p8_status p8_mul_mat_ex(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, const p8_prologue *pro, float *Y,
+                        int64_t ldy, void *workspace, size_t workspace_bytes, void *stream);
 
 /* y = W x like p8_mul_mat_vec, but with no workspace argument and no allocation: the scratch is a fixed 6 MiB device
  * array inside the library, for callers that cannot allocate device memory at call time and have no buffer to lend

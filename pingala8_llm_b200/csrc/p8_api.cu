@@ -245,6 +245,44 @@ p8_status p8_mul_mat(const p8_tensor *t, const float *X, int64_t ncols, int64_t 
     return launch_gemv(t, X, ncols, ldx, Y, ldy, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
+size_t p8_workspace_size_ex(const p8_tensor *t, int64_t ncols, int kind) {
+    if (!valid(t) || ncols <= 0) return 0;
+    size_t w = gemv_workspace(t, ncols);
+    if (gemm_supported(t, ncols)) {
+        const size_t g = gemm_workspace(t, ncols, kind != P8_PROLOGUE_NONE);
+        if (g > w) w = g;
+    }
+    return w;
+}
+
+p8_status p8_mul_mat_ex(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, const p8_prologue *pro, float *Y,
+                        int64_t ldy, void *workspace, size_t workspace_bytes, void *stream) {
+    if (!valid(t)) return P8_ERR_NOT_PREPARED;
+    if (!X || !Y || ncols <= 0 || ldx < t->K || ldy < t->rows || ((uintptr_t)X & 15) || (ldx & 3)) return P8_ERR_ARG;
+    if (pro) {
+        if (pro->kind == P8_PROLOGUE_RMSNORM) {
+            if (!pro->w || ((uintptr_t)pro->w & 15) || !(pro->eps >= 0.f)) return P8_ERR_ARG;
+        } else if (pro->kind == P8_PROLOGUE_SWIGLU) {
+            if (!pro->x2 || ((uintptr_t)pro->x2 & 15)) return P8_ERR_ARG;
+        } else if (pro->kind != P8_PROLOGUE_NONE) {
+            return P8_ERR_ARG;
+        }
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    if (gemm_supported(t, ncols)) return launch_gemm(t, X, ncols, ldx, Y, ldy, workspace, workspace_bytes, s, pro);
+    for (int64_t n = 0; n < ncols; ++n) {  // below the GEMM's column count: the batch-1 GEMV per column
+        p8_prologue pn;
+        if (pro) {
+            pn = *pro;
+            if (pn.x2) pn.x2 += n * ldx;
+        }
+        float *yn = Y + n * ldy;
+        const p8_status st = launch_gemv_group_pro(&t, 1, X + n * ldx, pro ? &pn : nullptr, &yn, workspace, workspace_bytes, s);
+        if (st) return st;
+    }
+    return P8_OK;
+}
+
 p8_status p8_get_rows(const p8_tensor *t, const int32_t *ids, int64_t n, float *out, int64_t ldo, void *stream) {
     if (!valid(t)) return P8_ERR_NOT_PREPARED;
     if (n < 0 || (n && (!ids || !out)) || ldo < t->K || ((uintptr_t)out & 15) || (ldo & 3)) return P8_ERR_ARG;

@@ -83,7 +83,21 @@ struct GxArgs {
     int K, nb, ncols, npad, nkc;
     unsigned int *kcnt;    // split-K tile counters to zero (or null)
     int ncnt;
+    // activation prologue (k_gx_*<PRO>, PRO != P8_PROLOGUE_NONE): x' per token from x and w (RMSNorm weight [K]) or
+    // x2 (SwiGLU up, [ncols][ldx]); ss [npad][nkc] partial sums of squares; x' f32 to xv [npad][K] for the delta term
+    const float *pw, *x2;
+    float eps;
+    float *ss, *xv;
 };
+
+// the prologue's x' of one element (x = the input, w / u = the weight or up value, scale = the token's RMSNorm scale),
+// the same formulas as the batch-1 prep: (x * scale) * w, or x / (1 + exp(-x)) * u
+template <int PRO>
+__device__ __forceinline__ float pro_val(float x, float wu, float scale) {
+    if (PRO == P8_PROLOGUE_RMSNORM) return __fmul_rn(__fmul_rn(x, scale), wu);
+    if (PRO == P8_PROLOGUE_SWIGLU) return __fmul_rn(__fdiv_rn(x, __fadd_rn(1.f, expf(-x))), wu);
+    return x;
+}
 
 // ---------------------------------------------------------------------------------------------------------------
 // tcgen05 / TMEM wrappers (PTX ISA 8.6+, sm_100a)
@@ -144,34 +158,63 @@ __global__ void __launch_bounds__(256) k_row_scale(const uint16_t *S, int rows, 
 
 // ---------------------------------------------------------------------------------------------------------------
 // activation prep
+template <int PRO>
 __global__ void __launch_bounds__(256) k_gx_max(const GxArgs a) {
     pdl_launch_dependents();
     pdl_wait();
     __shared__ float red[8];
+    __shared__ float red2[8];
     if (a.kcnt) {  // the GEMM's split-K tile counters start each call at zero
         for (int i = (blockIdx.y * gridDim.x + blockIdx.x) * 256 + threadIdx.x; i < a.ncnt; i += gridDim.x * gridDim.y * 256)
             a.kcnt[i] = 0u;
     }
     const int n = blockIdx.x, col = blockIdx.y * 2048 + threadIdx.x * 8;
-    float m = 0.f;
+    float m = 0.f, sq = 0.f;
     if (n < a.ncols && col < a.K) {
         const float4 *xp = reinterpret_cast<const float4 *>(a.X + (size_t)n * a.ldx + col);
         const float4 *ip = reinterpret_cast<const float4 *>(a.ic + col);
-        const float4 x0 = xp[0], x1 = xp[1], i0 = ip[0], i1 = ip[1];
+        float4 x0 = xp[0], x1 = xp[1];
+        const float4 i0 = ip[0], i1 = ip[1];
+        if (PRO == P8_PROLOGUE_RMSNORM) {  // sum of squares of x; the bound uses x * w (the scale is a positive scalar)
+            const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) sq = __fmaf_rn(xs[e], xs[e], sq);
+            const float4 w0 = *reinterpret_cast<const float4 *>(a.pw + col), w1 = *reinterpret_cast<const float4 *>(a.pw + col + 4);
+            x0 = make_float4(x0.x * w0.x, x0.y * w0.y, x0.z * w0.z, x0.w * w0.w);
+            x1 = make_float4(x1.x * w1.x, x1.y * w1.y, x1.z * w1.z, x1.w * w1.w);
+        } else if (PRO == P8_PROLOGUE_SWIGLU) {
+            const float4 *up = reinterpret_cast<const float4 *>(a.x2 + (size_t)n * a.ldx + col);
+            const float4 u0 = up[0], u1 = up[1];
+            x0 = make_float4(pro_val<PRO>(x0.x, u0.x, 1.f), pro_val<PRO>(x0.y, u0.y, 1.f), pro_val<PRO>(x0.z, u0.z, 1.f),
+                             pro_val<PRO>(x0.w, u0.w, 1.f));
+            x1 = make_float4(pro_val<PRO>(x1.x, u1.x, 1.f), pro_val<PRO>(x1.y, u1.y, 1.f), pro_val<PRO>(x1.z, u1.z, 1.f),
+                             pro_val<PRO>(x1.w, u1.w, 1.f));
+        }
         m = fmaxf(fmaxf(fmaxf(fabsf(x0.x * i0.x), fabsf(x0.y * i0.y)), fmaxf(fabsf(x0.z * i0.z), fabsf(x0.w * i0.w))),
                   fmaxf(fmaxf(fabsf(x1.x * i1.x), fabsf(x1.y * i1.y)), fmaxf(fabsf(x1.z * i1.z), fabsf(x1.w * i1.w))));
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+    if (PRO == P8_PROLOGUE_RMSNORM) {  // fixed-order tree: the same partial sums on every call
+#pragma unroll
+        for (int o = 16; o; o >>= 1) sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, o));
+        if ((threadIdx.x & 31) == 0) red2[threadIdx.x >> 5] = sq;
+    }
     __syncthreads();
     if (threadIdx.x == 0) {
         float v = red[0];
         for (int i = 1; i < 8; ++i) v = fmaxf(v, red[i]);
         a.pmax[(size_t)n * a.nkc + blockIdx.y] = v;
+        if (PRO == P8_PROLOGUE_RMSNORM) {
+            float t = red2[0];
+            for (int i = 1; i < 8; ++i) t = __fadd_rn(t, red2[i]);
+            a.ss[(size_t)n * a.nkc + blockIdx.y] = t;
+        }
     }
 }
 
+template <int PRO>
 __global__ void __launch_bounds__(256) k_gx_prep(const GxArgs a) {
     pdl_launch_dependents();
     pdl_wait();
@@ -180,6 +223,13 @@ __global__ void __launch_bounds__(256) k_gx_prep(const GxArgs a) {
     float m = lane < a.nkc ? a.pmax[(size_t)n * a.nkc + lane] : 0.f;
 #pragma unroll
     for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float scale = 1.f;
+    if (PRO == P8_PROLOGUE_RMSNORM) {  // 1 / sqrt(sum(x^2) / K + eps), chunk sums added in chunk order
+        float t = 0.f;
+        for (int y = 0; y < a.nkc; ++y) t = __fadd_rn(t, a.ss[(size_t)n * a.nkc + y]);
+        scale = __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)a.K), a.eps)));
+        m = m * scale;  // the bound of |x' * sgn/c| (the 2 spare bits of the fp16 range absorb its rounding)
+    }
     // |Xr| <= 16 max|x * sgn/c| < 16 * 2^e  ->  tau = 10 - e gives |Xr * 2^tau| < 2^14
     int tau = 0;
     if (m > 0.f && m <= 3.0e38f) tau = min(126, max(-126, 10 - exp_above(m)));
@@ -193,7 +243,19 @@ __global__ void __launch_bounds__(256) k_gx_prep(const GxArgs a) {
         if (n < a.ncols) {
             const float4 *xp = reinterpret_cast<const float4 *>(a.X + (size_t)n * a.ldx + b * 256 + 8 * lane);
             const float4 *ip = reinterpret_cast<const float4 *>(a.ic + b * 256 + 8 * lane);
-            const float4 x0 = xp[0], x1 = xp[1], i0 = ip[0], i1 = ip[1];
+            float4 x0 = xp[0], x1 = xp[1];
+            const float4 i0 = ip[0], i1 = ip[1];
+            if (PRO != P8_PROLOGUE_NONE) {
+                const float *wu = PRO == P8_PROLOGUE_RMSNORM ? a.pw + b * 256 + 8 * lane : a.x2 + (size_t)n * a.ldx + b * 256 + 8 * lane;
+                const float4 u0 = *reinterpret_cast<const float4 *>(wu), u1 = *reinterpret_cast<const float4 *>(wu + 4);
+                x0 = make_float4(pro_val<PRO>(x0.x, u0.x, scale), pro_val<PRO>(x0.y, u0.y, scale), pro_val<PRO>(x0.z, u0.z, scale),
+                                 pro_val<PRO>(x0.w, u0.w, scale));
+                x1 = make_float4(pro_val<PRO>(x1.x, u1.x, scale), pro_val<PRO>(x1.y, u1.y, scale), pro_val<PRO>(x1.z, u1.z, scale),
+                                 pro_val<PRO>(x1.w, u1.w, scale));
+                float4 *xo = reinterpret_cast<float4 *>(a.xv + (size_t)n * a.K + b * 256 + 8 * lane);  // x' for the delta term
+                xo[0] = x0;
+                xo[1] = x1;
+            }
             v[0] = __fmul_rn(x0.x, i0.x); v[1] = __fmul_rn(x0.y, i0.y); v[2] = __fmul_rn(x0.z, i0.z); v[3] = __fmul_rn(x0.w, i0.w);
             v[4] = __fmul_rn(x1.x, i1.x); v[5] = __fmul_rn(x1.y, i1.y); v[6] = __fmul_rn(x1.z, i1.z); v[7] = __fmul_rn(x1.w, i1.w);
         } else {
@@ -638,6 +700,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
 // host side
 struct GemmPlan {
     int bn, nbs, np, tileb, npad, nkc, mt, nnt, ks;
+    size_t ss, xv;  // prologue only: partial sums of squares [npad][nkc], x' [npad][K]
     size_t xh, pmax, tdown, kpart, kcnt, total, smem;
 };
 
@@ -648,7 +711,7 @@ static int gemm_tile_bytes(const p8_tensor *t) {  // staging bytes of one tile's
     return m * 128;
 }
 
-static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols) {
+static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols, bool pro = false) {
     const int nsm = sm_count();
     GemmPlan p;
     p.mt = (t->rows + 127) / 128;
@@ -686,6 +749,9 @@ static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols) {
     p.kpart = p.tdown + al256((size_t)p.npad * 4);
     p.kcnt = p.kpart + (p.ks > 1 ? al256((size_t)p.ks * p.npad * p.mt * 128 * 4) : 0);
     p.total = p.kcnt + (p.ks > 1 ? al256((size_t)base * 4) : 0);
+    p.ss = p.total;
+    p.xv = p.ss + (pro ? al256((size_t)p.npad * p.nkc * 4) : 0);
+    p.total = p.xv + (pro ? al256((size_t)p.npad * t->K * 4) : 0);
     return p;
 }
 
@@ -694,11 +760,12 @@ bool gemm_supported(const p8_tensor *t, int64_t ncols) {
            (size_t)gemm_plan(t, ncols).smem <= (size_t)kGemmSmemDyn;
 }
 
-size_t gemm_workspace(const p8_tensor *t, int64_t ncols) { return gemm_plan(t, ncols).total; }
+size_t gemm_workspace(const p8_tensor *t, int64_t ncols, bool pro) { return gemm_plan(t, ncols, pro).total; }
 
 p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy, void *ws,
-                      size_t ws_bytes, cudaStream_t st) {
-    const GemmPlan p = gemm_plan(t, ncols);
+                      size_t ws_bytes, cudaStream_t st, const p8_prologue *pro) {
+    const int pk = pro ? pro->kind : P8_PROLOGUE_NONE;
+    const GemmPlan p = gemm_plan(t, ncols, pk != P8_PROLOGUE_NONE);
     if (!ws || ws_bytes < p.total || ((uintptr_t)ws & 255)) return P8_ERR_WORKSPACE;
     if (p.smem > (size_t)kGemmSmemDyn) return P8_ERR_UNSUPPORTED;
     static bool attr_set[64] = {false};
@@ -711,6 +778,14 @@ p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t
     }
     uint8_t *w = static_cast<uint8_t *>(ws);
     GxArgs xa;
+    memset(&xa, 0, sizeof(xa));
+    if (pk != P8_PROLOGUE_NONE) {
+        xa.pw = pro->w;
+        xa.x2 = pro->x2;
+        xa.eps = pro->eps;
+        xa.ss = reinterpret_cast<float *>(w + p.ss);
+        xa.xv = reinterpret_cast<float *>(w + p.xv);
+    }
     xa.X = X; xa.ic = t->ic; xa.ldx = ldx; xa.K = t->K; xa.nb = t->nb; xa.ncols = (int)ncols; xa.npad = p.npad; xa.nkc = p.nkc;
     xa.Xh = w + p.xh;
     xa.pmax = reinterpret_cast<float *>(w + p.pmax);
@@ -719,13 +794,20 @@ p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t
     xa.ncnt = p.mt * p.nnt;
     {
         void *args[] = {&xa};
-        if (launch_pdl((const void *)k_gx_max, dim3(p.npad, p.nkc), dim3(256), 0, st, args) != cudaSuccess) return P8_ERR_CUDA;
-        if (launch_pdl((const void *)k_gx_prep, dim3(p.npad / 8, (t->nb + 3) / 4), dim3(256), 0, st, args) != cudaSuccess)
-            return P8_ERR_CUDA;
+        const void *fm = pk == P8_PROLOGUE_RMSNORM ? (const void *)k_gx_max<P8_PROLOGUE_RMSNORM>
+                         : pk == P8_PROLOGUE_SWIGLU  ? (const void *)k_gx_max<P8_PROLOGUE_SWIGLU>
+                                                     : (const void *)k_gx_max<P8_PROLOGUE_NONE>;
+        const void *fp = pk == P8_PROLOGUE_RMSNORM ? (const void *)k_gx_prep<P8_PROLOGUE_RMSNORM>
+                         : pk == P8_PROLOGUE_SWIGLU  ? (const void *)k_gx_prep<P8_PROLOGUE_SWIGLU>
+                                                     : (const void *)k_gx_prep<P8_PROLOGUE_NONE>;
+        if (launch_pdl(fm, dim3(p.npad, p.nkc), dim3(256), 0, st, args) != cudaSuccess) return P8_ERR_CUDA;
+        if (launch_pdl(fp, dim3(p.npad / 8, (t->nb + 3) / 4), dim3(256), 0, st, args) != cudaSuccess) return P8_ERR_CUDA;
     }
     GemmArgs ga;
     ga.A = t->A; ga.M = t->M; ga.D = t->D; ga.S = t->S; ga.prm = t->prm; ga.rsc = t->rsc; ga.cp = t->cp; ga.cc = t->cc;
-    ga.cv = t->cv; ga.X = X; ga.Y = Y; ga.Xh = xa.Xh; ga.tdown = xa.tdown; ga.ldx = ldx; ga.ldy = ldy; ga.cs = t->cs;
+    ga.cv = t->cv; ga.Y = Y; ga.Xh = xa.Xh; ga.tdown = xa.tdown; ga.ldy = ldy; ga.cs = t->cs;
+    ga.X = pk != P8_PROLOGUE_NONE ? xa.xv : X;  // the clamp-delta term multiplies x'
+    ga.ldx = pk != P8_PROLOGUE_NONE ? t->K : ldx;
     ga.rows = t->rows; ga.nb = t->nb; ga.ng = t->ng; ga.ncols = (int)ncols; ga.npad = p.npad; ga.bn = p.bn; ga.nbs = p.nbs;
     ga.np = p.np; ga.tileb = p.tileb; ga.ucls = t->uniform_class;
     ga.ksplit = p.ks; ga.mtr = p.mt * 128;

@@ -87,9 +87,9 @@ struct TpExchange {
 p8_status launch_gemv_tp(const p8_tensor *t, const float *x, float *y, const TpExchange &tp, unsigned int *epoch, void *ws,
                          size_t ws_bytes, cudaStream_t st);
 
-size_t gemm_workspace(const p8_tensor *t, int64_t ncols);
+size_t gemm_workspace(const p8_tensor *t, int64_t ncols, bool pro = false);
 p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy, void *ws,
-                      size_t ws_bytes, cudaStream_t st);
+                      size_t ws_bytes, cudaStream_t st, const p8_prologue *pro = nullptr);
 bool gemm_supported(const p8_tensor *t, int64_t ncols);
 p8_status gemm_prepare(p8_tensor *t, cudaStream_t st);  // prepare-time per-row scales (rsc)
 }  // namespace p8

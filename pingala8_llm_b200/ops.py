@@ -84,11 +84,12 @@ class P8Tensor:
               "p8_tp_gemv_allreduce")
         return y
 
-    def mul_mat(self, X, out=None, workspace=None, stream=None):
+    def mul_mat(self, X, out=None, workspace=None, stream=None, norm_weight=None, eps=1e-5, up=None):
         """Y = X W^T: X float32 [ncols, K] -> Y float32 [ncols, rows] (ggml dst [rows, ncols]).
 
         X and out may be row-strided views (unit column stride; X's row stride a multiple of 4 floats), as ggml's
-        src1 / dst with nb[1] > ne[0] * 4."""
+        src1 / dst with nb[1] > ne[0] * 4. norm_weight / up: each token's input op fused into the activation prep
+        (p8_mul_mat_ex): RMSNorm(X[n]) * norm_weight, or silu(X[n]) * up[n]."""
         if X.dim() == 2 and (X.stride(1) != 1 or X.stride(0) % 4 or X.data_ptr() % 16):
             X = X.contiguous()
         if X.dtype != torch.float32 or X.dim() != 2 or X.shape[1] != self.K or not X.is_cuda:
@@ -97,9 +98,28 @@ class P8Tensor:
         Y = out if out is not None else torch.empty(n, self.rows, dtype=torch.float32, device=X.device)
         if Y.dim() != 2 or Y.shape[0] != n or Y.shape[1] != self.rows or Y.stride(1) != 1 or Y.dtype != torch.float32:
             raise ValueError("out must be float32 [ncols, rows] with unit column stride")
-        ws = workspace if workspace is not None else self.workspace(n)
-        check(lib().p8_mul_mat(self.handle, _ptr(X), n, X.stride(0), _ptr(Y), Y.stride(0), _ptr(ws), ws.numel(),
-                               _stream(stream)), "p8_mul_mat")
+        if norm_weight is None and up is None:
+            ws = workspace if workspace is not None else self.workspace(n)
+            check(lib().p8_mul_mat(self.handle, _ptr(X), n, X.stride(0), _ptr(Y), Y.stride(0), _ptr(ws), ws.numel(),
+                                   _stream(stream)), "p8_mul_mat")
+            return Y
+        from ._lib import Prologue
+
+        if norm_weight is not None and up is not None:
+            raise ValueError("one prologue per call: norm_weight or up")
+        if norm_weight is not None:
+            if norm_weight.dtype != torch.float32 or not norm_weight.is_cuda or norm_weight.numel() != self.K:
+                raise ValueError("norm_weight must be float32 CUDA with K elements")
+            norm_weight = norm_weight.contiguous()
+            pro, kind = Prologue(1, norm_weight.data_ptr(), None, float(eps)), 1
+        else:
+            if up.shape != X.shape or up.stride() != X.stride() or up.dtype != torch.float32 or not up.is_cuda:
+                raise ValueError("up must be float32 CUDA with X's shape and strides")
+            pro, kind = Prologue(2, None, up.data_ptr(), 0.0), 2
+        need = int(lib().p8_workspace_size_ex(self.handle, n, kind))
+        ws = workspace if workspace is not None else torch.empty(max(need, 256), dtype=torch.uint8, device=X.device)
+        check(lib().p8_mul_mat_ex(self.handle, _ptr(X), n, X.stride(0), C.byref(pro), _ptr(Y), Y.stride(0), _ptr(ws),
+                                  ws.numel(), _stream(stream)), "p8_mul_mat_ex")
         return Y
 
     def get_rows(self, ids, out=None, stream=None):

@@ -248,6 +248,14 @@ class ColumnParallel:
             return torch.empty(0, dtype=torch.float32, device=x.device)
         return self.t.mul_mat_vec(x, out=out, workspace=workspace, stream=stream)
 
+    def mul_mat(self, X, out=None, workspace=None, stream=None):
+        """batched product [tokens, K] -> this rank's output columns [tokens, hi - lo] (prefill)"""
+        if self.t is None:
+            import torch
+
+            return torch.empty(X.shape[0], 0, dtype=torch.float32, device=X.device)
+        return self.t.mul_mat(X, out=out, workspace=workspace, stream=stream)
+
 
 class RowParallel:
     """this rank's input columns of a row-parallel projection: y = all_reduce_sum(W[:, lo:hi] x[lo:hi]).
@@ -277,3 +285,16 @@ class RowParallel:
         else:
             y = self.t.mul_mat_vec(x_local, out=out, workspace=workspace, stream=stream)
         return reduce_partials(y, self.group)
+
+    def mul_mat(self, X_local, out=None, workspace=None, stream=None):
+        """batched product (prefill): X_local [tokens, hi - lo] (this rank's input columns) -> the summed output
+        [tokens, rows] on every rank: the rank's partial from the batched product, then an NCCL all-reduce (the
+        partials are [tokens, rows] f32, large enough for the collective's bandwidth-optimised algorithms)"""
+        import torch
+
+        if self.t is None:
+            Y = out.zero_() if out is not None else torch.zeros(X_local.shape[0], self.shard.rows, dtype=torch.float32,
+                                                                 device=X_local.device)
+        else:
+            Y = self.t.mul_mat(X_local, out=out, workspace=workspace, stream=stream)
+        return reduce_partials(Y, self.group)

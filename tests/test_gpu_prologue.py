@@ -149,3 +149,41 @@ def test_prologue_arguments_are_checked():
     assert call(Prologue(0, None, None, 0.0)) == 0                  # none: the plain call
     torch.cuda.synchronize()
     assert torch.equal(y, t.mul_mat_vec(x))
+
+
+@pytest.mark.parametrize("ncols", [2, 16, 256])
+def test_batched_rmsnorm_prologue(ncols):
+    """p8_mul_mat_ex: RMSNorm per token (its own scale) with a shared weight; 2 tokens run the batch-1 GEMV per column
+    (1e-4), 16 and 256 the tcgen05 GEMM (fp16 operands: the 1e-3 bar)"""
+    K, rows = 4096, 512
+    (s, r, t), = _tensors((rows,), K, seed=31, nd=120)
+    rng = np.random.default_rng(ncols)
+    X = (rng.normal(0, 1, (ncols, K)) * rng.uniform(0.1, 30, (ncols, 1))).astype(np.float32)
+    w = rng.normal(1, 0.3, K).astype(np.float32)
+    Xp = np.stack([rmsnorm_np(X[n], w, 1e-5) for n in range(ncols)])
+    Y = t.mul_mat(torch.from_numpy(X).cuda(), norm_weight=torch.from_numpy(w).cuda(), eps=1e-5)
+    torch.cuda.synchronize()
+    assert device_error() == 0
+    ref = Oracle(s, r, K).mul_mat(Xp)
+    bar = BAR if ncols < 4 else 1e-3
+    assert rel(Y.cpu().numpy(), ref) < bar
+    wrong = ref + np.stack([_delta_shift(s, r, K, X[n], Xp[n]) for n in range(ncols)])
+    assert rel(wrong, ref) > 10 * bar
+
+
+@pytest.mark.parametrize("ncols", [3, 64])
+def test_batched_swiglu_prologue(ncols):
+    K, rows = 14336, 256
+    (s, r, t), = _tensors((rows,), K, seed=41, nd=1000)
+    rng = np.random.default_rng(ncols)
+    G = rng.normal(0, 2, (ncols, K)).astype(np.float32)
+    U = rng.normal(0, 1, (ncols, K)).astype(np.float32)
+    Xp = swiglu_np(G, U)
+    Y = t.mul_mat(torch.from_numpy(G).cuda(), up=torch.from_numpy(U).cuda())
+    torch.cuda.synchronize()
+    assert device_error() == 0
+    ref = Oracle(s, r, K).mul_mat(Xp)
+    bar = BAR if ncols < 4 else 1e-3
+    assert rel(Y.cpu().numpy(), ref) < bar
+    wrong = ref + np.stack([_delta_shift(s, r, K, G[n], Xp[n]) for n in range(ncols)])
+    assert rel(wrong, ref) > 10 * bar

@@ -53,8 +53,15 @@ def _rank(rank, world, port, name, q):
         dist.all_gather(parts, yc)
         row = tp.RowParallel(f.slot, f.K, f.rows, world, rank)
         yr = row(x[row.lo:row.hi].contiguous())
+        # batched (prefill) path: column shards gathered along the output columns, row shards all-reduced
+        X = torch.from_numpy(f.X).cuda()
+        Yc = col.mul_mat(X).contiguous()
+        ws_ = [torch.zeros(X.shape[0], int(v.item()), device="cuda") for v in ns]
+        dist.all_gather(ws_, Yc)
+        Yr = row.mul_mat(X[:, row.lo:row.hi].contiguous())
         torch.cuda.synchronize()
-        q.put((rank, torch.cat(parts).cpu().numpy(), yr.cpu().numpy(), device_error()))
+        q.put((rank, torch.cat(parts).cpu().numpy(), yr.cpu().numpy(), device_error(), torch.cat(ws_, 1).cpu().numpy(),
+               Yr.cpu().numpy()))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -80,10 +87,12 @@ def test_tp2_column_and_row_parallel(name):
         p.join(timeout=120)
         assert p.exitcode == 0
     rel = lambda a: float(np.linalg.norm(a - f.y_ref) / np.linalg.norm(f.y_ref))
-    for rank, yc, yr, err in res:
+    relY = lambda a: float(np.linalg.norm(a - f.Y_ref) / np.linalg.norm(f.Y_ref))
+    for rank, yc, yr, err, Yc, Yr in res:
         assert err == 0
         assert rel(yc) < 1e-5, (rank, rel(yc))
         assert rel(yr) < 1e-5, (rank, rel(yr))
+        assert relY(Yc) < 1e-3 and relY(Yr) < 1e-3, (rank, relY(Yc), relY(Yr))  # the batched product's fp16 bar
 
 
 def _rank_fused(rank, world, port, name, q):
