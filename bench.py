@@ -405,6 +405,44 @@ def run_b200(args, rank, world, local_rank):
             torch.cuda.synchronize()
             layer[name] = el0.elapsed_time(el1) / 1e3 / nrep
             del gl
+    # ---- (1 GPU) batched decode: bs sequences step together through the same projection chain, each call the batched
+    # product (p8_mul_mat: split-K tcgen05 GEMM for these token counts); one graph per bs, device-timed
+    batched = None
+    if world == 1 and not args.no_batched:
+        batched = {}
+        for bs in (8, 32, 64):
+            bws = torch.empty(max(ts[n].workspace_size(bs) for ts in layers for n in ts), dtype=torch.uint8, device=dev)
+            bx = {"x": torch.randn(bs, h, device=dev)}
+            for nm in ("q", "k", "v", "o", "gate", "up", "down"):
+                bx[nm] = torch.empty(bs, local[nm][0], device=dev)
+            bsrc = {"q": "x", "k": "x", "v": "x", "o": "q", "gate": "o", "up": "o", "down": "gate"}
+
+            def bstep():
+                for L, ts in enumerate(layers):
+                    for nm in ("q", "k", "v", "o", "gate", "up", "down"):
+                        src = bx[bsrc[nm]] if not (nm in ("q", "k", "v") and L > 0) else bx["down"]
+                        ts[nm].mul_mat(src, out=bx[nm], workspace=bws, stream=stream)
+
+            gb = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                bstep()
+                torch.cuda.synchronize()
+                with torch.cuda.graph(gb, stream=stream):
+                    bstep()
+            for _ in range(3):
+                gb.replay()
+            torch.cuda.synchronize()
+            b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            nb_ = max(5, args.steps // 5)
+            b0.record(stream)
+            with torch.cuda.stream(stream):
+                for _ in range(nb_):
+                    gb.replay()
+            b1.record(stream)
+            torch.cuda.synchronize()
+            t_b = b0.elapsed_time(b1) / 1e3 / nb_
+            batched[bs] = (t_b, bs / t_b)
+            del gb, bws, bx
     # ---- prefill (batched product, tcgen05 GEMM) at 1 GPU: 512 tokens through every projection of all 32 layers
     # (1.80 GB of weights per pass, larger than L2), one CUDA graph per pass, device-timed
     prefill = None
@@ -485,6 +523,11 @@ def run_b200(args, rank, world, local_rank):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),
     }
+    if batched is not None:
+        line["batched_decode"] = {
+            "kernel": "p8_mul_mat per projection (k_gx_max + k_gx_prep + k_gemm, split-K for these token counts)",
+            "per_bs": {str(bs): {"ms_per_step": round(t * 1e3, 3), "tok_s": round(v, 1),
+                                 "weight_gbs": round(bytes_token / t / 1e9, 1)} for bs, (t, v) in batched.items()}}
     if layer is not None:
         line["layer_prologues"] = {
             "ops": "RMSNorm*w -> q,k,v; o; RMSNorm*w -> gate,up; SwiGLU -> down (x 32 layers, graph-replayed, device-timed)",
@@ -517,6 +560,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-prefill", action="store_true", help="skip the batched-product (prefill) measurement")
     ap.add_argument("--no-layer", action="store_true", help="skip the fused-prologue layer measurement")
+    ap.add_argument("--no-batched", action="store_true", help="skip the batched-decode (bs 8/32/64) measurement")
     ap.add_argument("--tp-exchange", default="fused", choices=["fused", "nccl"],
                     help="row-parallel sum for N > 1: inside the GEMV over peer memory, or an NCCL all-reduce after it")
     args = ap.parse_args()
