@@ -17,7 +17,7 @@
 // rounding of the two operands (about 3e-4 relative L2 error against the exact product).
 //
 //   k_gx_max   grid (Npad, K/2048 rounded up), 256 thr: partial max |X[n] * sgn/c| over 2048 columns.
-//   k_gx_prep  grid (Npad/8, nb/4 rounded up), 256 thr, warp = token: tau from the partial maxima; Xr as fp16 in the
+//   k_gx_prep  grid (Npad/8, nb), 256 thr, warp = token: tau from the partial maxima; Xr as fp16 in the
 //              operand layout below ([half-slice][token group of 8][16 core matrices][8 tokens][8 columns]), so the
 //              GEMM moves one B stage with one bulk copy.
 //   k_gemm     grid (rows/128 rounded up, Npad/BN), 352 thr, 1 CTA per SM. One stage = one 128-column half-slice.
@@ -72,6 +72,10 @@ struct GemmArgs {
     float *kpart;          // split-K partial accumulators [ksplit][npad][mtr] (raw fp32)
     unsigned int *kcnt;    // split-K arrivals per output tile (zeroed by k_gx_max)
 };
+
+// 256-column blocks per k_gx_prep CTA: one, so that a token's blocks are converted in parallel (each warp's load ->
+// FWHT -> store chain is latency-bound; with several blocks per warp they ran one after another)
+constexpr int kGxBlocksPerCta = 1;
 
 struct GxArgs {
     const float *X;
@@ -236,8 +240,8 @@ __global__ void __launch_bounds__(256) k_gx_prep(const GxArgs a) {
     const float up = pow2f(tau);
     if (blockIdx.y == 0 && lane == 0) a.tdown[n] = pow2f(-tau);
     const size_t panel = (size_t)a.npad * 256;
-    for (int i = 0; i < 4; ++i) {
-        const int b = blockIdx.y * 4 + i;
+    for (int i = 0; i < kGxBlocksPerCta; ++i) {
+        const int b = blockIdx.y * kGxBlocksPerCta + i;
         if (b >= a.nb) break;
         float v[8];
         if (n < a.ncols) {
@@ -482,7 +486,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    pdl_wait();  // everything below may read memory written by earlier work in the stream
+    // The codebook, M words, payload and row scales belong to the tensor (no kernel of the stream writes them), so the
+    // set-up, the payload ring and the decoders run before the wait for the preceding kernels; the two roles that read
+    // what those kernels write wait first: the activation-tile loader (prepared operand) and the epilogue (x, the
+    // per-token scales, the split-K counters, the outputs).
     // lane-private codebook (entry f of lane l at word 32 f + l: a warp's lookups never share a bank), bytes + 128
     for (int i = threadIdx.x; i < 256 * 32; i += kGemmThreads) cbk[i] = a.A[i >> 5] ^ 0x80808080u;
     // M words of the CTA's four row tiles (arithmetic for uniform single-class layouts)
@@ -566,6 +573,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
             if (!__all_sync(0xffffffffu, mbar_wait_bounded(p_full + s % np, (uint32_t)(s / np) & 1u, kGemmPolls))) ok = false;
     } else if (warp == 10) {
         // ------------------------------------------------------------------ activation tiles (whole warp, lane 0 copies)
+        pdl_wait();  // the operand comes from the preceding prep kernel
         const uint8_t *src = a.Xh + (size_t)blockIdx.y * stageB;
         const size_t panel = (size_t)a.npad * 256;
         int last = -1;
@@ -616,6 +624,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
 
     if (warp < 8) {
         // ------------------------------------------------------------------ epilogue
+        pdl_wait();  // x, the token scales and the split-K counters come from earlier kernels; outputs are shared too
         pdl_launch_dependents();
         bool acc_ok = ok && mbar_wait_bounded(acc_bar, 0, kGemmPolls);
         acc_ok = __all_sync(0xffffffffu, acc_ok);
@@ -801,7 +810,9 @@ p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t
                          : pk == P8_PROLOGUE_SWIGLU  ? (const void *)k_gx_prep<P8_PROLOGUE_SWIGLU>
                                                      : (const void *)k_gx_prep<P8_PROLOGUE_NONE>;
         if (launch_pdl(fm, dim3(p.npad, p.nkc), dim3(256), 0, st, args) != cudaSuccess) return P8_ERR_CUDA;
-        if (launch_pdl(fp, dim3(p.npad / 8, (t->nb + 3) / 4), dim3(256), 0, st, args) != cudaSuccess) return P8_ERR_CUDA;
+        if (launch_pdl(fp, dim3(p.npad / 8, (t->nb + kGxBlocksPerCta - 1) / kGxBlocksPerCta), dim3(256), 0, st, args) !=
+            cudaSuccess)
+            return P8_ERR_CUDA;
     }
     GemmArgs ga;
     ga.A = t->A; ga.M = t->M; ga.D = t->D; ga.S = t->S; ga.prm = t->prm; ga.rsc = t->rsc; ga.cp = t->cp; ga.cc = t->cc;
