@@ -31,6 +31,8 @@
 //              warp 9     allocates TMEM; one lane issues 8 MMAs (M = 128, N = BN, K = 16, A from TMEM) per stage and
 //                         commits them to the stage's A-slot and B-slot 'empty' barriers, after the last stage to the
 //                         accumulator barrier.
+//   k_splitk_reduce  (split-K only) one thread per output: the splits' raw partials summed in split order, scaled,
+//                    clamp delta, y[n][prm[r]].
 // The loader and MMA warps run their loops as whole warps (every lane polls, one or four lanes issue): a single active
 // lane with 31 parked at a warp barrier was starved behind the decoders' shared-memory traffic.
 // Keeping A in TMEM leaves shared-memory bandwidth to the B tile (written once by the copy, read once by the MMA). The
@@ -70,7 +72,6 @@ struct GemmArgs {
     int rows, nb, ng, ncols, npad, bn, nbs, np, tileb, ucls;
     int ksplit, mtr;       // split-K: CTAs per output tile along K; padded rows of the partials
     float *kpart;          // split-K partial accumulators [ksplit][npad][mtr] (raw fp32)
-    unsigned int *kcnt;    // split-K arrivals per output tile (zeroed by k_gx_max)
 };
 
 // 256-column blocks per k_gx_prep CTA: one, so that a token's blocks are converted in parallel (each warp's load ->
@@ -85,8 +86,6 @@ struct GxArgs {
     float *tdown;
     long long ldx;
     int K, nb, ncols, npad, nkc;
-    unsigned int *kcnt;    // split-K tile counters to zero (or null)
-    int ncnt;
     // activation prologue (k_gx_*<PRO>, PRO != P8_PROLOGUE_NONE): x' per token from x and w (RMSNorm weight [K]) or
     // x2 (SwiGLU up, [ncols][ldx]); ss [npad][nkc] partial sums of squares; x' f32 to xv [npad][K] for the delta term
     const float *pw, *x2;
@@ -168,10 +167,6 @@ __global__ void __launch_bounds__(256) k_gx_max(const GxArgs a) {
     pdl_wait();
     __shared__ float red[8];
     __shared__ float red2[8];
-    if (a.kcnt) {  // the GEMM's split-K tile counters start each call at zero
-        for (int i = (blockIdx.y * gridDim.x + blockIdx.x) * 256 + threadIdx.x; i < a.ncnt; i += gridDim.x * gridDim.y * 256)
-            a.kcnt[i] = 0u;
-    }
     const int n = blockIdx.x, col = blockIdx.y * 2048 + threadIdx.x * 8;
     float m = 0.f, sq = 0.f;
     if (n < a.ncols && col < a.K) {
@@ -489,7 +484,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
     // The codebook, M words, payload and row scales belong to the tensor (no kernel of the stream writes them), so the
     // set-up, the payload ring and the decoders run before the wait for the preceding kernels; the two roles that read
     // what those kernels write wait first: the activation-tile loader (prepared operand) and the epilogue (x, the
-    // per-token scales, the split-K counters, the outputs).
+    // per-token scales, the outputs).
     // lane-private codebook (entry f of lane l at word 32 f + l: a warp's lookups never share a bank), bytes + 128
     for (int i = threadIdx.x; i < 256 * 32; i += kGemmThreads) cbk[i] = a.A[i >> 5] ^ 0x80808080u;
     // M words of the CTA's four row tiles (arithmetic for uniform single-class layouts)
@@ -624,7 +619,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
 
     if (warp < 8) {
         // ------------------------------------------------------------------ epilogue
-        pdl_wait();  // x, the token scales and the split-K counters come from earlier kernels; outputs are shared too
+        pdl_wait();  // x and the token scales come from earlier kernels; outputs and partials are shared too
         pdl_launch_dependents();
         bool acc_ok = ok && mbar_wait_bounded(acc_bar, 0, kGemmPolls);
         acc_ok = __all_sync(0xffffffffu, acc_ok);
@@ -638,7 +633,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
         const int e0 = row ? a.cp[ro] : 0, e1 = row ? a.cp[ro + 1] : 0;
         const int n0 = blockIdx.y * bn;
         const int cw = bn >> 1;
-        if (a.ksplit > 1) {  // raw accumulators of this K range -> partials (the tile's last CTA finishes below)
+        if (a.ksplit > 1) {  // raw accumulators of this K range -> partials (k_splitk_reduce finishes them)
             const int rp = blockIdx.x * 128 + q * 32 + lane;
             for (int cc0 = half * cw; acc_ok && cc0 < (half + 1) * cw; cc0 += 16) {
                 uint32_t v[16];
@@ -667,36 +662,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
     }
     ok = __all_sync(0xffffffffu, ok);
     if (!ok && lane == 0) atomicOr(&g_p8_device_error, 4u);
-    if (a.ksplit > 1) {
-        // split-K fixup: the last CTA of the output tile sums the partials in split order (deterministic), then
-        // scales, adds the clamp delta and scatters y
-        __shared__ int s_last;
-        __threadfence();
-        __syncthreads();
-        if (threadIdx.x == 0) s_last = atomicAdd(a.kcnt + blockIdx.y * gridDim.x + blockIdx.x, 1u) == (unsigned)a.ksplit - 1;
-        __syncthreads();
-        if (s_last && warp < 8) {
-            __threadfence();
-            const int q = warp & 3, half = warp >> 2;
-            const int r = blockIdx.x * 128 + q * 32 + lane;
-            if (r < a.rows) {
-                const int ro = a.prm[r];
-                const float down = a.rsc[r].y;
-                const int e0 = a.cp[ro], e1 = a.cp[ro + 1];
-                const int cw = bn >> 1, n0 = blockIdx.y * bn;
-                for (int c = half * cw; c < (half + 1) * cw; ++c) {
-                    const int n = n0 + c;
-                    if (n >= a.ncols) break;
-                    float acc = 0.f;
-                    for (int z = 0; z < a.ksplit; ++z) acc = __fadd_rn(acc, __ldcg(a.kpart + ((size_t)z * a.npad + n) * a.mtr + r));
-                    float y = __fmul_rn(__fmul_rn(acc, down), a.tdown[n]);
-                    const float *xn = a.X + (size_t)n * a.ldx;
-                    for (int e = e0; e < e1; ++e) y = __fadd_rn(y, __fmul_rn(a.cv[e], xn[a.cc[e]]));
-                    a.Y[(size_t)n * a.ldy + ro] = y;
-                }
-            }
-        }
-    }
     tc_fence_before();
     __syncthreads();
     if (warp == 9) {
@@ -705,12 +670,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
     }
 }
 
+// Split-K reduction (ksplit > 1), the kernel after k_gemm: one thread per output (token n, sorted row r), r fastest
+// (coalesced partial reads). y[n][prm[r]] = (sum over splits z in order of the raw partials) * 2^-sigma_r * 2^-tau_n
+// + the row's clamp delta -- the same operations in the same order as the single-split epilogue. A kernel of its own
+// instead of the last CTA of each tile: no fence / counter chain at the tail of the GEMM, and every SM takes part.
+__global__ void __launch_bounds__(256) k_splitk_reduce(const __grid_constant__ GemmArgs a) {
+    pdl_wait();  // the partials come from k_gemm
+    pdl_launch_dependents();
+    const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
+    if (i >= (long long)a.rows * a.ncols) return;
+    const int n = (int)(i / a.rows), r = (int)(i - (long long)n * a.rows);
+    float acc = 0.f;
+    for (int z = 0; z < a.ksplit; ++z) acc = __fadd_rn(acc, __ldcg(a.kpart + ((size_t)z * a.npad + n) * a.mtr + r));
+    const int ro = a.prm[r];
+    float y = __fmul_rn(__fmul_rn(acc, a.rsc[r].y), a.tdown[n]);
+    const float *xn = a.X + (size_t)n * a.ldx;
+    for (int e = a.cp[ro]; e < a.cp[ro + 1]; ++e) y = __fadd_rn(y, __fmul_rn(a.cv[e], xn[a.cc[e]]));
+    a.Y[(size_t)n * a.ldy + ro] = y;
+}
+
 // ---------------------------------------------------------------------------------------------------------------
 // host side
 struct GemmPlan {
     int bn, nbs, np, tileb, npad, nkc, mt, nnt, ks;
     size_t ss, xv;  // prologue only: partial sums of squares [npad][nkc], x' [npad][K]
-    size_t xh, pmax, tdown, kpart, kcnt, total, smem;
+    size_t xh, pmax, tdown, kpart, total, smem;
 };
 
 static int gemm_tile_bytes(const p8_tensor *t) {  // staging bytes of one tile's half-slice: the largest class present
@@ -756,8 +740,7 @@ static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols, bool pro = false) {
     p.pmax = al256((size_t)t->K * p.npad * 2);
     p.tdown = p.pmax + al256((size_t)p.npad * p.nkc * 4);
     p.kpart = p.tdown + al256((size_t)p.npad * 4);
-    p.kcnt = p.kpart + (p.ks > 1 ? al256((size_t)p.ks * p.npad * p.mt * 128 * 4) : 0);
-    p.total = p.kcnt + (p.ks > 1 ? al256((size_t)base * 4) : 0);
+    p.total = p.kpart + (p.ks > 1 ? al256((size_t)p.ks * p.npad * p.mt * 128 * 4) : 0);
     p.ss = p.total;
     p.xv = p.ss + (pro ? al256((size_t)p.npad * p.nkc * 4) : 0);
     p.total = p.xv + (pro ? al256((size_t)p.npad * t->K * 4) : 0);
@@ -799,8 +782,6 @@ p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t
     xa.Xh = w + p.xh;
     xa.pmax = reinterpret_cast<float *>(w + p.pmax);
     xa.tdown = reinterpret_cast<float *>(w + p.tdown);
-    xa.kcnt = p.ks > 1 ? reinterpret_cast<unsigned int *>(w + p.kcnt) : nullptr;
-    xa.ncnt = p.mt * p.nnt;
     {
         void *args[] = {&xa};
         const void *fm = pk == P8_PROLOGUE_RMSNORM ? (const void *)k_gx_max<P8_PROLOGUE_RMSNORM>
@@ -823,10 +804,14 @@ p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t
     ga.np = p.np; ga.tileb = p.tileb; ga.ucls = t->uniform_class;
     ga.ksplit = p.ks; ga.mtr = p.mt * 128;
     ga.kpart = reinterpret_cast<float *>(w + p.kpart);
-    ga.kcnt = xa.kcnt;
     void *args[] = {&ga};
     if (launch_pdl((const void *)k_gemm, dim3(p.mt, p.nnt, p.ks), dim3(kGemmThreads), p.smem, st, args) != cudaSuccess)
         return P8_ERR_CUDA;
+    if (p.ks > 1) {
+        const long long outs = (long long)t->rows * ncols;
+        if (launch_pdl((const void *)k_splitk_reduce, dim3((unsigned)((outs + 255) / 256)), dim3(256), 0, st, args) != cudaSuccess)
+            return P8_ERR_CUDA;
+    }
     return P8_OK;
 }
 
