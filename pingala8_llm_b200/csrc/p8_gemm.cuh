@@ -33,6 +33,9 @@
 //                         accumulator barrier.
 //   k_splitk_reduce  (split-K only) one thread per output: the splits' raw partials summed in split order, scaled,
 //                    clamp delta, y[n][prm[r]].
+//   k_unpermute      (single split, >= 64 tokens) the epilogue stores finished outputs in sorted-row order with 16-byte
+//                    stores; this kernel writes Y[n][ro] from row pinv[ro] with coalesced stores (Y's rows are the
+//                    permuted ones, so direct stores would scatter one 4-byte store per output).
 // The loader and MMA warps run their loops as whole warps (every lane polls, one or four lanes issue): a single active
 // lane with 31 parked at a warp barrier was starved behind the decoders' shared-memory traffic.
 // Keeping A in TMEM leaves shared-memory bandwidth to the B tile (written once by the copy, read once by the MMA). The
@@ -54,6 +57,7 @@ constexpr int kGemmSmemMax = 227 * 1024;            // shared memory per CTA (sm
 constexpr int kGemmSmemDyn = kGemmSmemMax - 1024;   // dynamic part (the kernel's static shared memory takes 1 KB)
 constexpr uint32_t kGemmPolls = 1u << 22;
 constexpr int kGemmMinCols = 4;                     // below this the per-column table GEMV is faster (measured crossover)
+constexpr int kGemmStagedMinCols = 64;              // from here (single split) outputs go out in sorted-row order first
 
 struct GemmArgs {
     const uint32_t *A, *M, *D;
@@ -72,6 +76,8 @@ struct GemmArgs {
     int rows, nb, ng, ncols, npad, bn, nbs, np, tileb, ucls;
     int ksplit, mtr;       // split-K: CTAs per output tile along K; padded rows of the partials
     float *kpart;          // split-K partial accumulators [ksplit][npad][mtr] (raw fp32)
+    float *Yt;             // (single split, many tokens) outputs in sorted-row order [mtr][npad], un-permuted after
+    const int16_t *pinv;   // original row -> sorted row
 };
 
 // 256-column blocks per k_gx_prep CTA: one, so that a token's blocks are converted in parallel (each warp's load ->
@@ -643,7 +649,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
                     a.kpart[((size_t)blockIdx.z * a.npad + n0 + cc0 + i) * a.mtr + rp] = __uint_as_float(v[i]);
             }
         }
-        for (int cc0 = half * cw; acc_ok && a.ksplit == 1 && cc0 < (half + 1) * cw; cc0 += 16) {
+        for (int cc0 = half * cw; acc_ok && a.ksplit == 1 && a.Yt && cc0 < (half + 1) * cw; cc0 += 16) {
+            // sorted-row order: the lane's 16 tokens as four 16-byte stores (the permuted rows of Y would take one
+            // scattered 4-byte store per output); k_unpermute writes Y from here with coalesced stores
+            uint32_t v[16];
+            tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)cc0, v);
+            if (row) {
+                float yv[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    const int n = n0 + cc0 + i;
+                    float y = 0.f;
+                    if (n < a.ncols) {
+                        y = __fmul_rn(__fmul_rn(__uint_as_float(v[i]), down), a.tdown[n]);
+                        const float *xn = a.X + (size_t)n * a.ldx;
+                        for (int e = e0; e < e1; ++e) y = __fadd_rn(y, __fmul_rn(a.cv[e], xn[a.cc[e]]));
+                    }
+                    yv[i] = y;
+                }
+                float4 *o = reinterpret_cast<float4 *>(a.Yt + (size_t)r * a.npad + n0 + cc0);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o[i] = make_float4(yv[4 * i], yv[4 * i + 1], yv[4 * i + 2], yv[4 * i + 3]);
+            }
+        }
+        for (int cc0 = half * cw; acc_ok && a.ksplit == 1 && !a.Yt && cc0 < (half + 1) * cw; cc0 += 16) {
             uint32_t v[16];
             tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)cc0, v);
             if (row) {
@@ -670,6 +699,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
     }
 }
 
+// Outputs staged in sorted-row order (Yt) to Y: thread = (original row ro, 8 tokens); reads the 8 tokens of sorted row
+// pinv[ro] (32 contiguous bytes), writes Y[n][ro] (a warp's 32 consecutive rows: one coalesced store per token).
+__global__ void __launch_bounds__(256) k_unpermute(const __grid_constant__ GemmArgs a) {
+    pdl_wait();  // Yt comes from k_gemm
+    pdl_launch_dependents();
+    const int ro = blockIdx.x * 256 + threadIdx.x, n8 = blockIdx.y * 8;
+    if (ro >= a.rows) return;
+    const float4 *src = reinterpret_cast<const float4 *>(a.Yt + (size_t)a.pinv[ro] * a.npad + n8);
+    const float4 u0 = __ldcg(src), u1 = __ldcg(src + 1);
+    const float v[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        if (n8 + i < a.ncols) a.Y[(size_t)(n8 + i) * a.ldy + ro] = v[i];
+}
+
 // Split-K reduction (ksplit > 1), the kernel after k_gemm: one thread per output (token n, sorted row r), r fastest
 // (coalesced partial reads). y[n][prm[r]] = (sum over splits z in order of the raw partials) * 2^-sigma_r * 2^-tau_n
 // + the row's clamp delta -- the same operations in the same order as the single-split epilogue. A kernel of its own
@@ -694,6 +738,8 @@ __global__ void __launch_bounds__(256) k_splitk_reduce(const __grid_constant__ G
 struct GemmPlan {
     int bn, nbs, np, tileb, npad, nkc, mt, nnt, ks;
     size_t ss, xv;  // prologue only: partial sums of squares [npad][nkc], x' [npad][K]
+    size_t yt;      // staged outputs [mt * 128][npad] (single split, >= kGemmStagedMinCols tokens), else 0 bytes
+    bool staged;
     size_t xh, pmax, tdown, kpart, total, smem;
 };
 
@@ -741,6 +787,9 @@ static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols, bool pro = false) {
     p.tdown = p.pmax + al256((size_t)p.npad * p.nkc * 4);
     p.kpart = p.tdown + al256((size_t)p.npad * 4);
     p.total = p.kpart + (p.ks > 1 ? al256((size_t)p.ks * p.npad * p.mt * 128 * 4) : 0);
+    p.staged = p.ks == 1 && ncols >= kGemmStagedMinCols;
+    p.yt = p.total;
+    p.total = p.yt + (p.staged ? al256((size_t)p.mt * 128 * p.npad * 4) : 0);
     p.ss = p.total;
     p.xv = p.ss + (pro ? al256((size_t)p.npad * p.nkc * 4) : 0);
     p.total = p.xv + (pro ? al256((size_t)p.npad * t->K * 4) : 0);
@@ -804,9 +853,16 @@ p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t
     ga.np = p.np; ga.tileb = p.tileb; ga.ucls = t->uniform_class;
     ga.ksplit = p.ks; ga.mtr = p.mt * 128;
     ga.kpart = reinterpret_cast<float *>(w + p.kpart);
+    ga.Yt = p.staged ? reinterpret_cast<float *>(w + p.yt) : nullptr;
+    ga.pinv = t->pinv;
     void *args[] = {&ga};
     if (launch_pdl((const void *)k_gemm, dim3(p.mt, p.nnt, p.ks), dim3(kGemmThreads), p.smem, st, args) != cudaSuccess)
         return P8_ERR_CUDA;
+    if (p.staged) {
+        if (launch_pdl((const void *)k_unpermute, dim3((unsigned)((t->rows + 255) / 256), (unsigned)((ncols + 7) / 8)), dim3(256), 0,
+                       st, args) != cudaSuccess)
+            return P8_ERR_CUDA;
+    }
     if (p.ks > 1) {
         const long long outs = (long long)t->rows * ncols;
         if (launch_pdl((const void *)k_splitk_reduce, dim3((unsigned)((outs + 255) / 256)), dim3(256), 0, st, args) != cudaSuccess)

@@ -140,3 +140,21 @@ def test_gemm_deterministic_and_graph_capturable():
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(out, y1)
+
+
+def test_gemm_staged_outputs_with_strides():
+    """From 64 tokens (single split) the outputs are written in sorted-row order first and un-permuted into Y: with
+    ldx > K and ldy > rows, nothing outside the output rows is touched and every value matches the oracle"""
+    rows, K, n = 768, 2048, 80
+    s = synth.make_slot(rows, K, seed=12, nd=17, c16="random")
+    t = P8Tensor(s, K, rows)
+    o = Oracle(s, rows, K)
+    X = np.random.default_rng(12).normal(0, 1, (n, K)).astype(np.float32)
+    Xs = torch.zeros(n, K + 8, dtype=torch.float32, device="cuda")
+    Xs[:, :K] = torch.from_numpy(X).cuda()
+    Ys = torch.full((n, rows + 36), 7.0, dtype=torch.float32, device="cuda")
+    t.mul_mat(Xs[:, :K], out=Ys[:, :rows])
+    torch.cuda.synchronize()
+    assert device_error() == 0
+    assert rel(Ys[:, :rows].cpu().numpy(), o.mul_mat_f64(X.astype(np.float64))) < BAR
+    assert torch.all(Ys[:, rows:] == 7.0)
