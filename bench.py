@@ -214,7 +214,7 @@ def run_b200(args, rank, world, local_rank):
     import torch.distributed as dist
 
     from pingala8_llm_b200 import synth, tp
-    from pingala8_llm_b200.ops import P8Tensor, device_error, group_workspace_size, mul_mat_vec_group
+    from pingala8_llm_b200.ops import P8Tensor, device_error, group_workspace_size, mul_mat_group, mul_mat_vec_group
 
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
@@ -409,13 +409,16 @@ def run_b200(args, rank, world, local_rank):
             torch.cuda.synchronize()
             layer[name] = el0.elapsed_time(el1) / 1e3 / nrep
             del gl
-    # ---- (1 GPU) batched decode: bs sequences step together through the same projection chain, each call the batched
-    # product (p8_mul_mat: split-K tcgen05 GEMM for these token counts); one graph per bs, device-timed
+    # ---- (1 GPU) batched decode: bs sequences step together through the same projection chain, each group of
+    # projections on one input (q/k/v, o, gate/up, down) one grouped batched product (p8_mul_mat_group: one activation
+    # prep, then the split-K tcgen05 GEMM per tensor at these token counts); one graph per bs, device-timed
+    groups = (("q", "k", "v"), ("o",), ("gate", "up"), ("down",))
     batched = None
     if world == 1 and not args.no_batched:
         batched = {}
         for bs in (8, 32, 64):
-            bws = torch.empty(max(ts[n].workspace_size(bs) for ts in layers for n in ts), dtype=torch.uint8, device=dev)
+            bws = torch.empty(max(group_workspace_size([ts[n] for n in g], bs) for ts in layers for g in groups),
+                              dtype=torch.uint8, device=dev)
             bx = {"x": torch.randn(bs, h, device=dev)}
             for nm in ("q", "k", "v", "o", "gate", "up", "down"):
                 bx[nm] = torch.empty(bs, local[nm][0], device=dev)
@@ -423,9 +426,9 @@ def run_b200(args, rank, world, local_rank):
 
             def bstep():
                 for L, ts in enumerate(layers):
-                    for nm in ("q", "k", "v", "o", "gate", "up", "down"):
-                        src = bx[bsrc[nm]] if not (nm in ("q", "k", "v") and L > 0) else bx["down"]
-                        ts[nm].mul_mat(src, out=bx[nm], workspace=bws, stream=stream)
+                    for g in groups:
+                        src = bx[bsrc[g[0]]] if not (g[0] == "q" and L > 0) else bx["down"]
+                        mul_mat_group([ts[n] for n in g], src, outs=[bx[n] for n in g], workspace=bws, stream=stream)
 
             gb = torch.cuda.CUDAGraph()
             with torch.cuda.stream(stream):
@@ -448,37 +451,48 @@ def run_b200(args, rank, world, local_rank):
             batched[bs] = (t_b, bs / t_b)
             del gb, bws, bx
     # ---- prefill (batched product, tcgen05 GEMM) at 1 GPU: 512 tokens through every projection of all 32 layers
-    # (1.80 GB of weights per pass, larger than L2), one CUDA graph per pass, device-timed
+    # (1.80 GB of weights per pass, larger than L2), one CUDA graph per pass, device-timed; the projections on one
+    # input as grouped products (p8_mul_mat_group, one activation prep per group), and as separate p8_mul_mat calls
     prefill = None
     if world == 1 and not args.no_prefill:
         ntok = 512
-        pws = torch.empty(max(ts[n].workspace_size(ntok) for ts in layers for n in ts), dtype=torch.uint8, device=dev)
+        pws = torch.empty(max(group_workspace_size([ts[n] for n in g], ntok) for ts in layers for g in groups),
+                          dtype=torch.uint8, device=dev)
         Xp = {K: torch.randn(ntok, K, device=dev) for K in {k for _, _, k in shapes}}
         Yp = {n: torch.empty(ntok, r, device=dev) for n, (r, k) in local.items()}
-        gp = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(stream):
-            for ts in layers[:1]:
+
+        def pass_grouped(lys):
+            for ts in lys:
+                for g in groups:
+                    mul_mat_group([ts[n] for n in g], Xp[ts[g[0]].K], outs=[Yp[n] for n in g], workspace=pws, stream=stream)
+
+        def pass_separate(lys):
+            for ts in lys:
                 for n, tt in ts.items():
                     tt.mul_mat(Xp[tt.K], out=Yp[n], workspace=pws, stream=stream)
+
+        t_pf = {}
+        for name, fn in (("grouped", pass_grouped), ("separate", pass_separate)):
+            gp = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                fn(layers[:1])
+                torch.cuda.synchronize()
+                with torch.cuda.graph(gp, stream=stream):
+                    fn(layers)
+            gp.replay()
             torch.cuda.synchronize()
-            with torch.cuda.graph(gp, stream=stream):
-                for ts in layers:
-                    for n, tt in ts.items():
-                        tt.mul_mat(Xp[tt.K], out=Yp[n], workspace=pws, stream=stream)
-        gp.replay()
-        torch.cuda.synchronize()
-        ep0, ep1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        npass = 3
-        ep0.record(stream)
-        with torch.cuda.stream(stream):
-            for _ in range(npass):
-                gp.replay()
-        ep1.record(stream)
-        torch.cuda.synchronize()
-        t_pass = ep0.elapsed_time(ep1) / 1e3 / npass
+            ep0, ep1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            npass = 3
+            ep0.record(stream)
+            with torch.cuda.stream(stream):
+                for _ in range(npass):
+                    gp.replay()
+            ep1.record(stream)
+            torch.cuda.synchronize()
+            t_pf[name] = ep0.elapsed_time(ep1) / 1e3 / npass
+            del gp
         flop = sum(2.0 * r * k * ntok for _, r, k in shapes) * model["layers"]
-        prefill = (ntok, t_pass, flop)
-        del gp
+        prefill = (ntok, t_pf["grouped"], flop, t_pf["separate"])
     # ---- max over ranks
     gnames = list(per_group)
     times = torch.tensor([t_dev, t_e2e] + [per_group[g][0] for g in gnames], dtype=torch.float64, device=dev)
@@ -529,7 +543,7 @@ def run_b200(args, rank, world, local_rank):
     }
     if batched is not None:
         line["batched_decode"] = {
-            "kernel": "p8_mul_mat per projection (k_gx_max + k_gx_prep + k_gemm, split-K for these token counts)",
+            "kernel": "p8_mul_mat_group per input (k_gx_max + k_gx_prep once, then k_gemm + k_splitk_reduce per projection)",
             "per_bs": {str(bs): {"ms_per_step": round(t * 1e3, 3), "tok_s": round(v, 1),
                                  "weight_gbs": round(bytes_token / t / 1e9, 1)} for bs, (t, v) in batched.items()}}
     if layer is not None:
@@ -539,10 +553,13 @@ def run_b200(args, rank, world, local_rank):
             "fused": "p8_mul_mat_vec_group_ex (prologue in k_act_prep)",
             "torch_ops": "separate torch elementwise/reduction kernels, then p8_mul_mat_vec_group"}
     if prefill is not None:
-        ntok, t_pass, flop = prefill
+        ntok, t_pass, flop, t_sep = prefill
         bf16_peak = measured_bf16_tflops()
         line["prefill"] = {"tokens": ntok, "ms": round(t_pass * 1e3, 3), "tok_s": round(ntok / t_pass, 1),
-                           "kernel": "p8_mul_mat (k_gx_max + k_gx_prep + k_gemm, tcgen05 kind::f16, fp32 accumulate)",
+                           "kernel": "p8_mul_mat_group per input (k_gx_max + k_gx_prep once; k_gemm, tcgen05 kind::f16, "
+                                     "fp32 accumulate, + k_unpermute per projection)",
+                           "separate_calls": {"ms": round(t_sep * 1e3, 3), "tflops": round(flop / t_sep / 1e12, 1),
+                                              "kernel": "p8_mul_mat per projection"},
                            "tflops": round(flop / t_pass / 1e12, 1), "bound": "tensor", "peak_tflops": bf16_peak,
                            "frac": round(flop / t_pass / 1e12 / bf16_peak, 4),
                            "peak_source": "MEASURED_PEAKS.json bf16_tflops (cuBLAS bf16 burst; the GEMM runs fp16 operands at the same rate)",

@@ -108,6 +108,15 @@ size_t p8_workspace_size_ex(const p8_tensor *t, int64_t ncols, int kind);
 p8_status p8_mul_mat_ex(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, const p8_prologue *pro, float *Y,
                         int64_t ldy, void *workspace, size_t workspace_bytes, void *stream);
 
+/* p8_mul_mat_ex for several tensors that read the same X (q/k/v, gate/up; n <= 4, requirements as
+ * p8_mul_mat_vec_group, else P8_ERR_ARG): the activation prep, prologue included, runs once and each tensor's product
+ * reads it; Y_i [ncols][ldys[i]]. Results are bit-identical to separate p8_mul_mat_ex calls. The reference's
+ * activation cache (vrc_tg, CP:1171-1180) reuses a prepared x across consecutive tensors the same way; ggml has no
+ * grouped op, so this entry point is an extension. Workspace p8_workspace_size_group_ex(ts, n, ncols, kind). */
+size_t p8_workspace_size_group_ex(const p8_tensor *const *ts, int n, int64_t ncols, int kind);
+p8_status p8_mul_mat_group(const p8_tensor *const *ts, int n, const float *X, int64_t ncols, int64_t ldx, const p8_prologue *pro,
+                           float *const *Ys, const int64_t *ldys, void *workspace, size_t workspace_bytes, void *stream);
+
 /* y = W x like p8_mul_mat_vec, but with no workspace argument and no allocation: the scratch is a fixed 6 MiB device
  * array inside the library, for callers that cannot allocate device memory at call time and have no buffer to lend
  * (e.g. a host framework that plans all device memory up front). No counterpart in the reference (its GEMV takes

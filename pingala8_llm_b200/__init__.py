@@ -12,7 +12,7 @@ __all__ = ["P8Error", "P8Tensor", "fmt", "synth", "lib", "active", "device_error
 
 def __getattr__(name):
     # the torch-facing operator layer is imported lazily so the host format helpers work without CUDA
-    if name in ("P8Tensor", "active", "device_error", "mul_mat_vec_group", "group_workspace_size"):
+    if name in ("P8Tensor", "active", "device_error", "mul_mat_vec_group", "group_workspace_size", "mul_mat_group"):
         import importlib
 
         return getattr(importlib.import_module(".ops", __name__), name)

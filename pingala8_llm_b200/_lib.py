@@ -52,6 +52,8 @@ _SIGS = {
     "p8_mul_mat_vec_group_ex": (C.c_int, [_vp, C.c_int, _vp, C.POINTER(Prologue), _vp, _vp, _sz, _vp]),
     "p8_workspace_size_ex": (_sz, [_vp, _i64, C.c_int]),
     "p8_mul_mat_ex": (C.c_int, [_vp, _vp, _i64, _i64, C.POINTER(Prologue), _vp, _i64, _vp, _sz, _vp]),
+    "p8_workspace_size_group_ex": (_sz, [_vp, C.c_int, _i64, C.c_int]),
+    "p8_mul_mat_group": (C.c_int, [_vp, C.c_int, _vp, _i64, _i64, C.POINTER(Prologue), _vp, _vp, _vp, _sz, _vp]),
     "p8_noalloc_scratch_bytes": (_sz, []),
     "p8_mul_mat_vec_noalloc": (C.c_int, [_vp, _vp, _vp, _vp]),
     "p8_mul_mat": (C.c_int, [_vp, _vp, _i64, _i64, _vp, _i64, _vp, _sz, _vp]),

@@ -283,6 +283,72 @@ p8_status p8_mul_mat_ex(const p8_tensor *t, const float *X, int64_t ncols, int64
     return P8_OK;
 }
 
+size_t p8_workspace_size_group_ex(const p8_tensor *const *ts, int n, int64_t ncols, int kind) {
+    if (!ts || n < 1 || n > 4 || ncols <= 0) return 0;
+    for (int i = 0; i < n; ++i)
+        if (!valid(ts[i])) return 0;
+    size_t w = gemv_group_workspace(ts, n, ncols);
+    int nsup = 0;
+    for (int i = 0; i < n; ++i) {
+        const size_t g = gemv_workspace(ts[i], ncols);
+        if (g > w) w = g;
+        if (gemm_supported(ts[i], ncols)) {
+            ++nsup;
+            const size_t h = gemm_workspace(ts[i], ncols, kind != P8_PROLOGUE_NONE);
+            if (h > w) w = h;
+        }
+    }
+    if (nsup == n) {
+        const size_t h = gemm_group_workspace(ts, n, ncols, kind != P8_PROLOGUE_NONE);
+        if (h > w) w = h;
+    }
+    return w;
+}
+
+p8_status p8_mul_mat_group(const p8_tensor *const *ts, int n, const float *X, int64_t ncols, int64_t ldx, const p8_prologue *pro,
+                           float *const *Ys, const int64_t *ldys, void *workspace, size_t workspace_bytes, void *stream) {
+    if (!ts || !Ys || !ldys || n < 1 || n > 4) return P8_ERR_ARG;
+    for (int i = 0; i < n; ++i)
+        if (!valid(ts[i])) return P8_ERR_NOT_PREPARED;
+    if (!X || ncols <= 0 || ldx < ts[0]->K || ((uintptr_t)X & 15) || (ldx & 3)) return P8_ERR_ARG;
+    int nsup = 0;
+    for (int i = 0; i < n; ++i) {
+        if (!Ys[i] || ldys[i] < ts[i]->rows) return P8_ERR_ARG;
+        if (ts[i]->K != ts[0]->K || ts[i]->act_hash != ts[0]->act_hash) return P8_ERR_ARG;
+        nsup += gemm_supported(ts[i], ncols) ? 1 : 0;
+    }
+    if (pro) {
+        if (pro->kind == P8_PROLOGUE_RMSNORM) {
+            if (!pro->w || ((uintptr_t)pro->w & 15) || !(pro->eps >= 0.f)) return P8_ERR_ARG;
+        } else if (pro->kind == P8_PROLOGUE_SWIGLU) {
+            if (!pro->x2 || ((uintptr_t)pro->x2 & 15)) return P8_ERR_ARG;
+        } else if (pro->kind != P8_PROLOGUE_NONE) {
+            return P8_ERR_ARG;
+        }
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    if (nsup == n) return launch_gemm_group(ts, n, X, ncols, ldx, Ys, ldys, workspace, workspace_bytes, s, pro);
+    if (nsup == 0) {  // below the GEMM's column count: the grouped batch-1 GEMV per column
+        for (int64_t c = 0; c < ncols; ++c) {
+            p8_prologue pn;
+            if (pro) {
+                pn = *pro;
+                if (pn.x2) pn.x2 += c * ldx;
+            }
+            float *yc[4];
+            for (int i = 0; i < n; ++i) yc[i] = Ys[i] + c * ldys[i];
+            const p8_status st = launch_gemv_group_pro(ts, n, X + c * ldx, pro ? &pn : nullptr, yc, workspace, workspace_bytes, s);
+            if (st) return st;
+        }
+        return P8_OK;
+    }
+    for (int i = 0; i < n; ++i) {  // tensors on different paths: one call each
+        const p8_status st = p8_mul_mat_ex(ts[i], X, ncols, ldx, pro, Ys[i], ldys[i], workspace, workspace_bytes, stream);
+        if (st) return st;
+    }
+    return P8_OK;
+}
+
 p8_status p8_get_rows(const p8_tensor *t, const int32_t *ids, int64_t n, float *out, int64_t ldo, void *stream) {
     if (!valid(t)) return P8_ERR_NOT_PREPARED;
     if (n < 0 || (n && (!ids || !out)) || ldo < t->K || ((uintptr_t)out & 15) || (ldo & 3)) return P8_ERR_ARG;

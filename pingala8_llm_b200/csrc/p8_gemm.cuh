@@ -74,6 +74,7 @@ struct GemmArgs {
     long long ldx, ldy;
     uint32_t cs;
     int rows, nb, ng, ncols, npad, bn, nbs, np, tileb, ucls;
+    int xpad;              // token count of Xh's panels (the prep's padding: >= npad when a group shares the prep)
     int ksplit, mtr;       // split-K: CTAs per output tile along K; padded rows of the partials
     float *kpart;          // split-K partial accumulators [ksplit][npad][mtr] (raw fp32)
     float *Yt;             // (single split, many tokens) outputs in sorted-row order [mtr][npad], un-permuted after
@@ -576,7 +577,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
         // ------------------------------------------------------------------ activation tiles (whole warp, lane 0 copies)
         pdl_wait();  // the operand comes from the preceding prep kernel
         const uint8_t *src = a.Xh + (size_t)blockIdx.y * stageB;
-        const size_t panel = (size_t)a.npad * 256;
+        const size_t panel = (size_t)a.xpad * 256;
         int last = -1;
         for (int s = 0; s < nls; ++s) {
             const int bs = s % nbs;
@@ -740,7 +741,9 @@ struct GemmPlan {
     size_t ss, xv;  // prologue only: partial sums of squares [npad][nkc], x' [npad][K]
     size_t yt;      // staged outputs [mt * 128][npad] (single split, >= kGemmStagedMinCols tokens), else 0 bytes
     bool staged;
-    size_t xh, pmax, tdown, kpart, total, smem;
+    size_t xh, pmax, tdown, prep;  // the activation prep's part [0, prep)
+    size_t kpart, own;             // the tensor's own part, offsets from its start; own = its size
+    size_t total, smem;
 };
 
 static int gemm_tile_bytes(const p8_tensor *t) {  // staging bytes of one tile's half-slice: the largest class present
@@ -782,17 +785,18 @@ static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols, bool pro = false) {
         const int kmax = t->nb / 2 > 1 ? t->nb / 2 : 1;
         if (p.ks > kmax) p.ks = kmax;
     }
+    // workspace: the activation prep's part first (shared by the tensors of a group), then the tensor's own part
     p.xh = 0;
     p.pmax = al256((size_t)t->K * p.npad * 2);
     p.tdown = p.pmax + al256((size_t)p.npad * p.nkc * 4);
-    p.kpart = p.tdown + al256((size_t)p.npad * 4);
-    p.total = p.kpart + (p.ks > 1 ? al256((size_t)p.ks * p.npad * p.mt * 128 * 4) : 0);
-    p.staged = p.ks == 1 && ncols >= kGemmStagedMinCols;
-    p.yt = p.total;
-    p.total = p.yt + (p.staged ? al256((size_t)p.mt * 128 * p.npad * 4) : 0);
-    p.ss = p.total;
+    p.ss = p.tdown + al256((size_t)p.npad * 4);
     p.xv = p.ss + (pro ? al256((size_t)p.npad * p.nkc * 4) : 0);
-    p.total = p.xv + (pro ? al256((size_t)p.npad * t->K * 4) : 0);
+    p.prep = p.xv + (pro ? al256((size_t)p.npad * t->K * 4) : 0);
+    p.staged = p.ks == 1 && ncols >= kGemmStagedMinCols;
+    p.kpart = 0;
+    p.yt = p.kpart + (p.ks > 1 ? al256((size_t)p.ks * p.npad * p.mt * 128 * 4) : 0);
+    p.own = p.yt + (p.staged ? al256((size_t)p.mt * 128 * p.npad * 4) : 0);
+    p.total = p.prep + p.own;
     return p;
 }
 
@@ -803,12 +807,74 @@ bool gemm_supported(const p8_tensor *t, int64_t ncols) {
 
 size_t gemm_workspace(const p8_tensor *t, int64_t ncols, bool pro) { return gemm_plan(t, ncols, pro).total; }
 
-p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy, void *ws,
-                      size_t ws_bytes, cudaStream_t st, const p8_prologue *pro) {
+// A group's tensors (equal K and prepared-activation hash) share one activation prep. Their plans may pad the tokens
+// differently (the tile width follows the row count), so the prep pads to the largest npad: Xh's panels carry that
+// token count (GemmArgs::xpad) and each tensor reads its first npad tokens, which are the same as its own prep's.
+// The tensors' own parts (split-K partials, staged outputs) follow the prep's part and are reused one after another.
+static int gemm_group_prep(const GemmPlan *pl, int n) {
+    int j = 0;
+    for (int i = 1; i < n; ++i)
+        if (pl[i].npad > pl[j].npad) j = i;
+    return j;
+}
+
+size_t gemm_group_workspace(const p8_tensor *const *ts, int n, int64_t ncols, bool pro) {
+    if (n < 1 || n > 4) return 0;
+    GemmPlan pl[4];
+    size_t own = 0;
+    for (int i = 0; i < n; ++i) {
+        pl[i] = gemm_plan(ts[i], ncols, pro);
+        if (pl[i].own > own) own = pl[i].own;
+    }
+    return pl[gemm_group_prep(pl, n)].prep + own;
+}
+
+static p8_status launch_gemm_one(const p8_tensor *t, const GemmPlan &p, const GxArgs &xa, int pk, const float *X, int64_t ncols,
+                                 int64_t ldx, float *Y, int64_t ldy, uint8_t *own, cudaStream_t st) {
+    GemmArgs ga;
+    ga.A = t->A; ga.M = t->M; ga.D = t->D; ga.S = t->S; ga.prm = t->prm; ga.rsc = t->rsc; ga.cp = t->cp; ga.cc = t->cc;
+    ga.cv = t->cv; ga.Y = Y; ga.Xh = xa.Xh; ga.tdown = xa.tdown; ga.ldy = ldy; ga.cs = t->cs;
+    ga.X = pk != P8_PROLOGUE_NONE ? xa.xv : X;  // the clamp-delta term multiplies x'
+    ga.ldx = pk != P8_PROLOGUE_NONE ? t->K : ldx;
+    ga.rows = t->rows; ga.nb = t->nb; ga.ng = t->ng; ga.ncols = (int)ncols; ga.npad = p.npad; ga.bn = p.bn; ga.nbs = p.nbs;
+    ga.np = p.np; ga.tileb = p.tileb; ga.ucls = t->uniform_class;
+    ga.xpad = xa.npad;
+    ga.ksplit = p.ks; ga.mtr = p.mt * 128;
+    ga.kpart = reinterpret_cast<float *>(own + p.kpart);
+    ga.Yt = p.staged ? reinterpret_cast<float *>(own + p.yt) : nullptr;
+    ga.pinv = t->pinv;
+    void *args[] = {&ga};
+    if (launch_pdl((const void *)k_gemm, dim3(p.mt, p.nnt, p.ks), dim3(kGemmThreads), p.smem, st, args) != cudaSuccess)
+        return P8_ERR_CUDA;
+    if (p.staged) {
+        if (launch_pdl((const void *)k_unpermute, dim3((unsigned)((t->rows + 255) / 256), (unsigned)((ncols + 7) / 8)), dim3(256), 0,
+                       st, args) != cudaSuccess)
+            return P8_ERR_CUDA;
+    }
+    if (p.ks > 1) {
+        const long long outs = (long long)t->rows * ncols;
+        if (launch_pdl((const void *)k_splitk_reduce, dim3((unsigned)((outs + 255) / 256)), dim3(256), 0, st, args) != cudaSuccess)
+            return P8_ERR_CUDA;
+    }
+    return P8_OK;
+}
+
+// tensors reading the same X (equal K and activation hash, checked by the caller): one activation prep, then each
+// tensor's product
+p8_status launch_gemm_group(const p8_tensor *const *ts, int n, const float *X, int64_t ncols, int64_t ldx, float *const *Ys,
+                            const int64_t *ldys, void *ws, size_t ws_bytes, cudaStream_t st, const p8_prologue *pro) {
+    if (n < 1 || n > 4) return P8_ERR_ARG;
     const int pk = pro ? pro->kind : P8_PROLOGUE_NONE;
-    const GemmPlan p = gemm_plan(t, ncols, pk != P8_PROLOGUE_NONE);
-    if (!ws || ws_bytes < p.total || ((uintptr_t)ws & 255)) return P8_ERR_WORKSPACE;
-    if (p.smem > (size_t)kGemmSmemDyn) return P8_ERR_UNSUPPORTED;
+    GemmPlan pl[4];
+    size_t own = 0;
+    for (int i = 0; i < n; ++i) {
+        if (ts[i]->K != ts[0]->K) return P8_ERR_ARG;
+        pl[i] = gemm_plan(ts[i], ncols, pk != P8_PROLOGUE_NONE);
+        if (pl[i].smem > (size_t)kGemmSmemDyn) return P8_ERR_UNSUPPORTED;
+        if (pl[i].own > own) own = pl[i].own;
+    }
+    const GemmPlan &p = pl[gemm_group_prep(pl, n)];
+    if (!ws || ws_bytes < p.prep + own || ((uintptr_t)ws & 255)) return P8_ERR_WORKSPACE;
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -817,6 +883,7 @@ p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t
             return P8_ERR_CUDA;
         attr_set[dev] = true;
     }
+    const p8_tensor *t = ts[0];
     uint8_t *w = static_cast<uint8_t *>(ws);
     GxArgs xa;
     memset(&xa, 0, sizeof(xa));
@@ -844,31 +911,16 @@ p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t
             cudaSuccess)
             return P8_ERR_CUDA;
     }
-    GemmArgs ga;
-    ga.A = t->A; ga.M = t->M; ga.D = t->D; ga.S = t->S; ga.prm = t->prm; ga.rsc = t->rsc; ga.cp = t->cp; ga.cc = t->cc;
-    ga.cv = t->cv; ga.Y = Y; ga.Xh = xa.Xh; ga.tdown = xa.tdown; ga.ldy = ldy; ga.cs = t->cs;
-    ga.X = pk != P8_PROLOGUE_NONE ? xa.xv : X;  // the clamp-delta term multiplies x'
-    ga.ldx = pk != P8_PROLOGUE_NONE ? t->K : ldx;
-    ga.rows = t->rows; ga.nb = t->nb; ga.ng = t->ng; ga.ncols = (int)ncols; ga.npad = p.npad; ga.bn = p.bn; ga.nbs = p.nbs;
-    ga.np = p.np; ga.tileb = p.tileb; ga.ucls = t->uniform_class;
-    ga.ksplit = p.ks; ga.mtr = p.mt * 128;
-    ga.kpart = reinterpret_cast<float *>(w + p.kpart);
-    ga.Yt = p.staged ? reinterpret_cast<float *>(w + p.yt) : nullptr;
-    ga.pinv = t->pinv;
-    void *args[] = {&ga};
-    if (launch_pdl((const void *)k_gemm, dim3(p.mt, p.nnt, p.ks), dim3(kGemmThreads), p.smem, st, args) != cudaSuccess)
-        return P8_ERR_CUDA;
-    if (p.staged) {
-        if (launch_pdl((const void *)k_unpermute, dim3((unsigned)((t->rows + 255) / 256), (unsigned)((ncols + 7) / 8)), dim3(256), 0,
-                       st, args) != cudaSuccess)
-            return P8_ERR_CUDA;
-    }
-    if (p.ks > 1) {
-        const long long outs = (long long)t->rows * ncols;
-        if (launch_pdl((const void *)k_splitk_reduce, dim3((unsigned)((outs + 255) / 256)), dim3(256), 0, st, args) != cudaSuccess)
-            return P8_ERR_CUDA;
+    for (int i = 0; i < n; ++i) {
+        const p8_status r = launch_gemm_one(ts[i], pl[i], xa, pk, X, ncols, ldx, Ys[i], ldys[i], w + p.prep, st);
+        if (r) return r;
     }
     return P8_OK;
+}
+
+p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy, void *ws,
+                      size_t ws_bytes, cudaStream_t st, const p8_prologue *pro) {
+    return launch_gemm_group(&t, 1, X, ncols, ldx, &Y, &ldy, ws, ws_bytes, st, pro);
 }
 
 // prepare-time part: per-row weight scales. bint = max |int| over the classes the tensor uses.

@@ -91,5 +91,8 @@ size_t gemm_workspace(const p8_tensor *t, int64_t ncols, bool pro = false);
 p8_status launch_gemm(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy, void *ws,
                       size_t ws_bytes, cudaStream_t st, const p8_prologue *pro = nullptr);
 bool gemm_supported(const p8_tensor *t, int64_t ncols);
+size_t gemm_group_workspace(const p8_tensor *const *ts, int n, int64_t ncols, bool pro = false);
+p8_status launch_gemm_group(const p8_tensor *const *ts, int n, const float *X, int64_t ncols, int64_t ldx, float *const *Ys,
+                            const int64_t *ldys, void *ws, size_t ws_bytes, cudaStream_t st, const p8_prologue *pro = nullptr);
 p8_status gemm_prepare(p8_tensor *t, cudaStream_t st);  // prepare-time per-row scales (rsc)
 }  // namespace p8

@@ -155,9 +155,10 @@ class P8Tensor:
             pass
 
 
-def group_workspace_size(tensors, ncols=1):
+def group_workspace_size(tensors, ncols=1, kind=0):
+    """workspace bytes of mul_mat_vec_group (ncols 1) and mul_mat_group over ncols tokens (prologue kind 0/1/2)"""
     arr = (C.c_void_p * len(tensors))(*[t.handle.value for t in tensors])
-    return int(lib().p8_workspace_size_group(arr, len(tensors), ncols))
+    return int(lib().p8_workspace_size_group_ex(arr, len(tensors), ncols, kind))
 
 
 def mul_mat_vec_group(tensors, x, outs=None, workspace=None, stream=None, norm_weight=None, eps=1e-5, up=None):
@@ -188,6 +189,45 @@ def mul_mat_vec_group(tensors, x, outs=None, workspace=None, stream=None, norm_w
     pro = Prologue(1, extra.data_ptr(), None, float(eps)) if norm_weight is not None else Prologue(2, None, extra.data_ptr(), 0.0)
     check(lib().p8_mul_mat_vec_group_ex(arr, n, _ptr(x), C.byref(pro), ys, _ptr(workspace), workspace.numel(),
                                         _stream(stream)), "p8_mul_mat_vec_group_ex")
+    return outs
+
+
+def mul_mat_group(tensors, X, outs=None, workspace=None, stream=None, norm_weight=None, eps=1e-5, up=None):
+    """Y_i = X W_i^T for tensors sharing X [ncols, K] (q/k/v, gate/up; <= 4): the activation prep, prologue included,
+    runs once (p8_mul_mat_group); bit-identical to separate P8Tensor.mul_mat calls. outs: float32 [ncols, rows_i]
+    with unit column stride; norm_weight / up as P8Tensor.mul_mat."""
+    if X.dim() == 2 and (X.stride(1) != 1 or X.stride(0) % 4 or X.data_ptr() % 16):
+        X = X.contiguous()
+    if X.dtype != torch.float32 or X.dim() != 2 or X.shape[1] != tensors[0].K or not X.is_cuda:
+        raise ValueError("X must be float32 CUDA [ncols, K]")
+    if norm_weight is not None and up is not None:
+        raise ValueError("one prologue per call: norm_weight or up")
+    n, nt = X.shape[0], len(tensors)
+    outs = outs if outs is not None else [torch.empty(n, t.rows, dtype=torch.float32, device=X.device) for t in tensors]
+    for t, o in zip(tensors, outs):
+        if o.dim() != 2 or o.shape[0] != n or o.shape[1] != t.rows or o.stride(1) != 1 or o.dtype != torch.float32:
+            raise ValueError("outs must be float32 [ncols, rows] with unit column stride")
+    from ._lib import Prologue
+
+    kind = 0
+    pro = None
+    if norm_weight is not None:
+        if norm_weight.dtype != torch.float32 or not norm_weight.is_cuda or norm_weight.numel() != X.shape[1]:
+            raise ValueError("norm_weight must be float32 CUDA with K elements")
+        norm_weight = norm_weight.contiguous()
+        pro, kind = Prologue(1, norm_weight.data_ptr(), None, float(eps)), 1
+    elif up is not None:
+        if up.shape != X.shape or up.stride() != X.stride() or up.dtype != torch.float32 or not up.is_cuda:
+            raise ValueError("up must be float32 CUDA with X's shape and strides")
+        pro, kind = Prologue(2, None, up.data_ptr(), 0.0), 2
+    arr = (C.c_void_p * nt)(*[t.handle.value for t in tensors])
+    ys = (C.c_void_p * nt)(*[o.data_ptr() for o in outs])
+    lds = (C.c_int64 * nt)(*[o.stride(0) for o in outs])
+    if workspace is None:
+        need = int(lib().p8_workspace_size_group_ex(arr, nt, n, kind))
+        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=X.device)
+    check(lib().p8_mul_mat_group(arr, nt, _ptr(X), n, X.stride(0), C.byref(pro) if pro is not None else None, ys, lds,
+                                 _ptr(workspace), workspace.numel(), _stream(stream)), "p8_mul_mat_group")
     return outs
 
 
