@@ -75,7 +75,10 @@ struct GemmArgs {
     uint32_t cs;
     int rows, nb, ng, ncols, npad, bn, nbs, np, tileb, ucls;
     int xpad;              // token count of Xh's panels (the prep's padding: >= npad when a group shares the prep)
-    int ksplit, mtr;       // split-K: CTAs per output tile along K; padded rows of the partials
+    int mt0;               // first row tile of this launch (the split-K tail launch covers the last row tiles)
+    int rs;                // sorted rows >= rs come from split-K partials: k_splitk_reduce covers [rs, rows),
+                           // k_unpermute [0, rs); partial rows are indexed from rs
+    int ksplit, mtr;       // split-K: CTAs per output tile along K; rows of the partials
     float *kpart;          // split-K partial accumulators [ksplit][npad][mtr] (raw fp32)
     float *Yt;             // (single split, many tokens) outputs in sorted-row order [mtr][npad], un-permuted after
     const int16_t *pinv;   // original row -> sorted row
@@ -496,7 +499,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
     for (int i = threadIdx.x; i < 256 * 32; i += kGemmThreads) cbk[i] = a.A[i >> 5] ^ 0x80808080u;
     // M words of the CTA's four row tiles (arithmetic for uniform single-class layouts)
     for (int i = threadIdx.x; i < 4 * a.nb; i += kGemmThreads) {
-        const int q = i / a.nb, b = i - q * a.nb, g = blockIdx.x * 4 + q;
+        const int q = i / a.nb, b = i - q * a.nb, g = ((int)blockIdx.x + a.mt0) * 4 + q;
         uint32_t m = 0u;
         if (g < a.ng) {
             const size_t ti = (size_t)g * a.nb + b;
@@ -510,7 +513,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
     if (warp < 8) {
         // ------------------------------------------------------------------ decoders
         const int q = warp & 3, hs = warp >> 2;
-        const int g = blockIdx.x * 4 + q;
+        const int g = ((int)blockIdx.x + a.mt0) * 4 + q;
         const bool tile = g < a.ng;
         const int r = g * 32 + lane;
         const float up = tile ? a.rsc[r].x : 0.f;
@@ -633,7 +636,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
         tc_fence_after();
         if (!acc_ok) ok = false;
         const int q = warp & 3, half = warp >> 2;
-        const int r = blockIdx.x * 128 + q * 32 + lane;
+        const int r = ((int)blockIdx.x + a.mt0) * 128 + q * 32 + lane;
         const bool row = r < a.rows;
         const int ro = row ? a.prm[r] : 0;
         const float down = row ? a.rsc[r].y : 0.f;
@@ -641,7 +644,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
         const int n0 = blockIdx.y * bn;
         const int cw = bn >> 1;
         if (a.ksplit > 1) {  // raw accumulators of this K range -> partials (k_splitk_reduce finishes them)
-            const int rp = blockIdx.x * 128 + q * 32 + lane;
+            const int rp = r - a.rs;
             for (int cc0 = half * cw; acc_ok && cc0 < (half + 1) * cw; cc0 += 16) {
                 uint32_t v[16];
                 tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)cc0, v);
@@ -707,7 +710,9 @@ __global__ void __launch_bounds__(256) k_unpermute(const __grid_constant__ GemmA
     pdl_launch_dependents();
     const int ro = blockIdx.x * 256 + threadIdx.x, n8 = blockIdx.y * 8;
     if (ro >= a.rows) return;
-    const float4 *src = reinterpret_cast<const float4 *>(a.Yt + (size_t)a.pinv[ro] * a.npad + n8);
+    const int r = a.pinv[ro];
+    if (r >= a.rs) return;  // a row of the split-K tail
+    const float4 *src = reinterpret_cast<const float4 *>(a.Yt + (size_t)r * a.npad + n8);
     const float4 u0 = __ldcg(src), u1 = __ldcg(src + 1);
     const float v[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
@@ -723,10 +728,11 @@ __global__ void __launch_bounds__(256) k_splitk_reduce(const __grid_constant__ G
     pdl_wait();  // the partials come from k_gemm
     pdl_launch_dependents();
     const long long i = (long long)blockIdx.x * 256 + threadIdx.x;
-    if (i >= (long long)a.rows * a.ncols) return;
-    const int n = (int)(i / a.rows), r = (int)(i - (long long)n * a.rows);
+    const int nr = a.rows - a.rs;
+    if (i >= (long long)nr * a.ncols) return;
+    const int n = (int)(i / nr), rr = (int)(i - (long long)n * nr), r = a.rs + rr;
     float acc = 0.f;
-    for (int z = 0; z < a.ksplit; ++z) acc = __fadd_rn(acc, __ldcg(a.kpart + ((size_t)z * a.npad + n) * a.mtr + r));
+    for (int z = 0; z < a.ksplit; ++z) acc = __fadd_rn(acc, __ldcg(a.kpart + ((size_t)z * a.npad + n) * a.mtr + rr));
     const int ro = a.prm[r];
     float y = __fmul_rn(__fmul_rn(acc, a.rsc[r].y), a.tdown[n]);
     const float *xn = a.X + (size_t)n * a.ldx;
@@ -738,6 +744,7 @@ __global__ void __launch_bounds__(256) k_splitk_reduce(const __grid_constant__ G
 // host side
 struct GemmPlan {
     int bn, nbs, np, tileb, npad, nkc, mt, nnt, ks;
+    int mh, kt;     // tail split (kt > 1): row tiles [0, mh) in whole waves, single split; [mh, mt) split kt ways
     size_t ss, xv;  // prologue only: partial sums of squares [npad][nkc], x' [npad][K]
     size_t yt;      // staged outputs [mt * 128][npad] (single split, >= kGemmStagedMinCols tokens), else 0 bytes
     bool staged;
@@ -757,14 +764,39 @@ static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols, bool pro = false) {
     const int nsm = sm_count();
     GemmPlan p;
     p.mt = (t->rows + 127) / 128;
-    // tile width: fewest waves, weighting a tile's time as its MMA share (BN) plus the decode it cannot hide
+    // Tile width and K split: the lowest estimated time. A tile's time is modelled as BN + 200 (the MMA share plus
+    // the decode and fixed part; the 200 is fitted to measured 128- and 256-wide tiles of the same projection).
+    // Tiles that leave at least half the SMs idle are split along K (ks CTAs per tile, at least two 256-column blocks
+    // each; time / ks). More tiles than SMs take whole waves, or a tail split: the row tiles of the full waves as
+    // one launch, the remaining row tiles as a second launch split kt ways along K (one wave of 1/kt-long tiles),
+    // charged 32 more for the extra launch and reduction. Widths below 64 are not used (no better in this model).
+    const int kmax = t->nb / 2 > 1 ? t->nb / 2 : 1;
     int best = 256;
     long long best_cost = -1;
-    for (int bn = 256; bn >= 32; bn >>= 1) {
-        const long long tiles = (long long)p.mt * ((ncols + bn - 1) / bn);
-        const long long waves = (tiles + nsm - 1) / nsm;
-        const long long cost = waves * ((bn > 64 ? bn : 64) + 32);
-        if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = bn; }
+    p.ks = 1;
+    p.mh = 0;
+    p.kt = 1;
+    for (int bn = 256; bn >= 64; bn >>= 1) {
+        const long long nnt = (ncols + bn - 1) / bn, tiles = (long long)p.mt * nnt, c = (long long)(bn + 200) * 64;
+        long long cost;
+        int ks = 1, mh = 0, kt = 1;
+        if (2 * tiles <= nsm) {
+            ks = (int)(nsm / tiles);
+            if (ks > kmax) ks = kmax;
+            cost = c / ks;
+        } else {
+            cost = (tiles + nsm - 1) / nsm * c;
+            if (tiles > nsm && tiles % nsm) {
+                const long long full = tiles / nsm;
+                const int h = (int)(full * nsm / nnt);
+                const long long tt = (long long)(p.mt - h) * nnt;
+                int k = h > 0 && tt > 0 ? (int)(nsm / tt) : 1;
+                if (k > kmax) k = kmax;
+                const long long ct = ((long long)h * nnt + nsm - 1) / nsm * c + c / (k > 1 ? k : 1) + 32 * 64;
+                if (k >= 2 && ct < cost) { cost = ct; mh = h; kt = k; }
+            }
+        }
+        if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = bn; p.ks = ks; p.mh = mh; p.kt = kt; }
     }
     p.bn = best;
     p.tileb = gemm_tile_bytes(t);
@@ -776,15 +808,6 @@ static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols, bool pro = false) {
     p.nnt = (int)((ncols + best - 1) / best);
     p.npad = p.nnt * best;
     p.nkc = (t->K + 2047) / 2048;
-    // split-K when the output tiles leave at least half the SMs idle (small batches): CTAs per tile along K, at
-    // least two 256-column blocks each
-    p.ks = 1;
-    const int base = p.mt * p.nnt;
-    if (2 * base <= nsm) {
-        p.ks = nsm / base;
-        const int kmax = t->nb / 2 > 1 ? t->nb / 2 : 1;
-        if (p.ks > kmax) p.ks = kmax;
-    }
     // workspace: the activation prep's part first (shared by the tensors of a group), then the tensor's own part
     p.xh = 0;
     p.pmax = al256((size_t)t->K * p.npad * 2);
@@ -794,7 +817,9 @@ static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols, bool pro = false) {
     p.prep = p.xv + (pro ? al256((size_t)p.npad * t->K * 4) : 0);
     p.staged = p.ks == 1 && ncols >= kGemmStagedMinCols;
     p.kpart = 0;
-    p.yt = p.kpart + (p.ks > 1 ? al256((size_t)p.ks * p.npad * p.mt * 128 * 4) : 0);
+    p.yt = p.kpart + (p.ks > 1   ? al256((size_t)p.ks * p.npad * p.mt * 128 * 4)
+                      : p.kt > 1 ? al256((size_t)p.kt * p.npad * (p.mt - p.mh) * 128 * 4)
+                                 : 0);
     p.own = p.yt + (p.staged ? al256((size_t)p.mt * 128 * p.npad * 4) : 0);
     p.total = p.prep + p.own;
     return p;
@@ -839,11 +864,31 @@ static p8_status launch_gemm_one(const p8_tensor *t, const GemmPlan &p, const Gx
     ga.rows = t->rows; ga.nb = t->nb; ga.ng = t->ng; ga.ncols = (int)ncols; ga.npad = p.npad; ga.bn = p.bn; ga.nbs = p.nbs;
     ga.np = p.np; ga.tileb = p.tileb; ga.ucls = t->uniform_class;
     ga.xpad = xa.npad;
+    ga.mt0 = 0;
     ga.ksplit = p.ks; ga.mtr = p.mt * 128;
+    ga.rs = p.ks > 1 ? 0 : t->rows;
     ga.kpart = reinterpret_cast<float *>(own + p.kpart);
     ga.Yt = p.staged ? reinterpret_cast<float *>(own + p.yt) : nullptr;
     ga.pinv = t->pinv;
     void *args[] = {&ga};
+    if (p.kt > 1) {  // tail split: the full waves, then the split-K tail; both before the epilogue kernels
+        GemmArgs gt = ga;
+        ga.rs = gt.rs = p.mh * 128;
+        gt.mt0 = p.mh;
+        gt.ksplit = p.kt;
+        gt.mtr = (p.mt - p.mh) * 128;
+        void *targs[] = {&gt};
+        if (launch_pdl((const void *)k_gemm, dim3(p.mh, p.nnt, 1), dim3(kGemmThreads), p.smem, st, args) != cudaSuccess ||
+            launch_pdl((const void *)k_gemm, dim3(p.mt - p.mh, p.nnt, p.kt), dim3(kGemmThreads), p.smem, st, targs) != cudaSuccess)
+            return P8_ERR_CUDA;
+        if (p.staged && launch_pdl((const void *)k_unpermute, dim3((unsigned)((t->rows + 255) / 256), (unsigned)((ncols + 7) / 8)),
+                                   dim3(256), 0, st, args) != cudaSuccess)
+            return P8_ERR_CUDA;
+        const long long outs = (long long)(t->rows - gt.rs) * ncols;
+        if (launch_pdl((const void *)k_splitk_reduce, dim3((unsigned)((outs + 255) / 256)), dim3(256), 0, st, targs) != cudaSuccess)
+            return P8_ERR_CUDA;
+        return P8_OK;
+    }
     if (launch_pdl((const void *)k_gemm, dim3(p.mt, p.nnt, p.ks), dim3(kGemmThreads), p.smem, st, args) != cudaSuccess)
         return P8_ERR_CUDA;
     if (p.staged) {

@@ -58,6 +58,25 @@ def test_gemm_vs_oracle_shapes(rows, K, ncols):
     assert rel(Y, o.mul_mat_f64(X)) < BAR
 
 
+@pytest.mark.parametrize("rows,K,ncols", [(20000, 1024, 40), (20000, 1024, 300), (9696, 2560, 512)])
+def test_gemm_tail_split(rows, K, ncols):
+    """Tile counts that fill some waves and leave a partial one: the row tiles of the full waves run single-split,
+    the rest as a second launch split along K (direct stores at 40 tokens, staged outputs at 300 and 512; ragged last
+    row tile at both row counts). The two smaller cases against the oracle, the 512-token one against the product
+    with the dequantized weight in fp64 (the dequant is bit-exact to the oracle's)."""
+    s = synth.make_slot(rows, K, seed=rows + ncols, nd=31)
+    t = P8Tensor(s, K, rows)
+    X = np.random.default_rng(ncols).normal(0, 1, (ncols, K)).astype(np.float32)
+    Xd = torch.from_numpy(X).cuda()
+    Y = gemm(t, Xd)
+    if ncols <= 300:
+        assert rel(Y.cpu().numpy(), Oracle(s, rows, K).mul_mat(X)) < BAR
+    else:
+        ref = (Xd.double() @ t.dequant().double().T)
+        assert float(torch.linalg.norm(Y.double() - ref) / torch.linalg.norm(ref)) < BAR
+    assert torch.equal(gemm(t, Xd), Y)  # deterministic (the tail's partials are summed in split order)
+
+
 @pytest.mark.parametrize("cls", [1, 2, 3, 4, 5, 6, 7])
 def test_gemm_each_class(cls):
     rows, K = 256, 1024
