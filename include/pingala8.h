@@ -110,7 +110,9 @@ p8_status p8_mul_mat_ex(const p8_tensor *t, const float *X, int64_t ncols, int64
 
 /* p8_mul_mat_ex for several tensors that read the same X (q/k/v, gate/up; n <= 4, requirements as
  * p8_mul_mat_vec_group, else P8_ERR_ARG): the activation prep, prologue included, runs once and each tensor's product
- * reads it; Y_i [ncols][ldys[i]]. Results are bit-identical to separate p8_mul_mat_ex calls. The reference's
+ * reads it; Y_i [ncols][ldys[i]]. Two consecutive tensors of one shape (gate/up) may share one GEMM launch when
+ * their row tiles fill the SMs' waves better together. Results are bit-identical to separate p8_mul_mat_ex calls,
+ * except the rows of a shared launch's last, K-split row tiles (same products, fp32 sums in another order). The reference's
  * activation cache (vrc_tg, CP:1171-1180) reuses a prepared x across consecutive tensors the same way; ggml has no
  * grouped op, so this entry point is an extension. Workspace p8_workspace_size_group_ex(ts, n, ncols, kind). */
 size_t p8_workspace_size_group_ex(const p8_tensor *const *ts, int n, int64_t ncols, int kind);

@@ -75,7 +75,6 @@ struct GemmArgs {
     uint32_t cs;
     int rows, nb, ng, ncols, npad, bn, nbs, np, tileb, ucls;
     int xpad;              // token count of Xh's panels (the prep's padding: >= npad when a group shares the prep)
-    int mt0;               // first row tile of this launch (the split-K tail launch covers the last row tiles)
     int rs;                // sorted rows >= rs come from split-K partials: k_splitk_reduce covers [rs, rows),
                            // k_unpermute [0, rs); partial rows are indexed from rs
     int ksplit, mtr;       // split-K: CTAs per output tile along K; rows of the partials
@@ -453,7 +452,18 @@ __host__ __device__ inline GemmSmem gemm_smem_layout(int bn, int nbs, int np, in
     return L;
 }
 
-__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant__ GemmArgs a) {
+// One k_gemm launch covers row tiles of one tensor, or of two tensors of one shape and plan that read the same
+// operand (the second's row tiles follow the first's, so both fill the same waves): global row tile gt =
+// blockIdx.x + mt0, tensor 1 from gt >= mtA. A launch can start past row tile 0 (the split-K tail of a tail split).
+template <int NT>
+struct GemmLaunch {
+    GemmArgs t[NT];
+    int mt0, mtA;
+};
+
+// the CTA's work on row tile mtile of one tensor; inlined once per tensor of the launch, so that every field of
+// the tensor's arguments is read at a fixed parameter offset
+__device__ __forceinline__ void gemm_cta(const GemmArgs &a, const int mtile) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bn = a.bn, nbs = a.nbs, np = a.np;
     const int stageB = bn * 256, stageP = 4 * a.tileb;
@@ -499,7 +509,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
     for (int i = threadIdx.x; i < 256 * 32; i += kGemmThreads) cbk[i] = a.A[i >> 5] ^ 0x80808080u;
     // M words of the CTA's four row tiles (arithmetic for uniform single-class layouts)
     for (int i = threadIdx.x; i < 4 * a.nb; i += kGemmThreads) {
-        const int q = i / a.nb, b = i - q * a.nb, g = ((int)blockIdx.x + a.mt0) * 4 + q;
+        const int q = i / a.nb, b = i - q * a.nb, g = mtile * 4 + q;
         uint32_t m = 0u;
         if (g < a.ng) {
             const size_t ti = (size_t)g * a.nb + b;
@@ -513,7 +523,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
     if (warp < 8) {
         // ------------------------------------------------------------------ decoders
         const int q = warp & 3, hs = warp >> 2;
-        const int g = ((int)blockIdx.x + a.mt0) * 4 + q;
+        const int g = mtile * 4 + q;
         const bool tile = g < a.ng;
         const int r = g * 32 + lane;
         const float up = tile ? a.rsc[r].x : 0.f;
@@ -636,7 +646,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
         tc_fence_after();
         if (!acc_ok) ok = false;
         const int q = warp & 3, half = warp >> 2;
-        const int r = ((int)blockIdx.x + a.mt0) * 128 + q * 32 + lane;
+        const int r = mtile * 128 + q * 32 + lane;
         const bool row = r < a.rows;
         const int ro = row ? a.prm[r] : 0;
         const float down = row ? a.rsc[r].y : 0.f;
@@ -703,6 +713,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant_
     }
 }
 
+template <int NT>
+__global__ void __launch_bounds__(kGemmThreads, 1) k_gemm(const __grid_constant__ GemmLaunch<NT> gl) {
+    const int gt = (int)blockIdx.x + gl.mt0;  // uniform per CTA
+    if (NT > 1 && gt >= gl.mtA)
+        gemm_cta(gl.t[NT - 1], gt - gl.mtA);
+    else
+        gemm_cta(gl.t[0], gt);
+}
+
 // Outputs staged in sorted-row order (Yt) to Y: thread = (original row ro, 8 tokens); reads the 8 tokens of sorted row
 // pinv[ro] (32 contiguous bytes), writes Y[n][ro] (a warp's 32 consecutive rows: one coalesced store per token).
 __global__ void __launch_bounds__(256) k_unpermute(const __grid_constant__ GemmArgs a) {
@@ -744,12 +763,15 @@ __global__ void __launch_bounds__(256) k_splitk_reduce(const __grid_constant__ G
 // host side
 struct GemmPlan {
     int bn, nbs, np, tileb, npad, nkc, mt, nnt, ks;
-    int mh, kt;     // tail split (kt > 1): row tiles [0, mh) in whole waves, single split; [mh, mt) split kt ways
-    size_t ss, xv;  // prologue only: partial sums of squares [npad][nkc], x' [npad][K]
-    size_t yt;      // staged outputs [mt * 128][npad] (single split, >= kGemmStagedMinCols tokens), else 0 bytes
-    bool staged;
+    int nten;        // tensors in one launch: 1, or 2 of one shape whose row tiles fill the same waves
+    int mh, kt;      // tail split (kt > 1): row tiles [0, mh) of the launch single-split in whole waves, the rest split kt
+                     // ways along K (with two tensors the tail lies in the second)
+    long long cost;  // modelled time
+    size_t ss, xv;   // prologue only: partial sums of squares [npad][nkc], x' [npad][K]
+    bool staged;     // single split, >= kGemmStagedMinCols tokens: outputs staged in sorted-row order, then un-permuted
     size_t xh, pmax, tdown, prep;  // the activation prep's part [0, prep)
-    size_t kpart, own;             // the tensor's own part, offsets from its start; own = its size
+    size_t kpart, yt, own;         // the launch's own part (offsets from its start; own = its size): split-K
+                                   // partials, then staged outputs [mt * 128][npad] per tensor
     size_t total, smem;
 };
 
@@ -760,10 +782,12 @@ static int gemm_tile_bytes(const p8_tensor *t) {  // staging bytes of one tile's
     return m * 128;
 }
 
-static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols, bool pro = false) {
+static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols, bool pro = false, int nten = 1) {
     const int nsm = sm_count();
     GemmPlan p;
+    p.nten = nten;
     p.mt = (t->rows + 127) / 128;
+    const int mtg = nten * p.mt;  // row tiles of the launch
     // Tile width and K split: the lowest estimated time. A tile's time is modelled as BN + 200 (the MMA share plus
     // the decode and fixed part; the 200 is fitted to measured 128- and 256-wide tiles of the same projection).
     // Tiles that leave at least half the SMs idle are split along K (ks CTAs per tile, at least two 256-column blocks
@@ -777,7 +801,7 @@ static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols, bool pro = false) {
     p.mh = 0;
     p.kt = 1;
     for (int bn = 256; bn >= 64; bn >>= 1) {
-        const long long nnt = (ncols + bn - 1) / bn, tiles = (long long)p.mt * nnt, c = (long long)(bn + 200) * 64;
+        const long long nnt = (ncols + bn - 1) / bn, tiles = (long long)mtg * nnt, c = (long long)(bn + 200) * 64;
         long long cost;
         int ks = 1, mh = 0, kt = 1;
         if (2 * tiles <= nsm) {
@@ -789,7 +813,7 @@ static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols, bool pro = false) {
             if (tiles > nsm && tiles % nsm) {
                 const long long full = tiles / nsm;
                 const int h = (int)(full * nsm / nnt);
-                const long long tt = (long long)(p.mt - h) * nnt;
+                const long long tt = (long long)(mtg - h) * nnt;
                 int k = h > 0 && tt > 0 ? (int)(nsm / tt) : 1;
                 if (k > kmax) k = kmax;
                 const long long ct = ((long long)h * nnt + nsm - 1) / nsm * c + c / (k > 1 ? k : 1) + 32 * 64;
@@ -798,6 +822,7 @@ static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols, bool pro = false) {
         }
         if (best_cost < 0 || cost < best_cost) { best_cost = cost; best = bn; p.ks = ks; p.mh = mh; p.kt = kt; }
     }
+    p.cost = best_cost;
     p.bn = best;
     p.tileb = gemm_tile_bytes(t);
     p.nbs = best >= 256 ? 2 : best >= 128 ? 3 : kGemmMaxB;
@@ -808,7 +833,7 @@ static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols, bool pro = false) {
     p.nnt = (int)((ncols + best - 1) / best);
     p.npad = p.nnt * best;
     p.nkc = (t->K + 2047) / 2048;
-    // workspace: the activation prep's part first (shared by the tensors of a group), then the tensor's own part
+    // workspace: the activation prep's part first (shared by the tensors of a group), then the launch's own part
     p.xh = 0;
     p.pmax = al256((size_t)t->K * p.npad * 2);
     p.tdown = p.pmax + al256((size_t)p.npad * p.nkc * 4);
@@ -817,10 +842,10 @@ static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols, bool pro = false) {
     p.prep = p.xv + (pro ? al256((size_t)p.npad * t->K * 4) : 0);
     p.staged = p.ks == 1 && ncols >= kGemmStagedMinCols;
     p.kpart = 0;
-    p.yt = p.kpart + (p.ks > 1   ? al256((size_t)p.ks * p.npad * p.mt * 128 * 4)
-                      : p.kt > 1 ? al256((size_t)p.kt * p.npad * (p.mt - p.mh) * 128 * 4)
+    p.yt = p.kpart + (p.ks > 1   ? al256((size_t)p.ks * p.npad * mtg * 128 * 4)
+                      : p.kt > 1 ? al256((size_t)p.kt * p.npad * (mtg - p.mh) * 128 * 4)
                                  : 0);
-    p.own = p.yt + (p.staged ? al256((size_t)p.mt * 128 * p.npad * 4) : 0);
+    p.own = p.yt + (p.staged ? (size_t)nten * al256((size_t)p.mt * 128 * p.npad * 4) : 0);
     p.total = p.prep + p.own;
     return p;
 }
@@ -832,31 +857,61 @@ bool gemm_supported(const p8_tensor *t, int64_t ncols) {
 
 size_t gemm_workspace(const p8_tensor *t, int64_t ncols, bool pro) { return gemm_plan(t, ncols, pro).total; }
 
-// A group's tensors (equal K and prepared-activation hash) share one activation prep. Their plans may pad the tokens
-// differently (the tile width follows the row count), so the prep pads to the largest npad: Xh's panels carry that
-// token count (GemmArgs::xpad) and each tensor reads its first npad tokens, which are the same as its own prep's.
-// The tensors' own parts (split-K partials, staged outputs) follow the prep's part and are reused one after another.
-static int gemm_group_prep(const GemmPlan *pl, int n) {
+// A group's tensors (equal K and prepared-activation hash) share one activation prep and run as launches of one
+// tensor, or of two consecutive tensors of one shape (gate/up, k/v) when their row tiles together fill the waves
+// better than apart. A pair shares a launch only where both tensors alone would run single-split without a tail, so
+// that every row keeps its K order except the rows of a shared launch's tail split (then summed over kt splits).
+// The launches' plans may pad the tokens differently (the tile width follows the row count), so the prep pads to
+// the largest npad: Xh's panels carry that token count (GemmArgs::xpad) and each launch reads its first npad
+// tokens, which are the same as its own prep's. The launches' own parts follow the prep's part, one after another.
+struct GemmItem {
+    int i0;
+    GemmPlan p;
+};
+
+static int gemm_group_items(const p8_tensor *const *ts, int n, int64_t ncols, bool pro, GemmItem *it) {
+    int m = 0;
+    for (int i = 0; i < n;) {
+        const GemmPlan p1 = gemm_plan(ts[i], ncols, pro);
+        if (i + 1 < n && ts[i + 1]->rows == ts[i]->rows && gemm_tile_bytes(ts[i + 1]) == gemm_tile_bytes(ts[i])) {
+            const GemmPlan p2 = gemm_plan(ts[i + 1], ncols, pro);
+            const GemmPlan pp = gemm_plan(ts[i], ncols, pro, 2);
+            if (p1.ks == 1 && p1.kt == 1 && p2.ks == 1 && p2.kt == 1 && pp.ks == 1 && (pp.kt == 1 || pp.mh >= pp.mt) &&
+                pp.cost < p1.cost + p2.cost) {
+                it[m].i0 = i;
+                it[m++].p = pp;
+                i += 2;
+                continue;
+            }
+        }
+        it[m].i0 = i;
+        it[m++].p = p1;
+        ++i;
+    }
+    return m;
+}
+
+static int gemm_items_prep(const GemmItem *it, int m, size_t *own) {
     int j = 0;
-    for (int i = 1; i < n; ++i)
-        if (pl[i].npad > pl[j].npad) j = i;
+    *own = 0;
+    for (int i = 0; i < m; ++i) {
+        if (it[i].p.npad > it[j].p.npad) j = i;
+        if (it[i].p.own > *own) *own = it[i].p.own;
+    }
     return j;
 }
 
 size_t gemm_group_workspace(const p8_tensor *const *ts, int n, int64_t ncols, bool pro) {
     if (n < 1 || n > 4) return 0;
-    GemmPlan pl[4];
+    GemmItem it[4];
+    const int m = gemm_group_items(ts, n, ncols, pro, it);
     size_t own = 0;
-    for (int i = 0; i < n; ++i) {
-        pl[i] = gemm_plan(ts[i], ncols, pro);
-        if (pl[i].own > own) own = pl[i].own;
-    }
-    return pl[gemm_group_prep(pl, n)].prep + own;
+    const int j = gemm_items_prep(it, m, &own);
+    return it[j].p.prep + own;
 }
 
-static p8_status launch_gemm_one(const p8_tensor *t, const GemmPlan &p, const GxArgs &xa, int pk, const float *X, int64_t ncols,
-                                 int64_t ldx, float *Y, int64_t ldy, uint8_t *own, cudaStream_t st) {
-    GemmArgs ga;
+static void launch_args(GemmArgs &ga, const p8_tensor *t, const GemmPlan &p, const GxArgs &xa, int pk, const float *X,
+                        int64_t ncols, int64_t ldx, float *Y, int64_t ldy) {
     ga.A = t->A; ga.M = t->M; ga.D = t->D; ga.S = t->S; ga.prm = t->prm; ga.rsc = t->rsc; ga.cp = t->cp; ga.cc = t->cc;
     ga.cv = t->cv; ga.Y = Y; ga.Xh = xa.Xh; ga.tdown = xa.tdown; ga.ldy = ldy; ga.cs = t->cs;
     ga.X = pk != P8_PROLOGUE_NONE ? xa.xv : X;  // the clamp-delta term multiplies x'
@@ -864,67 +919,82 @@ static p8_status launch_gemm_one(const p8_tensor *t, const GemmPlan &p, const Gx
     ga.rows = t->rows; ga.nb = t->nb; ga.ng = t->ng; ga.ncols = (int)ncols; ga.npad = p.npad; ga.bn = p.bn; ga.nbs = p.nbs;
     ga.np = p.np; ga.tileb = p.tileb; ga.ucls = t->uniform_class;
     ga.xpad = xa.npad;
-    ga.mt0 = 0;
-    ga.ksplit = p.ks; ga.mtr = p.mt * 128;
-    ga.rs = p.ks > 1 ? 0 : t->rows;
-    ga.kpart = reinterpret_cast<float *>(own + p.kpart);
-    ga.Yt = p.staged ? reinterpret_cast<float *>(own + p.yt) : nullptr;
     ga.pinv = t->pinv;
-    void *args[] = {&ga};
-    if (p.kt > 1) {  // tail split: the full waves, then the split-K tail; both before the epilogue kernels
-        GemmArgs gt = ga;
-        ga.rs = gt.rs = p.mh * 128;
-        gt.mt0 = p.mh;
-        gt.ksplit = p.kt;
-        gt.mtr = (p.mt - p.mh) * 128;
-        void *targs[] = {&gt};
-        if (launch_pdl((const void *)k_gemm, dim3(p.mh, p.nnt, 1), dim3(kGemmThreads), p.smem, st, args) != cudaSuccess ||
-            launch_pdl((const void *)k_gemm, dim3(p.mt - p.mh, p.nnt, p.kt), dim3(kGemmThreads), p.smem, st, targs) != cudaSuccess)
-            return P8_ERR_CUDA;
-        if (p.staged && launch_pdl((const void *)k_unpermute, dim3((unsigned)((t->rows + 255) / 256), (unsigned)((ncols + 7) / 8)),
-                                   dim3(256), 0, st, args) != cudaSuccess)
-            return P8_ERR_CUDA;
-        const long long outs = (long long)(t->rows - gt.rs) * ncols;
-        if (launch_pdl((const void *)k_splitk_reduce, dim3((unsigned)((outs + 255) / 256)), dim3(256), 0, st, targs) != cudaSuccess)
-            return P8_ERR_CUDA;
-        return P8_OK;
+}
+
+// one launch of NT (1 or 2) tensors: k_gemm (with a tail split: the full waves, then the split-K tail), then the
+// epilogue kernels (un-permute of staged outputs per tensor, split-K reduction)
+template <int NT>
+static p8_status launch_gemm_item(const p8_tensor *const *ts, const GemmPlan &p, const GxArgs &xa, int pk, const float *X,
+                                  int64_t ncols, int64_t ldx, float *const *Ys, const int64_t *ldys, uint8_t *own,
+                                  cudaStream_t st) {
+    GemmLaunch<NT> gl;
+    memset(&gl, 0, sizeof(gl));
+    const int mtg = NT * p.mt, last = NT - 1;
+    for (int i = 0; i < NT; ++i) {
+        GemmArgs &ga = gl.t[i];
+        launch_args(ga, ts[i], p, xa, pk, X, ncols, ldx, Ys[i], ldys[i]);
+        ga.ksplit = p.ks;
+        ga.mtr = p.mt * 128;
+        ga.rs = p.ks > 1 ? 0 : ts[i]->rows;
+        ga.kpart = reinterpret_cast<float *>(own + p.kpart);
+        ga.Yt = p.staged ? reinterpret_cast<float *>(own + p.yt + (size_t)i * al256((size_t)p.mt * 128 * p.npad * 4)) : nullptr;
     }
-    if (launch_pdl((const void *)k_gemm, dim3(p.mt, p.nnt, p.ks), dim3(kGemmThreads), p.smem, st, args) != cudaSuccess)
+    gl.mt0 = 0;
+    gl.mtA = NT > 1 ? p.mt : mtg;
+    const void *fn = (const void *)k_gemm<NT>;
+    void *args[] = {&gl};
+    GemmLaunch<NT> tl = gl;
+    if (p.kt > 1) {
+        gl.t[last].rs = (p.mh - last * p.mt) * 128;  // the tail's first row in the last tensor
+        tl = gl;
+        tl.mt0 = p.mh;
+        tl.t[last].ksplit = p.kt;
+        tl.t[last].mtr = (mtg - p.mh) * 128;
+        void *targs[] = {&tl};
+        if (launch_pdl(fn, dim3(p.mh, p.nnt, 1), dim3(kGemmThreads), p.smem, st, args) != cudaSuccess ||
+            launch_pdl(fn, dim3(mtg - p.mh, p.nnt, p.kt), dim3(kGemmThreads), p.smem, st, targs) != cudaSuccess)
+            return P8_ERR_CUDA;
+    } else if (launch_pdl(fn, dim3(mtg, p.nnt, p.ks), dim3(kGemmThreads), p.smem, st, args) != cudaSuccess) {
         return P8_ERR_CUDA;
-    if (p.staged) {
-        if (launch_pdl((const void *)k_unpermute, dim3((unsigned)((t->rows + 255) / 256), (unsigned)((ncols + 7) / 8)), dim3(256), 0,
-                       st, args) != cudaSuccess)
+    }
+    for (int i = 0; p.staged && i < NT; ++i) {
+        void *uargs[] = {&gl.t[i]};
+        if (launch_pdl((const void *)k_unpermute, dim3((unsigned)((ts[i]->rows + 255) / 256), (unsigned)((ncols + 7) / 8)), dim3(256),
+                       0, st, uargs) != cudaSuccess)
             return P8_ERR_CUDA;
     }
-    if (p.ks > 1) {
-        const long long outs = (long long)t->rows * ncols;
-        if (launch_pdl((const void *)k_splitk_reduce, dim3((unsigned)((outs + 255) / 256)), dim3(256), 0, st, args) != cudaSuccess)
+    if (p.ks > 1 || p.kt > 1) {
+        GemmArgs *ra = p.kt > 1 ? &tl.t[last] : &gl.t[0];
+        void *rargs[] = {ra};
+        const long long outs = (long long)(ra->rows - ra->rs) * ncols;
+        if (launch_pdl((const void *)k_splitk_reduce, dim3((unsigned)((outs + 255) / 256)), dim3(256), 0, st, rargs) != cudaSuccess)
             return P8_ERR_CUDA;
     }
     return P8_OK;
 }
 
-// tensors reading the same X (equal K and activation hash, checked by the caller): one activation prep, then each
-// tensor's product
+// tensors reading the same X (equal K and activation hash, checked by the caller): one activation prep, then the
+// group's launches
 p8_status launch_gemm_group(const p8_tensor *const *ts, int n, const float *X, int64_t ncols, int64_t ldx, float *const *Ys,
                             const int64_t *ldys, void *ws, size_t ws_bytes, cudaStream_t st, const p8_prologue *pro) {
     if (n < 1 || n > 4) return P8_ERR_ARG;
     const int pk = pro ? pro->kind : P8_PROLOGUE_NONE;
-    GemmPlan pl[4];
-    size_t own = 0;
-    for (int i = 0; i < n; ++i) {
+    for (int i = 0; i < n; ++i)
         if (ts[i]->K != ts[0]->K) return P8_ERR_ARG;
-        pl[i] = gemm_plan(ts[i], ncols, pk != P8_PROLOGUE_NONE);
-        if (pl[i].smem > (size_t)kGemmSmemDyn) return P8_ERR_UNSUPPORTED;
-        if (pl[i].own > own) own = pl[i].own;
-    }
-    const GemmPlan &p = pl[gemm_group_prep(pl, n)];
+    GemmItem it[4];
+    const int m = gemm_group_items(ts, n, ncols, pk != P8_PROLOGUE_NONE, it);
+    for (int i = 0; i < m; ++i)
+        if (it[i].p.smem > (size_t)kGemmSmemDyn) return P8_ERR_UNSUPPORTED;
+    size_t own = 0;
+    const GemmPlan &p = it[gemm_items_prep(it, m, &own)].p;
     if (!ws || ws_bytes < p.prep + own || ((uintptr_t)ws & 255)) return P8_ERR_WORKSPACE;
     static bool attr_set[64] = {false};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        if (cudaFuncSetAttribute(k_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemDyn) != cudaSuccess)
+        if (cudaFuncSetAttribute(k_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemDyn) != cudaSuccess ||
+            cudaFuncSetAttribute(k_gemm<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemDyn) != cudaSuccess)
             return P8_ERR_CUDA;
         attr_set[dev] = true;
     }
@@ -956,8 +1026,11 @@ p8_status launch_gemm_group(const p8_tensor *const *ts, int n, const float *X, i
             cudaSuccess)
             return P8_ERR_CUDA;
     }
-    for (int i = 0; i < n; ++i) {
-        const p8_status r = launch_gemm_one(ts[i], pl[i], xa, pk, X, ncols, ldx, Ys[i], ldys[i], w + p.prep, st);
+    for (int i = 0; i < m; ++i) {
+        const int i0 = it[i].i0;
+        const p8_status r =
+            it[i].p.nten > 1 ? launch_gemm_item<2>(ts + i0, it[i].p, xa, pk, X, ncols, ldx, Ys + i0, ldys + i0, w + p.prep, st)
+                             : launch_gemm_item<1>(ts + i0, it[i].p, xa, pk, X, ncols, ldx, Ys + i0, ldys + i0, w + p.prep, st);
         if (r) return r;
     }
     return P8_OK;

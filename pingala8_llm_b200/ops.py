@@ -194,7 +194,8 @@ def mul_mat_vec_group(tensors, x, outs=None, workspace=None, stream=None, norm_w
 
 def mul_mat_group(tensors, X, outs=None, workspace=None, stream=None, norm_weight=None, eps=1e-5, up=None):
     """Y_i = X W_i^T for tensors sharing X [ncols, K] (q/k/v, gate/up; <= 4): the activation prep, prologue included,
-    runs once (p8_mul_mat_group); bit-identical to separate P8Tensor.mul_mat calls. outs: float32 [ncols, rows_i]
+    runs once (p8_mul_mat_group); bit-identical to separate P8Tensor.mul_mat calls except the K-split tail rows of
+    two tensors that share one launch (fp32 summation order). outs: float32 [ncols, rows_i]
     with unit column stride; norm_weight / up as P8Tensor.mul_mat."""
     if X.dim() == 2 and (X.stride(1) != 1 or X.stride(0) % 4 or X.data_ptr() % 16):
         X = X.contiguous()
