@@ -31,6 +31,9 @@ def main():
     ap.add_argument("--copies", type=int, default=1)
     ap.add_argument("--graph", action="store_true", help="capture the calls in a CUDA graph (no host launch overhead)")
     ap.add_argument("--ncols", type=int, default=1, help="tokens per call; > 1 runs the batched product per tensor")
+    ap.add_argument("--grouped", action="store_true",
+                    help="with --ncols > 1: the group as one grouped product (mul_mat_group: one activation prep, "
+                         "tensors of one shape in one launch where that fills the waves better)")
     ap.add_argument("--encode", type=int, default=0, help="run the trellis encoder on ROWS x 4096 instead")
     a = ap.parse_args()
     if a.encode:
@@ -76,15 +79,25 @@ def run_batched(a, shapes):
     ts = [P8Tensor(synth.make_slot_device(r, k, seed=i), k, r) for i, (r, k) in enumerate(shapes)]
     X = torch.randn(a.ncols, shapes[0][1], device="cuda")
     outs = [torch.empty(a.ncols, r, device="cuda") for r, _ in shapes]
-    ws = [t.workspace(a.ncols) for t in ts]
-    for t, y, w in zip(ts, outs, ws):  # warm-up
-        t.mul_mat(X, out=y, workspace=w)
+    if a.grouped:
+        from .ops import mul_mat_group
+
+        gws = torch.empty(max(group_workspace_size(ts, a.ncols), 256), dtype=torch.uint8, device="cuda")
+
+        def once():
+            mul_mat_group(ts, X, outs=outs, workspace=gws)
+    else:
+        ws = [t.workspace(a.ncols) for t in ts]
+
+        def once():
+            for t, y, w in zip(ts, outs, ws):
+                t.mul_mat(X, out=y, workspace=w)
+    once()  # warm-up
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(a.iters):
-        for t, y, w in zip(ts, outs, ws):
-            t.mul_mat(X, out=y, workspace=w)
+        once()
     e1.record()
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / a.iters
