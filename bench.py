@@ -15,10 +15,11 @@ CUDA graph and replayed per step. Attention, norms and the LM head are not part 
             duration, timed with CUDA events around a graph of that call type's 32 per-layer calls, against
             MEASURED_PEAKS.json hbm_gbs; traffic = DRAM bytes of the same call from an ncu capture
   cpu_baseline  the reference's own CPU core (oracle/_ref, x16 vrc_tg) on one layer's 7 GEMVs, all host threads
-  prefill   (1 GPU) the batched product: 512 tokens through all 224 projections (tcgen05 GEMM), TFLOP/s against
-            MEASURED_PEAKS.json bf16_tflops
-  batched_decode  (1 GPU) bs = 8, 32, 64 sequences stepping together through the same chain, every call the batched
-            product (split-K tcgen05 GEMM at these token counts): tok/s per bs
+  prefill   (1 GPU) the batched product: 512 tokens through all 224 projections (tcgen05 GEMM), the projections on
+            one input as grouped products (p8_mul_mat_group), TFLOP/s against MEASURED_PEAKS.json bf16_tflops; the
+            same pass as separate p8_mul_mat calls beside it
+  batched_decode  (1 GPU) bs = 8, 32, 64 sequences stepping together through the same chain, every group call the
+            grouped batched product (split-K tcgen05 GEMM at these token counts): tok/s per bs
   layer_prologues (1 GPU) the chain with each layer's input ops (RMSNorm x weight, SwiGLU) fused into the GEMV's
             activation prep, against the same ops as separate torch kernels
 
