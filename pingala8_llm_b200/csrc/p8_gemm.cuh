@@ -505,8 +505,12 @@ __device__ __forceinline__ void gemm_cta(const GemmArgs &a, const int mtile) {
     // set-up, the payload ring and the decoders run before the wait for the preceding kernels; the two roles that read
     // what those kernels write wait first: the activation-tile loader (prepared operand) and the epilogue (x, the
     // per-token scales, the outputs).
-    // lane-private codebook (entry f of lane l at word 32 f + l: a warp's lookups never share a bank), bytes + 128
-    for (int i = threadIdx.x; i < 256 * 32; i += kGemmThreads) cbk[i] = a.A[i >> 5] ^ 0x80808080u;
+    // lane-private codebook (entry f of lane l at word 32 f + l: a warp's lookups never share a bank), bytes + 128;
+    // written as 16-byte groups (group i = words 4i..4i+3, all of entry i / 8): one load and one store per group
+    for (int i = threadIdx.x; i < 256 * 8; i += kGemmThreads) {
+        const uint32_t v = __ldg(a.A + (i >> 3)) ^ 0x80808080u;
+        reinterpret_cast<uint4 *>(cbk)[i] = make_uint4(v, v, v, v);
+    }
     // M words of the CTA's four row tiles (arithmetic for uniform single-class layouts)
     for (int i = threadIdx.x; i < 4 * a.nb; i += kGemmThreads) {
         const int q = i / a.nb, b = i - q * a.nb, g = mtile * 4 + q;
