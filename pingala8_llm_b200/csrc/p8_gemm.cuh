@@ -881,7 +881,7 @@ static int gemm_group_items(const p8_tensor *const *ts, int n, int64_t ncols, bo
             const GemmPlan p2 = gemm_plan(ts[i + 1], ncols, pro);
             const GemmPlan pp = gemm_plan(ts[i], ncols, pro, 2);
             if (p1.ks == 1 && p1.kt == 1 && p2.ks == 1 && p2.kt == 1 && pp.ks == 1 && (pp.kt == 1 || pp.mh >= pp.mt) &&
-                pp.cost < p1.cost + p2.cost) {
+                pp.smem <= (size_t)kGemmSmemDyn && pp.cost < p1.cost + p2.cost) {
                 it[m].i0 = i;
                 it[m++].p = pp;
                 i += 2;
