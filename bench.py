@@ -167,24 +167,40 @@ def measured_peaks():
 
 
 # ------------------------------------------------------------------------------------------------ CPU reference leg
-def cpu_reference_layer(model, reps, warmup, seed=0):
-    """Reference CPU core (vrc_tg, x16) over one layer's 7 projections; returns per-layer seconds (median of reps)."""
-    from oracle.oracle import RefOracle
-    from pingala8_llm_b200 import synth
+_REF_CACHE = {}
 
-    shapes = layer_shapes(model)
-    mats = []
-    for i, (nm, rows, K) in enumerate(shapes):
-        s = synth.make_slot(rows, K, seed=seed + i)
-        mats.append((RefOracle(s, rows, K), np.random.default_rng(i).normal(0, 1, K).astype(np.float32)))
+
+def cpu_reference_token(model, reps, warmup, seed=0):
+    """The reference's own CPU core (oracle/_ref: vr-native-cpu-core.h with the vrc_tg glue, x16 activations) over one
+    decode token: every projection of every layer, 32 x 7 distinct class-3 slots (1.80 GB, far larger than any host
+    cache, so weights stream from DRAM as on the GPU). Slots are built with numpy (oracle/synth_np.py): this leg never
+    loads the product library. OpenMP threads = all host cores, set explicitly (torchrun exports OMP_NUM_THREADS=1).
+    Returns (median seconds per token, threads, ISA)."""
+    from oracle import synth_np
+    from oracle.oracle import RefOracle
+
+    ncores = os.cpu_count() or 1
+    RefOracle.set_threads(ncores)
+    key = (model["name"], seed)
+    if key not in _REF_CACHE:
+        mats = []
+        for L in range(model["layers"]):
+            for i, (nm, rows, K) in enumerate(layer_shapes(model)):
+                mats.append(RefOracle(synth_np.make_slot(rows, K, seed=seed + 1000 * L + 17 * i), rows, K))
+        xs = {K: np.random.default_rng(K).normal(0, 1, K).astype(np.float32) for _, _, K in layer_shapes(model)}
+        _REF_CACHE[key] = (mats, xs)
+    mats, xs = _REF_CACHE[key]
+
+    def token():
+        for r in mats:
+            r.gemv(xs[r.K])
+
     for _ in range(warmup):
-        for r, x in mats:
-            r.gemv(x)
+        token()
     ts = []
     for _ in range(reps):
         t0 = time.perf_counter()
-        for r, x in mats:
-            r.gemv(x)
+        token()
         ts.append(time.perf_counter() - t0)
     return statistics.median(ts), RefOracle.threads(), RefOracle.isa()
 
@@ -193,16 +209,17 @@ def run_reference(args, rank, world):
     model = LLAMA8B
     if rank != 0:
         return 0
-    layer_s, cores, isa = cpu_reference_layer(model, reps=max(1, args.steps), warmup=max(1, args.warmup))
-    tok_s = 1.0 / (model["layers"] * layer_s)
+    tok_s_time, cores, isa = cpu_reference_token(model, reps=max(1, args.steps), warmup=max(1, args.warmup))
+    tok_s = 1.0 / tok_s_time
     line = {
         "impl": "reference", "metric": METRIC, "value": round(tok_s, 4), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(1e3 * model["layers"] * layer_s, 3), "higher_is_better": True,
+        "warmup": args.warmup, "ms_per_step": round(1e3 * tok_s_time, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int32+fp32 (x16 activations)", "data": "synthetic",
         "config": {"workload": "llama3.1-8b-bs1-decode-projections", "layers": model["layers"], "projections_per_layer": 7,
                    "batch": 1, "classes": "3"},
         "cpu_baseline": {"value": round(tok_s, 4), "unit": "tok/s", "cores": cores, "kind": "reference",
-                         "sample": f"1 of {model['layers']} layers (7 GEMVs) per step, x{model['layers']}; {isa} vr-native-cpu-core.h"},
+                         "sample": f"every step one token: all {model['layers'] * 7} projections, distinct slots (1.80 GB); "
+                                   f"median of {max(1, args.steps)}; {isa} vr-native-cpu-core.h, {cores} OpenMP threads"},
         "e2e": {"value": round(tok_s, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -228,8 +245,7 @@ def run_b200(args, rank, world, local_rank):
     plan = tp.layer_plan(dims, world, rank)
     local = {}  # name -> (rows, K) of this rank's shard
     for nm, rows, K in shapes:
-        kind, _, lo, hi, _, _ = plan[nm]
-        local[nm] = (hi - lo, K) if kind == "col" else (rows, hi - lo)
+        local[nm] = (plan[nm].shard_rows, plan[nm].shard_K)
     # ---- weights: 32 x 7 distinct slots (1.80 GB in total over the ranks), seeded per rank and layer. Each rank
     # synthesises slots of its shard's shape directly (random valid codes; the shard transforms themselves are
     # checked bit-exact in the tests)
@@ -239,7 +255,7 @@ def run_b200(args, rank, world, local_rank):
         for i, (nm, _, _) in enumerate(shapes):
             rows, K = local[nm]
             # a row-parallel shard keeps its tensor's row order on every rank (as p8_tp_shard_cols shards do)
-            perm_seed = 1000 * L + 17 * i + 31 if plan[nm][0] == "row" else None
+            perm_seed = 1000 * L + 17 * i + 31 if plan[nm].kind == "row" else None
             slot = synth.make_slot_device(rows, K, seed=1000 * L + 17 * i + 7919 * rank, device=dev, perm_seed=perm_seed)
             ts[nm] = P8Tensor(slot, K, rows)
         layers.append(ts)
@@ -566,10 +582,141 @@ def run_b200(args, rank, world, local_rank):
                            "peak_source": "MEASURED_PEAKS.json bf16_tflops (cuBLAS bf16 burst; the GEMM runs fp16 operands at the same rate)",
                            "config": "512 tokens x 224 projections (32 layers), distinct weights, inputs resident"}
     if world == 1 and not args.no_cpu:
-        layer_s, cores, isa = cpu_reference_layer(model, reps=5, warmup=1)
-        line["cpu_baseline"] = {"value": round(1.0 / (model["layers"] * layer_s), 4), "unit": "tok/s", "cores": cores, "kind": "reference",
-                                "sample": f"1 of {model['layers']} layers (7 GEMVs, x{model['layers']}), median of 5; {isa} vr-native-cpu-core.h"}
+        tok_time, cores, isa = cpu_reference_token(model, reps=5, warmup=1)
+        line["cpu_baseline"] = {"value": round(1.0 / tok_time, 4), "unit": "tok/s", "cores": cores, "kind": "reference",
+                                "sample": f"5 tokens, each all {model['layers'] * 7} projections (distinct slots, 1.80 GB), median; "
+                                          f"{isa} vr-native-cpu-core.h, {cores} OpenMP threads"}
     print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------------------------------------ profiling cases
+# One kernel family on one shape, repeated: small self-contained cases for ncu captures and quick timings
+# (python bench.py --case ...). Weights are seeded synthetic class-3 slots of the Llama-3.1-8B shapes.
+CASE_GROUPS = {  # Llama-3.1-8B: (rows, K) per tensor of a group that reads one x
+    "qkv": [(4096, 4096), (1024, 4096), (1024, 4096)],
+    "o": [(4096, 4096)],
+    "gate_up": [(14336, 4096), (14336, 4096)],
+    "down": [(4096, 14336)],
+}
+
+
+def run_case(args):
+    """--case gemv:GROUP          the grouped batch-1 GEMV (k_act_prep + k_gemv), --iters calls rotating over --copies
+                                  distinct weight copies (copies > 1 read DRAM rather than L2), optionally --graph
+       --case gemm:GROUP:NCOLS    the batched product per tensor (tcgen05 GEMM), or :grouped for p8_mul_mat_group
+       --case get_rows:GROUP:N    p8_get_rows of N random rows of each tensor of the group
+       --case dequant:GROUP       p8_dequant_f32 of each tensor of the group
+       --case encode:ROWS         the offline trellis encoder (k_vit) on ROWS x 4096 class 3 with a random Hessian
+    Prints the mean time per call (CUDA events)."""
+    import torch
+
+    from pingala8_llm_b200 import synth
+    from pingala8_llm_b200.ops import P8Tensor, group_workspace_size, mul_mat_group, mul_mat_vec_group
+
+    kind, *rest = args.case.split(":")
+    if kind == "encode":
+        return _case_encode(int(rest[0]), args.iters)
+    shapes = CASE_GROUPS[rest[0]]
+    copies = [[P8Tensor(synth.make_slot_device(r, k, seed=100 * c + i), k, r) for i, (r, k) in enumerate(shapes)]
+              for c in range(max(1, args.copies))]
+    K = shapes[0][1]
+    if kind == "gemv":
+        x = torch.randn(K, device="cuda")
+        outs = [torch.empty(r, device="cuda") for r, _ in shapes]
+        ws = torch.empty(max(group_workspace_size(ts) for ts in copies), dtype=torch.uint8, device="cuda")
+
+        def once(i, stream=None):
+            mul_mat_vec_group(copies[i % len(copies)], x, outs=outs, workspace=ws, stream=stream)
+        nbytes = sum((r // 32) * (k // 256) * (68 + 2048) for r, k in shapes)
+        unit = lambda us: f"{nbytes / us / 1e3:.1f} GB/s (algorithmic, class 3)"  # noqa: E731
+    elif kind == "gemm":
+        ncols = int(rest[1])
+        grouped = len(rest) > 2 and rest[2] == "grouped"
+        X = torch.randn(ncols, K, device="cuda")
+        outs = [torch.empty(ncols, r, device="cuda") for r, _ in shapes]
+        gws = torch.empty(max(max(group_workspace_size(ts, ncols) for ts in copies), 256), dtype=torch.uint8, device="cuda")
+
+        def once(i, stream=None):
+            ts = copies[i % len(copies)]
+            if grouped:
+                mul_mat_group(ts, X, outs=outs, workspace=gws, stream=stream)
+            else:
+                for t, y in zip(ts, outs):
+                    t.mul_mat(X, out=y, workspace=gws, stream=stream)
+        flop = sum(2.0 * r * k * ncols for r, k in shapes)
+        unit = lambda us: f"{flop / us / 1e6:.1f} TFLOP/s"  # noqa: E731
+    elif kind == "get_rows":
+        n = int(rest[1])
+        ids = [torch.randint(0, r, (n,), dtype=torch.int32, device="cuda") for r, _ in shapes]
+        outs = [torch.empty(n, K, device="cuda") for _ in shapes]
+
+        def once(i, stream=None):
+            for t, d, o in zip(copies[i % len(copies)], ids, outs):
+                t.get_rows(d, out=o, stream=stream)
+        nbytes = sum(n * (K // 256) * (2048 + 2 + 4 + K // (K // 256) * 4) for _ in shapes)
+        unit = lambda us: f"{nbytes / us / 1e3:.1f} GB/s (rows' tiles + f32 out)"  # noqa: E731
+    elif kind == "dequant":
+        outs = [torch.empty(r, k, device="cuda") for r, k in shapes]
+
+        def once(i, stream=None):
+            for t, o in zip(copies[i % len(copies)], outs):
+                t.dequant(out=o, stream=stream)
+        nbytes = sum((r // 32) * (k // 256) * (68 + 2048) + 4 * r * k for r, k in shapes)
+        unit = lambda us: f"{nbytes / us / 1e3:.1f} GB/s (slot + f32 out)"  # noqa: E731
+    else:
+        raise SystemExit(f"unknown case {args.case}")
+    for i in range(len(copies)):  # warm-up
+        once(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if args.graph:
+        st = torch.cuda.Stream()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(st):
+            with torch.cuda.graph(g, stream=st):
+                for i in range(args.iters):
+                    once(i, stream=st)
+        g.replay()
+        torch.cuda.synchronize()
+        e0.record(st)
+        g.replay()
+        e1.record(st)
+    else:
+        e0.record()
+        for i in range(args.iters):
+            once(i)
+        e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.iters
+    print(f"case {args.case}: {us:.2f} us/call, {unit(us)}", flush=True)
+    return 0
+
+
+def _case_encode(rows, iters):
+    import torch
+
+    from pingala8_llm_b200.encoder import encode
+
+    n = 4096
+    g = torch.Generator(device="cuda").manual_seed(0)
+    X = torch.randn(2 * n, n, device="cuda", generator=g, dtype=torch.float64)
+    H = X.T @ X / (2 * n)
+    H += 0.1 * H.diagonal().mean() * torch.eye(n, device="cuda", dtype=torch.float64)
+    Uc = torch.linalg.cholesky(torch.cholesky_inverse(torch.linalg.cholesky(H)), upper=True).float()
+    Y = torch.randn(rows, n, device="cuda", generator=g)
+    cls = torch.full((rows, n // 256), 3, dtype=torch.int64)
+    Sb = torch.full((rows, n // 256), 1 / 16.0)
+    encode(Y[:16], Uc, cls[:16], Sb[:16])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        encode(Y, Uc, cls, Sb)
+    e1.record()
+    torch.cuda.synchronize()
+    dt = e0.elapsed_time(e1) / 1e3 / iters
+    print(f"case encode:{rows}: {dt * 1e3:.3f} ms per {rows} x {n} tensor, {dt / (rows * n) * 1e9:.3f} ns per weight")
     return 0
 
 
@@ -585,7 +732,13 @@ def main():
     ap.add_argument("--no-batched", action="store_true", help="skip the batched-decode (bs 8/32/64) measurement")
     ap.add_argument("--tp-exchange", default="fused", choices=["fused", "nccl"],
                     help="row-parallel sum for N > 1: inside the GEMV over peer memory, or an NCCL all-reduce after it")
+    ap.add_argument("--case", default="", help="run one profiling case instead of the bench (see run_case)")
+    ap.add_argument("--iters", type=int, default=20, help="--case: calls timed")
+    ap.add_argument("--copies", type=int, default=1, help="--case: distinct weight copies the calls rotate over")
+    ap.add_argument("--graph", action="store_true", help="--case: capture the calls in a CUDA graph")
     args = ap.parse_args()
+    if args.case:
+        return run_case(args)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

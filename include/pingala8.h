@@ -42,7 +42,9 @@ typedef enum p8_status {
     P8_ERR_TIMEOUT = -14,   /* a bounded device-side wait gave up (kernel returned early, results invalid) */
     P8_ERR_SLOT = -15,      /* no slot type is large enough (loader: "no slot type fits", CU:3498) */
     P8_ERR_FILE = -16,      /* model file: I/O error, not a GGUF file (v2/v3), or a malformed container */
-    P8_ERR_MODEL = -17      /* model file: Pingala-8 keys or tensors missing or inconsistent (vr_native_init) */
+    P8_ERR_MODEL = -17,     /* model file: Pingala-8 keys or tensors missing or inconsistent (vr_native_init) */
+    P8_ERR_NOALLOC_SCRATCH = -18 /* p8_mul_mat_vec_noalloc: the library's fixed scratch array could not be placed on
+                                    this device (its module is loaded, and the array allocated, at the first call) */
 } p8_status;
 
 typedef struct p8_tensor p8_tensor;
@@ -119,13 +121,15 @@ size_t p8_workspace_size_group_ex(const p8_tensor *const *ts, int n, int64_t nco
 p8_status p8_mul_mat_group(const p8_tensor *const *ts, int n, const float *X, int64_t ncols, int64_t ldx, const p8_prologue *pro,
                            float *const *Ys, const int64_t *ldys, void *workspace, size_t workspace_bytes, void *stream);
 
-/* y = W x like p8_mul_mat_vec, but with no workspace argument and no allocation: the scratch is a fixed 6 MiB device
- * array inside the library, for callers that cannot allocate device memory at call time and have no buffer to lend
- * (e.g. a host framework that plans all device memory up front). No counterpart in the reference (its GEMV takes
- * scratch from the ggml pool, CU:3182-3184). Limit: tensors with p8_workspace_size(t, 1) <= p8_noalloc_scratch_bytes()
- * (else P8_ERR_WORKSPACE). Every GPU that loads the library holds the array until exit; calls share it, so calls that
- * can overlap on the GPU race and must be serialised by the caller. The first call on a device looks up the array's
- * device address: make it before any stream capture. */
+/* y = W x like p8_mul_mat_vec, but with no workspace argument and no allocation by this library: the scratch is a
+ * fixed 6 MiB device array inside the library, for callers that cannot allocate device memory at call time and have
+ * no buffer to lend (e.g. a host framework that plans all device memory up front). No counterpart in the reference.
+ * Limit: tensors with p8_workspace_size(t, 1) <= p8_noalloc_scratch_bytes() (else P8_ERR_WORKSPACE).
+ * The array is placed on a device when the library's module is loaded there, which under CUDA's default lazy loading
+ * is the first call on that device: that call makes the 6 MiB device allocation, can fail like one
+ * (P8_ERR_NOALLOC_SCRATCH) and must not be inside a stream capture, so make one call per device during set-up. From
+ * then on the GPU holds the array until the process exits. Calls share it, so calls that can overlap on the GPU race
+ * and must be serialised by the caller. */
 size_t p8_noalloc_scratch_bytes(void);
 p8_status p8_mul_mat_vec_noalloc(const p8_tensor *t, const float *x, float *y, void *stream);
 

@@ -158,6 +158,7 @@ class RefOracle:
             L.ref_gemv_x16.argtypes = [C.c_void_p, _fp, _fp]
             L.ref_mul_mat_x16.argtypes = [C.c_void_p, _fp, C.c_int, C.c_int, _fp, C.c_int]
             L.ref_threads.restype = C.c_int
+            L.ref_set_threads.argtypes = [C.c_int]
             L.ref_has_v4.restype = C.c_int
             L.ref_isa.restype = C.c_char_p
             L.ref_need.argtypes = [C.c_size_t] * 4
@@ -209,6 +210,11 @@ class RefOracle:
     @classmethod
     def threads(cls):
         return cls.lib().ref_threads()
+
+    @classmethod
+    def set_threads(cls, n):
+        """OpenMP threads of the reference core's parallel loops (overrides OMP_NUM_THREADS)."""
+        cls.lib().ref_set_threads(int(n))
 
     @classmethod
     def isa(cls):

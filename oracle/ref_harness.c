@@ -21,6 +21,8 @@ void ref_free(vrc_meta *m) { vrc_free(m); }
 void ref_decode_tile_int(const vrc_meta *m, int g, int b, int16_t *xi) { vrc_decode_tile_int(m, g, b, xi); }
 void ref_dequant_f32(const vrc_meta *m, float *W) { vrc_dequant_f32(m, W); }
 int ref_threads(void) { return omp_get_max_threads(); }
+/* all host cores for the timed baseline, whatever OMP_NUM_THREADS says (torchrun sets it to 1) */
+void ref_set_threads(int n) { if (n > 0) omp_set_num_threads(n); }
 int ref_has_v4(void) {
 #if defined(VRC_V4)
     return 1;

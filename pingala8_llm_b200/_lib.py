@@ -15,7 +15,7 @@ P8_STATUS = {
     0: "P8_OK", -1: "P8_ERR_ARG", -2: "P8_ERR_TRAILER", -3: "P8_ERR_HEADER", -4: "P8_ERR_PAYLOAD", -5: "P8_ERR_PERM",
     -6: "P8_ERR_DELTA", -7: "P8_ERR_SIGNS", -8: "P8_ERR_TABLES", -9: "P8_ERR_SHAPE", -10: "P8_ERR_CUDA",
     -11: "P8_ERR_WORKSPACE", -12: "P8_ERR_NOT_PREPARED", -13: "P8_ERR_UNSUPPORTED", -14: "P8_ERR_TIMEOUT", -15: "P8_ERR_SLOT",
-    -16: "P8_ERR_FILE", -17: "P8_ERR_MODEL",
+    -16: "P8_ERR_FILE", -17: "P8_ERR_MODEL", -18: "P8_ERR_NOALLOC_SCRATCH",
 }
 
 

@@ -17,6 +17,8 @@
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
+
+#include <atomic>
 #include <string.h>
 
 #include "p8_internal.h"
@@ -408,12 +410,12 @@ p8_status p8_encode_slice(const float *X, int64_t ldx, const float *Hb, int64_t 
     a.lds = lds; a.rows = (int)rows; a.Q = Q; a.ldq = ldq; a.E = E; a.lde = lde; a.IDX = IDX; a.ldi = ldi;
     for (int k = 0; k < 4; ++k) a.cvec[k] = (float)coset[k];
     const size_t smem = sizeof(RowSmem) * kVitRowsPerCta;
-    static bool attr[64] = {false};  // the attribute is per device
+    static std::atomic<bool> attr[64];  // the attribute is per device; published after it is set
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return P8_ERR_CUDA;
-    if (dev < 0 || dev >= 64 || !attr[dev]) {
+    if (dev < 0 || dev >= 64 || !attr[dev].load(std::memory_order_acquire)) {
         if (cudaFuncSetAttribute(k_vit, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return P8_ERR_CUDA;
-        if (dev >= 0 && dev < 64) attr[dev] = true;
+        if (dev >= 0 && dev < 64) attr[dev].store(true, std::memory_order_release);
     }
     const unsigned grid = (unsigned)((rows + kVitRowsPerCta - 1) / kVitRowsPerCta);
     k_vit<<<grid, 128, smem, st>>>(a);

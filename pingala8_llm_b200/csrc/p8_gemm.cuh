@@ -993,14 +993,14 @@ p8_status launch_gemm_group(const p8_tensor *const *ts, int n, const float *X, i
     size_t own = 0;
     const GemmPlan &p = it[gemm_items_prep(it, m, &own)].p;
     if (!ws || ws_bytes < p.prep + own || ((uintptr_t)ws & 255)) return P8_ERR_WORKSPACE;
-    static bool attr_set[64] = {false};
+    static std::atomic<bool> attr_set[64];  // published after the attributes are set (see sm_count)
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (dev < 0 || dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
         if (cudaFuncSetAttribute(k_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemDyn) != cudaSuccess ||
             cudaFuncSetAttribute(k_gemm<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmemDyn) != cudaSuccess)
             return P8_ERR_CUDA;
-        attr_set[dev] = true;
+        if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
     }
     const p8_tensor *t = ts[0];
     uint8_t *w = static_cast<uint8_t *>(ws);

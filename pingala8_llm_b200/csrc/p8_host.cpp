@@ -421,6 +421,7 @@ const char *p8_status_str(p8_status s) {
         case P8_ERR_SLOT: return "no slot type fits";
         case P8_ERR_FILE: return "model file unreadable, not GGUF v2/v3, or malformed";
         case P8_ERR_MODEL: return "model file: Pingala-8 keys or tensors missing or inconsistent";
+        case P8_ERR_NOALLOC_SCRATCH: return "the fixed no-allocation scratch array could not be placed on this device";
     }
     return "unknown status";
 }

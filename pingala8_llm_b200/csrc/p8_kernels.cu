@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "p8_device.cuh"
 #include "p8_internal.h"
 
@@ -229,6 +231,7 @@ constexpr int kGemvThreads = 512;
 constexpr int kGemvWarps = kGemvThreads / 32;
 constexpr int kMaxGroup = 4;
 constexpr uint32_t kWaitPolls = 1u << 20;  // a healthy table copy lands within a few polls
+constexpr unsigned long long kGridWaitNs = 20000000ull;  // grid-barrier deadline: 20 ms
 // dynamic shared memory of k_gemv: two table buffers, two G buffers (both half-slices), two mbarriers
 constexpr int kSmemT0 = 0, kSmemT1 = kTabBytes, kSmemG0 = 2 * kTabBytes, kSmemG1 = kSmemG0 + 2 * kGInts * 4,
               kSmemBar = kSmemG1 + 2 * kGInts * 4, kGemvSmem = kSmemBar + 16;
@@ -780,8 +783,13 @@ __global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
         unsigned int n;  // release: this CTA's partial stores are visible before its arrival is counted
         asm volatile("atom.add.release.gpu.global.u32 %0, [%1], 1;" : "=r"(n) : "l"(a.arrive) : "memory");
         ++n;
-        for (int spins = 0; n < gridDim.x && spins < (1 << 26); ++spins)
+        // all CTAs are resident in a healthy launch, so the wait is microseconds; the deadline ends it when another
+        // kernel holds SMs (results invalid, error bit 2) instead of spinning for seconds
+        const unsigned long long dl = global_ns() + kGridWaitNs;
+        while (n < gridDim.x) {
             asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(n) : "l"(a.arrive) : "memory");
+            if (n < gridDim.x && global_ns() > dl) break;
+        }
         asm volatile("fence.acq_rel.gpu;" ::: "memory");  // acquire: the other CTAs' partials are visible
         s_ok = n >= gridDim.x;
         if (!s_ok) atomicOr(&g_p8_device_error, 2u);
@@ -883,19 +891,23 @@ static cudaError_t launch_pdl(const void *fn, dim3 grid, dim3 block, size_t smem
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
+// SM count of the current device; the first call on a device also raises the GEMV kernels' shared-memory limit there.
+// The cache entry is published only after the attributes are set, so a second host thread never launches before them
+// (two threads racing on a first call both set the attributes, which is harmless).
 static int sm_count() {
-    static int n[64] = {0};
+    static std::atomic<int> n[64];
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return 148;
-    if (!n[dev]) {
-        int v = 0;
+    int v = n[dev].load(std::memory_order_acquire);
+    if (!v) {
         cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-        n[dev] = v > 0 ? v : 148;
+        if (v <= 0) v = 148;
         cudaFuncSetAttribute(k_gemv<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
         cudaFuncSetAttribute(k_gemv<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
+        n[dev].store(v, std::memory_order_release);
     }
-    return n[dev];
+    return v;
 }
 
 // one column: prep + persistent GEMV over the group

@@ -6,7 +6,11 @@
 // memory pressure). The scratch the GEMV needs (activation tables, coset tables, scales, the grid-barrier counter and
 // the row partials) lives in one fixed device array of this file instead of a caller workspace.
 //
-// The array is kNoAllocScratchBytes (6 MiB); every GPU that loads this library holds it until the process exits.
+// The array is kNoAllocScratchBytes (6 MiB). It is placed on a device when this file's device module is loaded there,
+// and with CUDA's default lazy module loading that happens inside the first p8_mul_mat_vec_noalloc call on that
+// device: that first call makes the 6 MiB device allocation (the driver's, not this library's) and can fail like one
+// (P8_ERR_NOALLOC_SCRATCH), and it must not run inside a stream capture. Make one call on every device during set-up,
+// outside any capture; from then on every GPU that loaded the array holds it until the process exits.
 // A tensor whose GEMV needs more scratch than that (p8_workspace_size(t, 1) > 6 MiB, e.g. K > 16384 or very many rows
 // per 256-column block) is rejected with P8_ERR_WORKSPACE.
 //
@@ -14,8 +18,6 @@
 // they read and clear the barrier counter at the start of each call, so no state leaks between calls. Calls that can
 // overlap on the GPU (other streams, other host threads) race on the array and must be serialised by the caller.
 #include <cuda_runtime.h>
-
-#include <mutex>
 
 #include "p8_internal.h"
 
@@ -25,22 +27,20 @@ constexpr size_t kNoAllocScratchBytes = (size_t)6 << 20;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-std::mutex g_mu;
-void *g_scratch_addr[64] = {nullptr};  // per device: the device address of g_noalloc_scratch
-
-// Device address of the scratch array on the current device. The array's name in host code is only a host-side
-// stand-in, so the address is looked up once per device with that device current (the first call on a device does
-// this set-up; make that first call before any stream capture).
+// Device address of the scratch array in the current device's context. In host code the array's name is only a
+// host-side stand-in, so the address is looked up with the device current. It is looked up on every call (cheap once
+// the module is loaded) rather than cached, so a context that was torn down and re-created (cudaDeviceReset) never sees
+// an address of the old one.
 p8_status scratch_for_current_device(void **out) {
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return P8_ERR_CUDA;
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (!g_scratch_addr[dev]) {
-        void *p = nullptr;
-        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return P8_ERR_CUDA;
-        g_scratch_addr[dev] = p;
+    if (cudaGetDevice(&dev) != cudaSuccess) return P8_ERR_CUDA;
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+        (void)cudaGetLastError();  // the failed module load is reported through the status, not left pending
+        return P8_ERR_NOALLOC_SCRATCH;
     }
-    *out = g_scratch_addr[dev];
+    *out = p;
     return P8_OK;
 }
 

@@ -12,12 +12,17 @@ between the two projections of a pair:
                                        peers' exchange buffers over NVLink and sums the ranks' rows in rank order) or
                                        by an NCCL all-reduce after it.
 
-Split units keep the pairs consistent: q and o's input in units of two heads (256 columns, o's K-shards must be
-whole 256-column blocks), k/v in single KV heads (query heads of rank i use KV heads of rank i under GQA), gate/up
-and down's input in 256-row units. Uneven counts are spread by a balanced contiguous split.
+Split units keep the pairs consistent. q/k/v are split by whole GQA groups: rank i holds KV heads [k0, k1) and exactly
+the query heads that read them, so attention needs no exchange. o's input columns are then the rank's q rows; where
+that range is not a whole number of 256-column Hadamard blocks (Qwen3-14B at TP8: 5 query heads = 640 columns per rank)
+the rank's o shard holds every block its range touches, and a boundary block is held by both neighbours: the Hadamard
+transform is linear, so each rank multiplies the full block's weights by its own columns with the other rank's
+columns zero, and the two partial outputs add up to the block's product. gate/up and down's input are split in
+256-row units (whole blocks). Uneven counts are spread by a balanced contiguous split.
 """
 import ctypes as C
 from dataclasses import dataclass
+from typing import NamedTuple
 
 import numpy as np
 
@@ -51,16 +56,25 @@ def column_shard(slot, K, rows, world, rank, unit=32):
     return Shard("col", lo, hi, hi - lo, K, s)
 
 
-def row_shard(slot, K, rows, world, rank, unit=256):
-    """Row-parallel shard: input columns [lo, hi) of this rank, split in units of `unit` columns (a multiple of 256)."""
-    if unit % 256 or K % unit:
-        raise ValueError("row split unit must divide K and be a multiple of 256")
-    u0, u1 = balanced(K // unit, world, rank)
-    lo, hi = u0 * unit, u1 * unit
+def row_shard(slot, K, rows, world, rank, unit=256, cols=None):
+    """Row-parallel shard: input columns [lo, hi) of this rank, split in units of `unit` columns (a multiple of 256),
+    or the explicit range cols = (lo, hi). The shard holds the 256-column blocks that [lo, hi) touches; with an
+    unaligned range its boundary blocks are also held by the neighbouring rank, and the caller zeroes the input
+    columns outside [lo, hi) (RowParallel does)."""
+    if cols is None:
+        if unit % 256 or K % unit:
+            raise ValueError("row split unit must divide K and be a multiple of 256")
+        u0, u1 = balanced(K // unit, world, rank)
+        lo, hi = u0 * unit, u1 * unit
+    else:
+        lo, hi = cols
+        if not 0 <= lo <= hi <= K:
+            raise ValueError("row shard columns outside [0, K)")
     if hi == lo:
         return Shard("row", lo, hi, rows, 0, np.zeros(0, np.uint8))
-    s = fmt.shard_cols(slot, K, rows, lo // 256, hi // 256)
-    return Shard("row", lo, hi, rows, hi - lo, s)
+    b0, b1 = lo // 256, (hi + 255) // 256
+    s = fmt.shard_cols(slot, K, rows, b0, b1)
+    return Shard("row", lo, hi, rows, 256 * (b1 - b0), s)
 
 
 @dataclass
@@ -75,35 +89,61 @@ class LayerDims:
 LLAMA3_8B = LayerDims(hidden=4096, ffn=14336, heads=32, kv_heads=8, head_dim=128)
 
 
-def layer_units(d: LayerDims):
-    """split unit (rows for column-parallel, input columns for row-parallel) of each projection of a layer"""
-    qunit = 2 * d.head_dim if (2 * d.head_dim) % 256 == 0 else 256
-    return {"q": qunit, "k": d.head_dim, "v": d.head_dim, "o": qunit, "gate": 256, "up": 256, "down": 256}
+QWEN3_14B = LayerDims(hidden=5120, ffn=17408, heads=40, kv_heads=8, head_dim=128)
+QWEN3_4B = LayerDims(hidden=2560, ffn=9728, heads=32, kv_heads=8, head_dim=128)
+
+
+class PlanEntry(NamedTuple):
+    """One projection's split on one rank. col: original output rows [lo, hi). row: input columns [lo, hi), held as
+    the 256-column blocks [b0, b1) (b0 = lo // 256, b1 = ceil(hi / 256); the rank's input is zero outside [lo, hi))."""
+    kind: str
+    unit: int
+    lo: int
+    hi: int
+    rows: int
+    K: int
+    b0: int = 0
+    b1: int = 0
+
+    @property
+    def shard_rows(self):
+        return self.hi - self.lo if self.kind == "col" else self.rows
+
+    @property
+    def shard_K(self):
+        return self.K if self.kind == "col" else 256 * (self.b1 - self.b0)
 
 
 def layer_plan(d: LayerDims, world, rank):
-    """(kind, unit) per projection and the rank's ranges; o's input range equals q's row range and down's input range
-    equals gate/up's row range, so each rank feeds its row-parallel projections from its own outputs."""
-    u = layer_units(d)
-    kinds = {"q": "col", "k": "col", "v": "col", "o": "row", "gate": "col", "up": "col", "down": "row"}
-    rows = {"q": d.heads * d.head_dim, "k": d.kv_heads * d.head_dim, "v": d.kv_heads * d.head_dim,
-            "o": d.hidden, "gate": d.ffn, "up": d.ffn, "down": d.hidden}
-    K = {"q": d.hidden, "k": d.hidden, "v": d.hidden, "o": d.heads * d.head_dim, "gate": d.hidden, "up": d.hidden,
-         "down": d.ffn}
-    plan = {}
-    for n in kinds:
-        n_units = (rows[n] if kinds[n] == "col" else K[n]) // u[n]
-        lo, hi = balanced(n_units, world, rank)
-        plan[n] = (kinds[n], u[n], lo * u[n], hi * u[n], rows[n], K[n])
+    """PlanEntry per projection of a decoder layer on this rank. o's input range equals q's row range and down's input
+    range equals gate/up's row range, so each rank feeds its row-parallel projections from its own outputs; q/k/v
+    follow whole GQA groups (the rank's query heads read exactly the rank's KV heads)."""
+    g = d.heads // d.kv_heads
+    hd = d.head_dim
+    k0, k1 = balanced(d.kv_heads, world, rank)
+    f0, f1 = balanced(d.ffn // 256, world, rank)
+    plan = {
+        "q": PlanEntry("col", g * hd, k0 * g * hd, k1 * g * hd, d.heads * hd, d.hidden),
+        "k": PlanEntry("col", hd, k0 * hd, k1 * hd, d.kv_heads * hd, d.hidden),
+        "v": PlanEntry("col", hd, k0 * hd, k1 * hd, d.kv_heads * hd, d.hidden),
+        "o": PlanEntry("row", g * hd, k0 * g * hd, k1 * g * hd, d.hidden, d.heads * hd,
+                       (k0 * g * hd) // 256, (k1 * g * hd + 255) // 256),
+        "gate": PlanEntry("col", 256, 256 * f0, 256 * f1, d.ffn, d.hidden),
+        "up": PlanEntry("col", 256, 256 * f0, 256 * f1, d.ffn, d.hidden),
+        "down": PlanEntry("row", 256, 256 * f0, 256 * f1, d.hidden, d.ffn, f0, f1),
+    }
     assert plan["o"][2:4] == plan["q"][2:4] and plan["down"][2:4] == plan["gate"][2:4]
     return plan
 
 
-def shard_for(plan_entry, slot, world, rank):
-    kind, unit, _, _, rows, K = plan_entry
-    if kind == "col":
-        return column_shard(slot, K, rows, world, rank, unit)
-    return row_shard(slot, K, rows, world, rank, unit)
+def shard_for(e, slot, world, rank):
+    """this rank's shard of one projection's slot, as the plan entry e says"""
+    if e.kind == "col":
+        if e.hi == e.lo:
+            return Shard("col", e.lo, e.hi, 0, e.K, np.zeros(0, np.uint8))
+        s, _ = fmt.shard_rows(slot, e.K, e.rows, e.lo, e.hi)
+        return Shard("col", e.lo, e.hi, e.hi - e.lo, e.K, s)
+    return row_shard(slot, e.K, e.rows, world, rank, cols=(e.lo, e.hi))
 
 
 def reduce_partials(y, group=None):
@@ -263,19 +303,35 @@ class RowParallel:
     With comm (a TpComm of the group) the sum happens inside the GEMV (p8_tp_gemv_allreduce); every rank must then
     hold input columns (world <= K / unit), else the NCCL all-reduce after the GEMV is used on every rank."""
 
-    def __init__(self, slot, K, rows, world, rank, unit=256, device="cuda", group=None, comm=None):
+    def __init__(self, slot, K, rows, world, rank, unit=256, device="cuda", group=None, comm=None, cols=None):
         import torch
 
         from .ops import P8Tensor
 
-        self.shard = row_shard(slot, K, rows, world, rank, unit)
+        self.shard = row_shard(slot, K, rows, world, rank, unit, cols=cols)
         self.lo, self.hi = self.shard.lo, self.shard.hi
+        self.off = self.lo - 256 * (self.lo // 256)  # the rank's columns inside its first block
         self.group = group
         self.t = P8Tensor(torch.from_numpy(self.shard.slot).to(device), self.shard.K, rows) if self.shard.K else None
-        # the same decision on every rank: it depends only on K, unit and world
-        self.comm = comm if comm is not None and world <= K // unit and world > 1 else None
+        # the same decision on every rank: it depends only on the split, which every rank computes alike
+        every_rank_has_columns = (cols is None and world <= K // unit) or (cols is not None and self.hi > self.lo)
+        self.comm = comm if comm is not None and every_rank_has_columns and world > 1 else None
+        self._xpad = None
+
+    def padded(self, x_local):
+        """x_local (the rank's hi - lo input columns) placed into the shard's blocks, zero outside [lo, hi)"""
+        if self.t is None or (self.off == 0 and x_local.shape[-1] == self.shard.K):
+            return x_local
+        import torch
+
+        shape = x_local.shape[:-1] + (self.shard.K,)
+        if self._xpad is None or self._xpad.shape != shape or self._xpad.device != x_local.device:
+            self._xpad = torch.zeros(shape, dtype=torch.float32, device=x_local.device)
+        self._xpad[..., self.off:self.off + x_local.shape[-1]] = x_local
+        return self._xpad
 
     def __call__(self, x_local, out=None, workspace=None, stream=None):
+        x_local = self.padded(x_local)
         if self.comm is not None:
             return self.t.mul_mat_vec_allreduce(x_local, self.comm, out=out, workspace=workspace, stream=stream)
         if self.t is None:  # no input columns on this rank: contribute zeros to the sum
@@ -296,5 +352,5 @@ class RowParallel:
             Y = out.zero_() if out is not None else torch.zeros(X_local.shape[0], self.shard.rows, dtype=torch.float32,
                                                                  device=X_local.device)
         else:
-            Y = self.t.mul_mat(X_local, out=out, workspace=workspace, stream=stream)
+            Y = self.t.mul_mat(self.padded(X_local).contiguous(), out=out, workspace=workspace, stream=stream)
         return reduce_partials(Y, self.group)

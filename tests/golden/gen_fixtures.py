@@ -92,11 +92,13 @@ def sha(a):
     return hashlib.sha256(a.tobytes()).hexdigest()
 
 
-def weights(rows, n, seed):
+def weights(rows, n, seed, flat_outliers=False):
     rng = np.random.default_rng(seed)
     W = rng.normal(0, 0.02, (rows, n))
     m = rng.random((rows, n)) < 1e-3
     W[m] = rng.standard_t(3, int(m.sum())) * 0.1
+    if flat_outliers:  # every outlier at the same magnitude: many of them decode past the clamp bound max|W|
+        W[m] = np.sign(W[m]) * 0.3
     return W.astype(np.float32)
 
 
@@ -135,13 +137,23 @@ def main():
     ] + [(f"cls{k}_64x512", 64, 512, 10 + k, RATES[k], 0) for k in range(1, 7)] + [
         # class 7 (6 b/w) needs a larger tensor to fit a Q6_K slot together with its side data
         ("cls7_256x1024", 256, 1024, 17, RATES[7], 0),
+        # config C1 at its stated size (Qwen3-4B ffn_up 9728 x 2560, seed 0): pure class 3, and class 3 with four
+        # salient class-6 tiles per row group
+        ("c1_9728x2560_c3", 9728, 2560, 0, 2.0, 0),
+        ("c1_9728x2560_sal", 9728, 2560, 0, None, 4),
     ]
+    # clamp-delta coverage: the C1 recipe leaves no decoded weight past the clamp bound (nd = 0 at both sizes), so this
+    # case sets every outlier to the same magnitude 0.3: decoded outliers then overshoot the fp16 bound max|W| * 1.001
+    # about half the time, and the slot carries the reference pipeline's own delta entries (r51_delta.py semantics)
+    specs_alpha = {}
+    flat = {"dl_2048x2560_c3"}
+    specs += [("dl_2048x2560_c3", 2048, 2560, 3, 2.0, 0)]
     if a.only:
         specs = [s for s in specs if s[0] in a.only.split(",")]
     index = {}
     for name, rows, n, seed, rate, nsal in specs:
         t0 = time.time()
-        W = torch.tensor(weights(rows, n, seed))
+        W = torch.tensor(weights(rows, n, seed, flat_outliers=name in flat))
         c = torch.ones(n)
         Hf = torch.eye(n)
         sw = torch.ones(n)
@@ -151,7 +163,7 @@ def main():
         def bud(r_, n_, r=r):
             return r * r_ * n_
 
-        R = K_.k_tensor(W, c, Hf, sw, bud, T, CD, G, True, alpha=1.05, dev="cpu", damp=0.1, nsal=nsal)
+        R = K_.k_tensor(W, c, Hf, sw, bud, T, CD, G, True, alpha=specs_alpha.get(name, 1.05), dev="cpu", damp=0.1, nsal=nsal)
         blob = K_.pack_blob(c.half().numpy(), R["prm"], R["S16"].numpy(), R["cs"], R["IDX"].cpu().numpy(), R["wmax"], True)
         hdr, Yd = K_.unpack_blob(blob, T)
         assert torch.equal(Yd, R["Yq"].cpu())
@@ -182,7 +194,9 @@ def main():
         np.save(os.path.join(HERE, f"{name}.y_ref.npy"), y_ref)
         np.save(os.path.join(HERE, f"{name}.Y_ref.npy"), Y_ref)
         meta = dict(
-            name=name, rows=rows, K=n, seed=seed, rate=rate, nsal=nsal, nd=int(len(dval)), kbytes=len(kb),
+            name=name, rows=rows, K=n, seed=seed, rate=rate, nsal=nsal, alpha=specs_alpha.get(name, 1.05), flat_outliers=name in flat,
+            nd=int(len(dval)),
+            kbytes=len(kb),
             slot_type=slot_type, slot_nbytes=int(slot.size), class_hist=hist, wmax=float(wm),
             sha_port_vs=sha(port),              # r51_transcode.cpu_vr_port: v*S fp32, sorted rows
             sha_wq_clamped=sha(Wq),             # encoder: clamp(ifw(Yq)/c), original rows

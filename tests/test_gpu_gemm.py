@@ -15,7 +15,7 @@ if not torch.cuda.is_available():
 
 from pingala8_llm_b200 import synth  # noqa: E402
 from pingala8_llm_b200.ops import P8Tensor, device_error  # noqa: E402
-from oracle.oracle import Oracle  # noqa: E402
+from oracle.oracle import Oracle, RefOracle  # noqa: E402
 
 from conftest import fixture_names, load_fixture  # noqa: E402
 
@@ -135,6 +135,29 @@ def test_full_size_gemm_unit_vectors(label, rows, K, ncols):
     ref = W[:, ks].T.contiguous()
     err = torch.linalg.norm((Y - ref).double()) / torch.linalg.norm(ref.double())
     assert float(err) < BAR
+
+
+@pytest.mark.parametrize("label,rows,K,ncols", [("llama_gate", 14336, 4096, 2048), ("llama_gate", 14336, 4096, 512),
+                                                ("llama_down", 4096, 14336, 2048), ("llama_down", 4096, 14336, 512)])
+def test_full_size_gemm_dense_tokens(label, rows, K, ncols):
+    """BASELINE C3 at its token counts with dense N(0, 1) activations (every token accumulates over all of K):
+    against the product with the bit-exact dequantized weight in fp64 on a subset of 1024 rows, and the first 8
+    tokens against the reference's own CPU core (oracle/_ref, x16 batch path) on every row"""
+    s = synth.make_slot_device(rows, K, seed=rows + K + ncols, nd=0)
+    t = P8Tensor(s, K, rows)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(ncols)
+    X = torch.randn(ncols, K, device="cuda", generator=g)
+    Y = gemm(t, X)
+    sub = torch.from_numpy(np.random.default_rng(ncols).choice(rows, 1024, replace=False)).cuda()
+    W = t.dequant()[sub]
+    ref = X.double() @ W.double().T
+    err = float(torch.linalg.norm(Y[:, sub].double() - ref) / torch.linalg.norm(ref))
+    assert err < BAR, err
+    if RefOracle.available():
+        r = RefOracle(s.cpu().numpy(), rows, K)
+        Yr = r.mul_mat(X[:8].cpu().numpy())
+        assert rel(Y[:8].cpu().numpy(), Yr) < BAR
 
 
 def test_gemm_deterministic_and_graph_capturable():

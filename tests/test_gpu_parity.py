@@ -16,7 +16,7 @@ if not torch.cuda.is_available():  # the gpu marker is deselected on CPU runs; g
 import pingala8_llm_b200 as p8  # noqa: E402
 from pingala8_llm_b200 import synth  # noqa: E402
 from pingala8_llm_b200.ops import P8Tensor, active  # noqa: E402
-from oracle.oracle import Oracle  # noqa: E402
+from oracle.oracle import Oracle, RefOracle  # noqa: E402
 
 from conftest import fixture_names, load_fixture  # noqa: E402
 
@@ -117,6 +117,8 @@ SHAPES = [
 
 @pytest.mark.parametrize("label,rows,K", SHAPES)
 def test_full_size_gemv_vs_oracle(label, rows, K):
+    """BASELINE shapes at full size against the restated oracle AND the reference's own CPU core (oracle/_ref,
+    vrc_tg with x16 activations) on the same slot and input"""
     s = synth.make_slot(rows, K, seed=rows + K, nd=37)
     t = P8Tensor(s, K, rows)
     o = Oracle(s, rows, K)
@@ -124,6 +126,9 @@ def test_full_size_gemv_vs_oracle(label, rows, K):
     y = t.mul_mat_vec(torch.from_numpy(x).cuda()).cpu().numpy()
     r = rel(y, o.mul_mat(x)[0])
     assert r < TIGHT, r
+    if RefOracle.available():
+        r_ref = rel(y, RefOracle(s, rows, K).gemv(x))
+        assert r_ref < TIGHT, r_ref
 
 
 @pytest.mark.parametrize("rows,K", [(256, 49152), (256, 65280)])

@@ -14,25 +14,65 @@ import torch.multiprocessing as mp  # noqa: E402
 from pingala8_llm_b200 import tp  # noqa: E402
 
 
+DIMS = {"llama3.1-8b": tp.LLAMA3_8B, "qwen3-14b": tp.QWEN3_14B, "qwen3-4b": tp.QWEN3_4B}
+
+
+@pytest.mark.parametrize("model", sorted(DIMS))
 @pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
-def test_layer_plan_covers_and_pairs(world):
-    d = tp.LLAMA3_8B
+def test_layer_plan_covers_and_pairs(model, world):
+    d = DIMS[model]
     plans = [tp.layer_plan(d, world, r) for r in range(world)]
     for n in ("q", "k", "v", "o", "gate", "up", "down"):
-        kind, unit, _, _, rows, K = plans[0][n]
-        total = rows if kind == "col" else K
-        got = [(p[n][2], p[n][3]) for p in plans]
+        e0 = plans[0][n]
+        total = e0.rows if e0.kind == "col" else e0.K
+        got = [(p[n].lo, p[n].hi) for p in plans]
         assert got[0][0] == 0 and got[-1][1] == total
         assert all(a[1] == b[0] for a, b in zip(got, got[1:]))        # contiguous, no overlap
-        assert all((hi - lo) % unit == 0 for lo, hi in got)
+        assert all((hi - lo) % e0.unit == 0 for lo, hi in got)
+        for p in plans:
+            e = p[n]
+            if e.kind == "col":
+                assert e.lo % 32 == 0 and e.hi % 32 == 0              # whole 32-row tiles
+            else:                                                     # the shard's blocks cover the rank's columns
+                assert e.b0 == e.lo // 256 and e.b1 == (e.hi + 255) // 256 and e.shard_K == 256 * (e.b1 - e.b0)
+                assert 256 * e.b0 <= e.lo <= e.hi <= 256 * e.b1
     for p in plans:  # each rank feeds its row-parallel projections from its own column-parallel outputs
         assert p["o"][2:4] == p["q"][2:4] and p["down"][2:4] == p["gate"][2:4] == p["up"][2:4]
-        # GQA: the rank's query heads use exactly the rank's KV heads (group = heads / kv_heads)
-        if d.kv_heads % world == 0:
-            g = d.heads // d.kv_heads
-            qh = (p["q"][2] // d.head_dim, p["q"][3] // d.head_dim)
-            kh = (p["k"][2] // d.head_dim, p["k"][3] // d.head_dim)
-            assert (qh[0] // g, (qh[1] + g - 1) // g) == kh
+        # GQA: the rank's query heads use exactly the rank's KV heads (group = heads / kv_heads), at every world size
+        g = d.heads // d.kv_heads
+        qh = (p["q"].lo // d.head_dim, p["q"].hi // d.head_dim)
+        kh = (p["k"].lo // d.head_dim, p["k"].hi // d.head_dim)
+        assert qh == (kh[0] * g, kh[1] * g) and p["v"][2:4] == p["k"][2:4]
+
+
+def test_qwen3_14b_tp8_o_shards_share_boundary_blocks():
+    """Qwen3-14B at TP8: 5 query heads = 640 o-input columns per rank, 2.5 Hadamard blocks: neighbours share a block"""
+    plans = [tp.layer_plan(tp.QWEN3_14B, 8, r) for r in range(8)]
+    assert [(p["o"].lo, p["o"].hi) for p in plans] == [(640 * r, 640 * (r + 1)) for r in range(8)]
+    assert [(p["o"].b0, p["o"].b1) for p in plans] == [(0, 3), (2, 5), (5, 8), (7, 10), (10, 13), (12, 15), (15, 18), (17, 20)]
+    assert sum(p["down"].b1 - p["down"].b0 for p in plans) == 17408 // 256   # down: whole blocks, 9/9/9/9/8/8/8/8
+
+
+def test_unaligned_row_shards_sum_to_the_whole_product():
+    """Row-parallel shards over an unaligned column split (a boundary block held by both ranks, each rank's input zero
+    outside its columns) sum to the unsharded product: the Hadamard transform is linear. Oracle GEMVs on the CPU."""
+    import sys
+
+    sys.path.insert(0, os.path.dirname(__file__))
+    from conftest import load_fixture
+    from oracle.oracle import Oracle
+
+    f = load_fixture("mix_256x1024_sal")  # K = 1024: 4 blocks; split at 640 (inside block 2)
+    y_full = Oracle(f.slot, f.rows, f.K).mul_mat(f.x)[0]
+    total = np.zeros(f.rows, np.float64)
+    for rank, (lo, hi) in enumerate([(0, 640), (640, 1024)]):
+        sh = tp.row_shard(f.slot, f.K, f.rows, 2, rank, cols=(lo, hi))
+        b0 = lo // 256
+        xs = np.zeros(sh.K, np.float32)
+        xs[lo - 256 * b0:hi - 256 * b0] = f.x[lo:hi]
+        total += Oracle(sh.slot, f.rows, sh.K).mul_mat(xs)[0]
+    rel = np.linalg.norm(total - y_full) / np.linalg.norm(y_full)
+    assert rel < 1e-3, rel  # each rank quantises its own masked block (x16), so the sum is within the x16 floor
 
 
 def test_balanced_split_uneven():
