@@ -147,7 +147,8 @@ class ClockSampler:
                 "samples": len(self.sm)}
 
 
-# DRAM bytes (read + write) of one call, from ncu captures of the same call (profiles/k_gemv_llama8b_gate_up.md)
+# DRAM bytes (read + write) of one call, from ncu captures of the same call at 1 GPU (profiles/k_gemv_llama8b_gate_up.md);
+# reported only for the configuration the capture measured
 TRAFFIC_BYTES = {"gate+up": 31587840}
 
 
@@ -292,18 +293,47 @@ def run_b200(args, rank, world, local_rank):
             x = buf["down"]
         return x
 
-    launches_per_step = 2 * len(groups) * model["layers"]  # k_act_prep + k_gemv per group
+    launches_ops = 2 * len(groups) * model["layers"]  # k_act_prep + k_gemv per group
+    # ---- (1 GPU) the same chain as chained launches (p8_chain: one persistent launch runs several projections with
+    # one grid barrier each). Launches split where attention sits in a real decoder layer (between q/k/v and o):
+    # [q/k/v 0], [o L-1, gate/up L-1, down L-1, q/k/v L] for L = 1..31, [o 31, gate/up 31, down 31]
+    chains = None
+    if world == 1 and args.decode == "chain":
+        from pingala8_llm_b200.ops import Chain
+
+        def cstep(L, grp):
+            x = {("q", "k", "v"): buf["x"] if L == 0 else buf["down"], ("o",): buf["q"], ("gate", "up"): buf["o"],
+                 ("down",): buf["gate"]}[grp]
+            return dict(tensors=[layers[L][n] for n in grp], x=x, outs=[buf[n] for n in grp])
+
+        nL = model["layers"]
+        plan_c = [[cstep(0, groups[0])]] + [[cstep(L - 1, g) for g in groups[1:]] + [cstep(L, groups[0])] for L in range(1, nL)]
+        plan_c.append([cstep(nL - 1, g) for g in groups[1:]])
+        chains = [Chain(c) for c in plan_c]
+        cws = torch.empty(max(c.workspace_size() for c in chains), dtype=torch.uint8, device=dev)
+    launches_per_step = len(chains) if chains is not None else launches_ops
+
+    def step_chain(stream):
+        for c in chains:
+            c.run(workspace=cws, stream=stream)
+
     stream = torch.cuda.Stream(device=dev)
     buf["x"].copy_(x0)
     torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        step(stream)  # warm-up outside capture (kernel attributes, lazy module loading)
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(stream):
-        with torch.cuda.graph(graph, stream=stream):
-            step(stream)
-    torch.cuda.synchronize()
+    graphs = {}
+    for name, fn in (("ops", step), ("chain", step_chain)):
+        if name == "chain" and chains is None:
+            continue
+        with torch.cuda.stream(stream):
+            fn(stream)  # warm-up outside capture (kernel attributes, lazy module loading)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                fn(stream)
+        torch.cuda.synchronize()
+        graphs[name] = g
+    graph = graphs["chain"] if chains is not None else graphs["ops"]
 
     def barrier():
         # the device is idle before the collective: a collective kernel that waits for other ranks must never share
@@ -348,6 +378,20 @@ def run_b200(args, rank, world, local_rank):
     torch.cuda.synchronize()
     barrier()
     t_e2e = e2.elapsed_time(e3) / 1e3
+    # ---- the other decode path at 1 GPU (per-op calls when the headline is the chain), device-timed
+    t_ops = None
+    if chains is not None:
+        for _ in range(args.warmup):
+            graphs["ops"].replay()
+        torch.cuda.synchronize()
+        eo0, eo1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        eo0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(args.steps):
+                graphs["ops"].replay()
+        eo1.record(stream)
+        torch.cuda.synchronize()
+        t_ops = eo0.elapsed_time(eo1) / 1e3
     # ---- roofline per call type: the 32 calls of one group type (one per layer, distinct weights) captured as a
     # graph and replayed; per-call duration = replay time / 32, against the call's algorithmic bytes
     dims = dict(local)
@@ -517,6 +561,7 @@ def run_b200(args, rank, world, local_rank):
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
     t_dev, t_e2e = times[0].item(), times[1].item()
     del graph
+    graphs.clear()
     torch.cuda.synchronize()
     derr = device_error()
     if derr:
@@ -534,6 +579,23 @@ def run_b200(args, rank, world, local_rank):
     dom = max(gnames, key=lambda g: per_group[g][0])
     dom_s, dom_bytes = per_group[dom]
     achieved = dom_bytes / dom_s / 1e9
+    per_call = {g: {"us": round(per_group[g][0] * 1e6, 3), "gbs": round(per_group[g][1] / per_group[g][0] / 1e9, 1)}
+                for g in gnames}
+    if chains is not None:  # the step is nothing but chain launches: the kernel's bytes and time are the step's
+        dom_s = t_dev / args.steps / len(chains)
+        dom_bytes = bytes_token / len(chains)
+        roof = {"kernel": f"k_chain (p8_chain_run: {len(chains)} launches per token, 4 projections per launch in layers "
+                          f"1-31)", "bound": "hbm", "achieved": round(dom_bytes / dom_s / 1e9, 1), "peak": peak,
+                "unit": "GB/s", "frac": round(dom_bytes / dom_s / 1e9 / peak, 4),
+                "traffic": TRAFFIC_BYTES.get("chain"), "algorithmic_bytes": round(dom_bytes), "call_us": round(dom_s * 1e6, 3),
+                "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs (burst copy)",
+                "timing": "CUDA events around graph replays of the whole step; every kernel of the step is a k_chain launch"}
+    else:
+        roof = {"kernel": f"p8_mul_mat_vec_group {dom} (k_act_prep + k_gemv)", "bound": "hbm", "achieved": round(achieved, 1),
+                "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "traffic": TRAFFIC_BYTES.get(dom) if world == 1 else None, "algorithmic_bytes": dom_bytes,
+                "call_us": round(dom_s * 1e6, 3), "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs (burst copy)",
+                "per_call_type": per_call}
     tok_s = args.steps / t_dev  # one token stream; with N GPUs every token is split over the ranks (strong scaling)
     line = {
         "metric": METRIC, "value": round(tok_s, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -548,16 +610,15 @@ def run_b200(args, rank, world, local_rank):
                          if world > 1 else None,
                    "weight_bytes_per_token": bytes_token, "l2": "inputs larger than L2 (1.80 GB of weights streamed per step)",
                    "hbm_gbs_step": round(bytes_token / (t_dev / args.steps) / 1e9, 1)},
-        "roofline": {"kernel": f"p8_mul_mat_vec_group {dom} (k_act_prep + k_gemv)", "bound": "hbm", "achieved": round(achieved, 1),
-                     "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "traffic": TRAFFIC_BYTES.get(dom), "algorithmic_bytes": dom_bytes,
-                     "call_us": round(dom_s * 1e6, 3), "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs (burst copy)",
-                     "per_call_type": {g: {"us": round(per_group[g][0] * 1e6, 3),
-                                           "gbs": round(per_group[g][1] / per_group[g][0] / 1e9, 1)} for g in gnames}},
+        "roofline": roof,
         "e2e": {"value": round(args.steps / t_e2e, 3), "unit": "tok/s", "h2d_bytes_per_step": 4 * h, "d2h_bytes_per_step": 4 * h},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),
     }
+    if t_ops is not None:
+        line["per_op_decode"] = {"tok_s": round(args.steps / t_ops, 3), "ms_per_step": round(1e3 * t_ops / args.steps, 4),
+                                 "kernels": "p8_mul_mat_vec_group per group call (k_act_prep + k_gemv), 256 launches per token",
+                                 "per_call_type": per_call}
     if batched is not None:
         line["batched_decode"] = {
             "kernel": "p8_mul_mat_group per input (k_gx_max + k_gx_prep once, then k_gemm + k_splitk_reduce per projection)",
@@ -730,6 +791,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="skip the batched-product (prefill) measurement")
     ap.add_argument("--no-layer", action="store_true", help="skip the fused-prologue layer measurement")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched-decode (bs 8/32/64) measurement")
+    ap.add_argument("--decode", default="chain", choices=["chain", "ops"],
+                    help="1 GPU decode path timed as the headline: chained launches (p8_chain) or per-op group calls")
     ap.add_argument("--tp-exchange", default="fused", choices=["fused", "nccl"],
                     help="row-parallel sum for N > 1: inside the GEMV over peer memory, or an NCCL all-reduce after it")
     ap.add_argument("--case", default="", help="run one profiling case instead of the bench (see run_case)")

@@ -121,6 +121,38 @@ size_t p8_workspace_size_group_ex(const p8_tensor *const *ts, int n, int64_t nco
 p8_status p8_mul_mat_group(const p8_tensor *const *ts, int n, const float *X, int64_t ncols, int64_t ldx, const p8_prologue *pro,
                            float *const *Ys, const int64_t *ldys, void *workspace, size_t workspace_bytes, void *stream);
 
+/* ---------------------------------------------------------------- chained batch-1 GEMVs -------------------------- */
+
+/* A decode step evaluates a fixed run of MUL_MAT nodes, each reading an earlier one's output, with RMS_NORM + MUL,
+ * SWIGLU and ADD nodes between them (ggml_backend_cuda_graph_compute walking the graph, each MUL_MAT through
+ * ggml_cuda_mul_mat, CU:1330-1342). A chain runs such a run of batch-1 Pingala-8 products as ONE persistent launch
+ * with one grid barrier per step, instead of two kernels and a barrier per product; an extension, the reference
+ * launches every op separately. Step s computes, for its n tensors (equal K and column tables, as
+ * p8_mul_mat_vec_group):
+ *     y_i = W_i x' (+ res_i),  x' = pro(x)
+ * pro as p8_prologue (NONE, RMSNORM with w and eps, SWIGLU with x2 = up). x (and x2) may be any device buffer of K
+ * floats, or exactly an output y_j of the previous step (then the chain reads it straight from that step's partial
+ * sums); any other overlap with the previous step's outputs is refused. An earlier step's output (two or more steps
+ * back) may be read as x, x2 or res. res_i must not overlap y_i. Results equal the separate calls up to float
+ * rounding (the RMSNorm scale multiplies the product instead of its input; the integer table sums are exact).
+ * A plan holds device copies of the steps (buffers are fixed at creation, like a captured graph) and two barrier words:
+ * p8_chain_create allocates and synchronises (set-up time); p8_chain_run only enqueues one launch on the stream and
+ * is capturable; runs of one plan must not overlap on the GPU. A bounded barrier wait that runs out sets bit 32 of
+ * p8_device_error (results of that run invalid). Workspace: p8_chain_workspace_size bytes, 256-byte aligned. */
+typedef struct p8_chain_step {
+    int n;                   /* tensors reading the same input, 1..4 */
+    const p8_tensor *t[4];
+    const float *x;          /* input [K] (16-byte aligned) */
+    p8_prologue pro;         /* kind 0: none */
+    float *y[4];             /* outputs [rows_i] */
+    const float *res[4];     /* optional residual [rows_i] added to y_i (NULL: none) */
+} p8_chain_step;
+typedef struct p8_chain p8_chain;
+p8_status p8_chain_create(const p8_chain_step *steps, int nsteps, p8_chain **out);
+size_t p8_chain_workspace_size(const p8_chain *c);
+p8_status p8_chain_run(const p8_chain *c, void *workspace, size_t workspace_bytes, void *stream);
+p8_status p8_chain_destroy(p8_chain *c);
+
 /* y = W x like p8_mul_mat_vec, but with no workspace argument and no allocation by this library: the scratch is a
  * fixed 6 MiB device array inside the library, for callers that cannot allocate device memory at call time and have
  * no buffer to lend (e.g. a host framework that plans all device memory up front). No counterpart in the reference.
@@ -276,7 +308,7 @@ p8_status p8_gguf_load_linear(p8_gguf *g, int64_t i, uint8_t *out, size_t out_ca
 
 /* Non-zero if a kernel since the last call gave up (that launch's results are invalid), then clears the word. Bits:
  * 1 GEMV table wait, 2 GEMV grid barrier, 4 GEMM pipeline wait timed out; 8 row-parallel exchange wait timed out,
- * 16 exchange entry with a foreign tag. Synchronises the device. */
+ * 16 exchange entry with a foreign tag; 32 chain grid barrier timed out. Synchronises the device. */
 int p8_device_error(void);
 
 const char *p8_status_str(p8_status s);

@@ -40,6 +40,12 @@ class Prologue(C.Structure):
     _fields_ = [("kind", C.c_int), ("w", C.c_void_p), ("x2", C.c_void_p), ("eps", C.c_float)]
 
 
+class ChainStepC(C.Structure):
+    """p8_chain_step: one step of a chained batch-1 GEMV run (p8_chain_create)"""
+    _fields_ = [("n", C.c_int), ("t", C.c_void_p * 4), ("x", C.c_void_p), ("pro", Prologue), ("y", C.c_void_p * 4),
+                ("res", C.c_void_p * 4)]
+
+
 _SIGS = {
     "p8_prepare": (C.c_int, [_vp, _sz, _i64, _i64, _vp, C.POINTER(_vp)]),
     "p8_release": (C.c_int, [_vp]),
@@ -88,6 +94,10 @@ _SIGS = {
     "p8_encode_workspace": (_sz, []),
     "p8_encode_slice": (C.c_int, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _i64, _vp,
                                   _i64, _vp, _sz, _vp]),
+    "p8_chain_create": (C.c_int, [C.POINTER(ChainStepC), C.c_int, C.POINTER(_vp)]),
+    "p8_chain_workspace_size": (_sz, [_vp]),
+    "p8_chain_run": (C.c_int, [_vp, _vp, _sz, _vp]),
+    "p8_chain_destroy": (C.c_int, [_vp]),
     "p8_device_error": (C.c_int, []),
     "p8_status_str": (C.c_char_p, [C.c_int]),
     "p8_build_info": (C.c_char_p, []),

@@ -1,5 +1,6 @@
 // p8_api.cu -- C ABI entry points: tensor preparation, registry and the compute calls.
 #include <cuda_runtime.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <map>
@@ -366,6 +367,17 @@ p8_status p8_decode_int(const p8_tensor *t, int16_t *out, void *stream) {
     if (!out) return P8_ERR_ARG;
     return launch_decode_int(t, out, (cudaStream_t)stream) == cudaSuccess ? P8_OK : P8_ERR_CUDA;
 }
+
+p8_status p8_chain_create(const p8_chain_step *steps, int nsteps, p8_chain **out) { return chain_create(steps, nsteps, out); }
+size_t p8_chain_workspace_size(const p8_chain *c) { return chain_workspace(c); }
+p8_status p8_chain_run(const p8_chain *c, void *workspace, size_t workspace_bytes, void *stream) {
+    static const int pf = [] {  // units per CTA prefetched into L2 ahead of each step (P8_CHAIN_PF; tuning knob)
+        const char *e = getenv("P8_CHAIN_PF");
+        return e ? atoi(e) : 32;
+    }();
+    return chain_run(c, workspace, workspace_bytes, (cudaStream_t)stream, pf);
+}
+p8_status p8_chain_destroy(p8_chain *c) { return chain_destroy(c); }
 
 /* 1 if a kernel since the last call gave up on a bounded wait (results of that launch are invalid). Synchronous. */
 int p8_device_error(void) { return (int)read_and_clear_device_error(); }

@@ -95,4 +95,10 @@ size_t gemm_group_workspace(const p8_tensor *const *ts, int n, int64_t ncols, bo
 p8_status launch_gemm_group(const p8_tensor *const *ts, int n, const float *X, int64_t ncols, int64_t ldx, float *const *Ys,
                             const int64_t *ldys, void *ws, size_t ws_bytes, cudaStream_t st, const p8_prologue *pro = nullptr);
 p8_status gemm_prepare(p8_tensor *t, cudaStream_t st);  // prepare-time per-row scales (rsc)
+
+// chained batch-1 GEMVs (p8_chain.cuh)
+p8_status chain_create(const p8_chain_step *steps, int n, p8_chain **out);
+p8_status chain_destroy(p8_chain *c);
+size_t chain_workspace(const p8_chain *c);
+p8_status chain_run(const p8_chain *c, void *ws, size_t ws_bytes, cudaStream_t st, int pf);
 }  // namespace p8

@@ -1019,4 +1019,9 @@ unsigned int read_and_clear_device_error() {
 // ================================================================================================================
 #include "p8_gemm.cuh"
 
+// ================================================================================================================
+// 4. Chained batch-1 GEMVs in one persistent launch
+// ================================================================================================================
+#include "p8_chain.cuh"
+
 }  // namespace p8

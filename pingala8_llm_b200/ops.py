@@ -232,6 +232,74 @@ def mul_mat_group(tensors, X, outs=None, workspace=None, stream=None, norm_weigh
     return outs
 
 
+class Chain:
+    """A run of batch-1 projections in one persistent launch (p8_chain_*): each step is a dict
+        tensors      list of P8Tensor reading the same input (1..4; q/k/v, gate/up)
+        x            float32 CUDA [K]: any buffer, or exactly an output of the previous step (read from its partials)
+        outs         float32 CUDA [rows_i] per tensor
+        norm_weight  RMSNorm weight [K] (with eps), or up: SwiGLU's up [K] (may be the previous step's other output)
+        res          optional list of residuals [rows_i] (or None entries) added to the outputs
+    Buffers are fixed at creation (like a captured graph); run() enqueues one launch and is capturable. Results equal
+    the separate mul_mat_vec_group calls up to float rounding."""
+
+    def __init__(self, steps):
+        from ._lib import ChainStepC, Prologue
+
+        self._keep = []
+        arr = (ChainStepC * len(steps))()
+        for i, st in enumerate(steps):
+            ts, x, outs = st["tensors"], st["x"], st["outs"]
+            if not 1 <= len(ts) <= 4 or len(outs) != len(ts):
+                raise ValueError("a chain step has 1..4 tensors and one output per tensor")
+            for o, t in zip(outs, ts):
+                if o.dtype != torch.float32 or not o.is_cuda or not o.is_contiguous() or o.numel() != t.rows:
+                    raise ValueError("outs must be contiguous float32 CUDA [rows]")
+            if x.dtype != torch.float32 or not x.is_cuda or not x.is_contiguous() or x.numel() != ts[0].K:
+                raise ValueError("x must be contiguous float32 CUDA [K]")
+            c = arr[i]
+            c.n = len(ts)
+            for j, t in enumerate(ts):
+                c.t[j] = t.handle.value
+                c.y[j] = outs[j].data_ptr()
+                r = (st.get("res") or [None] * len(ts))[j]
+                c.res[j] = r.data_ptr() if r is not None else None
+            c.x = x.data_ptr()
+            nw, up = st.get("norm_weight"), st.get("up")
+            if nw is not None and up is not None:
+                raise ValueError("one prologue per step: norm_weight or up")
+            if nw is not None:
+                c.pro = Prologue(1, nw.data_ptr(), None, float(st.get("eps", 1e-5)))
+            elif up is not None:
+                c.pro = Prologue(2, None, up.data_ptr(), 0.0)
+            self._keep.append((ts, x, outs, nw, up, st.get("res")))
+        h = C.c_void_p()
+        check(lib().p8_chain_create(arr, len(steps), C.byref(h)), "p8_chain_create")
+        self._h = h
+        self._ws = None
+        self.device = steps[0]["x"].device
+
+    def workspace_size(self):
+        return int(lib().p8_chain_workspace_size(self._h))
+
+    def run(self, workspace=None, stream=None):
+        if workspace is None:
+            if self._ws is None:
+                self._ws = torch.empty(max(self.workspace_size(), 256), dtype=torch.uint8, device=self.device)
+            workspace = self._ws
+        check(lib().p8_chain_run(self._h, _ptr(workspace), workspace.numel(), _stream(stream)), "p8_chain_run")
+
+    def close(self):
+        if getattr(self, "_h", None) is not None:
+            lib().p8_chain_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
 def active(slot):
     """ggml_cuda_f44_active: is this device slot a prepared Pingala-8 tensor?"""
     return bool(lib().p8_active(_ptr(slot)))
