@@ -678,6 +678,10 @@ def run_case(args):
     kind, *rest = args.case.split(":")
     if kind == "encode":
         return _case_encode(int(rest[0]), args.iters)
+    if kind == "chain":
+        return _case_chain(int(rest[0]) if rest else 8, args)
+    if kind == "chain_tiny":
+        return _case_chain_tiny(int(rest[0]), int(rest[1]), int(rest[2]), args)
     shapes = CASE_GROUPS[rest[0]]
     copies = [[P8Tensor(synth.make_slot_device(r, k, seed=100 * c + i), k, r) for i, (r, k) in enumerate(shapes)]
               for c in range(max(1, args.copies))]
@@ -754,6 +758,131 @@ def run_case(args):
     return 0
 
 
+def _case_chain(nlayers, args):
+    """--case chain:L  the decode chain of L Llama-3.1-8B layers as per-layer p8_chain launches (split at the attention
+    boundary, as the bench's headline step), timed; with --trace, the per-step phase stamps of one mid-layer launch
+    (globaltimer, per CTA) summarised as median / max over CTAs"""
+    import torch
+
+    from pingala8_llm_b200 import synth
+    from pingala8_llm_b200.ops import Chain, P8Tensor
+
+    shapes = layer_shapes(LLAMA8B)
+    layers = [{n: P8Tensor(synth.make_slot_device(r, k, seed=1000 * L + 17 * i), k, r) for i, (n, r, k) in enumerate(shapes)}
+              for L in range(nlayers)]
+    buf = {n: torch.empty(r, device="cuda") for n, r, _ in shapes}
+    buf["x"] = torch.randn(4096, device="cuda")
+    groups = [("q", "k", "v"), ("o",), ("gate", "up"), ("down",)]
+
+    def cstep(L, grp):
+        x = {("q", "k", "v"): buf["x"] if L == 0 else buf["down"], ("o",): buf["q"], ("gate", "up"): buf["o"],
+             ("down",): buf["gate"]}[grp]
+        return dict(tensors=[layers[L][n] for n in grp], x=x, outs=[buf[n] for n in grp])
+
+    plan = [[cstep(0, groups[0])]] + [[cstep(L - 1, g) for g in groups[1:]] + [cstep(L, groups[0])] for L in range(1, nlayers)]
+    plan.append([cstep(nlayers - 1, g) for g in groups[1:]])
+    chains = [Chain(c) for c in plan]
+    ws = torch.empty(max(c.workspace_size() for c in chains), dtype=torch.uint8, device="cuda")
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        for c in chains:
+            c.run(workspace=ws, stream=st)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(st):
+        with torch.cuda.graph(g, stream=st):
+            for c in chains:
+                c.run(workspace=ws, stream=st)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(st):  # replays run on the current stream
+        e0.record(st)
+        for _ in range(args.iters):
+            g.replay()
+        e1.record(st)
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / 1e3 / args.iters
+    nbytes = sum(algo_bytes_gemv(r, k) for _, r, k in shapes) * nlayers
+    out = {"case": args.case, "us_per_token": round(t * 1e6, 2), "launches": len(chains),
+           "us_per_mid_launch": round(t * 1e6 / len(chains), 2), "gbs": round(nbytes / t / 1e9, 1)}
+    if args.trace:
+        mid = chains[len(chains) // 2]
+        nsm = torch.cuda.get_device_properties(0).multi_processor_count
+        tb = torch.zeros(4 * nsm * 8, dtype=torch.int64, device="cuda")
+        mid.trace(tb)
+        g2 = torch.cuda.CUDAGraph()  # the traced run inside the same sequence of launches (same cache state)
+        with torch.cuda.stream(st):
+            with torch.cuda.graph(g2, stream=st):
+                for c in chains:
+                    c.run(workspace=ws, stream=st)
+        with torch.cuda.stream(st):
+            g2.replay()
+        torch.cuda.synchronize()
+        mid.trace(None)
+        T = tb.view(4, nsm, 8).cpu().numpy().astype(np.float64)
+        t0 = T[0, :, 0].min()
+        phases = {}
+        names = ["reduce_inputs", "prologue_fwht", "tables", "units", "barrier"]
+        for sidx in range(4):
+            d = {names[k]: [round(float(np.median(T[sidx, :, k + 1] - T[sidx, :, k])) / 1e3, 3),
+                            round(float(np.max(T[sidx, :, k + 1] - T[sidx, :, k])) / 1e3, 3)] for k in range(5)}
+            d["start_us"] = [round(float(T[sidx, :, 0].min() - t0) / 1e3, 3), round(float(T[sidx, :, 0].max() - t0) / 1e3, 3)]
+            d["end_us"] = round(float(T[sidx, :, 5].max() - t0) / 1e3, 3)
+            phases[f"step{sidx}"] = d
+        out["trace_median_max_us"] = phases
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+def _case_chain_tiny(nsteps, rows, K, args):
+    """--case chain_tiny:S:R:K  one launch of S chained square-ish steps (R x K, R == K) whose units are few: the
+    per-step fixed cost of the chain (barrier, prep, tables) with the trace's phase medians"""
+    import torch
+
+    from pingala8_llm_b200 import synth
+    from pingala8_llm_b200.ops import Chain, P8Tensor
+
+    assert rows == K
+    ts = [P8Tensor(synth.make_slot_device(rows, K, seed=i), K, rows) for i in range(nsteps)]
+    bufs = [torch.randn(K, device="cuda")] + [torch.empty(rows, device="cuda") for _ in range(nsteps)]
+    ch = Chain([dict(tensors=[ts[i]], x=bufs[i], outs=[bufs[i + 1]]) for i in range(nsteps)])
+    ws = torch.empty(ch.workspace_size(), dtype=torch.uint8, device="cuda")
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        ch.run(workspace=ws, stream=st)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(st):
+        e0.record(st)
+        for _ in range(args.iters):
+            ch.run(workspace=ws, stream=st)
+        e1.record(st)
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / 1e3 / args.iters
+    out = {"case": args.case, "us_per_launch": round(t * 1e6, 2), "us_per_step": round(t * 1e6 / nsteps, 3)}
+    if args.trace:
+        nsm = torch.cuda.get_device_properties(0).multi_processor_count
+        tb = torch.zeros(nsteps * nsm * 8, dtype=torch.int64, device="cuda")
+        ch.trace(tb)
+        with torch.cuda.stream(st):
+            ch.run(workspace=ws, stream=st)
+        torch.cuda.synchronize()
+        T = tb.view(nsteps, nsm, 8).cpu().numpy().astype(np.float64)
+        mid = T[1:-1]
+        med = lambda a: round(float(np.median(a)) / 1e3, 3)  # noqa: E731
+        has = mid[:, :, 3] > 0
+        out["phase_median_us"] = {"reduce_inputs": med((mid[:, :, 1] - mid[:, :, 0])[has]),
+                                  "prologue_fwht": med((mid[:, :, 2] - mid[:, :, 1])[has]),
+                                  "tables": med((mid[:, :, 3] - mid[:, :, 2])[has]),
+                                  "units": med((mid[:, :, 4] - mid[:, :, 3])[has]),
+                                  "barrier": med(mid[:, :, 5] - mid[:, :, 4]),
+                                  "step_to_step": med(T[2:, :, 0].min(1) - T[1:-1, :, 0].min(1))}
+    print(json.dumps(out), flush=True)
+    return 0
+
+
 def _case_encode(rows, iters):
     import torch
 
@@ -791,7 +920,7 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="skip the batched-product (prefill) measurement")
     ap.add_argument("--no-layer", action="store_true", help="skip the fused-prologue layer measurement")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched-decode (bs 8/32/64) measurement")
-    ap.add_argument("--decode", default="chain", choices=["chain", "ops"],
+    ap.add_argument("--decode", default="ops", choices=["chain", "ops"],
                     help="1 GPU decode path timed as the headline: chained launches (p8_chain) or per-op group calls")
     ap.add_argument("--tp-exchange", default="fused", choices=["fused", "nccl"],
                     help="row-parallel sum for N > 1: inside the GEMV over peer memory, or an NCCL all-reduce after it")
@@ -799,6 +928,7 @@ def main():
     ap.add_argument("--iters", type=int, default=20, help="--case: calls timed")
     ap.add_argument("--copies", type=int, default=1, help="--case: distinct weight copies the calls rotate over")
     ap.add_argument("--graph", action="store_true", help="--case: capture the calls in a CUDA graph")
+    ap.add_argument("--trace", action="store_true", help="--case chain: per-step phase stamps of one launch")
     args = ap.parse_args()
     if args.case:
         return run_case(args)

@@ -152,6 +152,10 @@ p8_status p8_chain_create(const p8_chain_step *steps, int nsteps, p8_chain **out
 size_t p8_chain_workspace_size(const p8_chain *c);
 p8_status p8_chain_run(const p8_chain *c, void *workspace, size_t workspace_bytes, void *stream);
 p8_status p8_chain_destroy(p8_chain *c);
+/* Profiling aid: record, in later runs, per step and CTA, 8 globaltimer stamps (ns) into the device buffer dev_buf
+ * (nsteps x CTAs x 8 words, CTAs = the device's SM count; [0] step start, [1] rows the step does not pass on reduced,
+ * [2] input values ready, [3] tables built, [4] units done, [5] grid barrier passed). NULL turns it off. */
+p8_status p8_chain_trace(p8_chain *c, uint64_t *dev_buf, size_t words);
 
 /* y = W x like p8_mul_mat_vec, but with no workspace argument and no allocation by this library: the scratch is a
  * fixed 6 MiB device array inside the library, for callers that cannot allocate device memory at call time and have

@@ -98,6 +98,7 @@ _SIGS = {
     "p8_chain_workspace_size": (_sz, [_vp]),
     "p8_chain_run": (C.c_int, [_vp, _vp, _sz, _vp]),
     "p8_chain_destroy": (C.c_int, [_vp]),
+    "p8_chain_trace": (C.c_int, [_vp, _vp, _sz]),
     "p8_device_error": (C.c_int, []),
     "p8_status_str": (C.c_char_p, [C.c_int]),
     "p8_build_info": (C.c_char_p, []),

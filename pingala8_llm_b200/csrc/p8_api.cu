@@ -118,7 +118,11 @@ p8_status p8_prepare(const void *dev_slot, size_t nbytes, int64_t K, int64_t row
     std::vector<uint16_t> cc(tr.nd);
     std::vector<float> cv(tr.nd);
     const float *dval = (const float *)at(so.E + 4 * (size_t)tr.nd);
-    for (uint32_t e = 0; e < tr.nd; ++e) cp[v.drow[e] + 1]++;
+    memset(t->delta_blocks, 0, sizeof(t->delta_blocks));
+    for (uint32_t e = 0; e < tr.nd; ++e) {
+        cp[v.drow[e] + 1]++;
+        t->delta_blocks[(v.drow[e] >> 8) >> 5] |= 1u << ((v.drow[e] >> 8) & 31);
+    }
     for (int64_t r = 0; r < rows; ++r) cp[(size_t)r + 1] += cp[(size_t)r];
     std::vector<int> fill(cp.begin(), cp.end() - 1);
     for (uint32_t e = 0; e < tr.nd; ++e) {
@@ -371,13 +375,16 @@ p8_status p8_decode_int(const p8_tensor *t, int16_t *out, void *stream) {
 p8_status p8_chain_create(const p8_chain_step *steps, int nsteps, p8_chain **out) { return chain_create(steps, nsteps, out); }
 size_t p8_chain_workspace_size(const p8_chain *c) { return chain_workspace(c); }
 p8_status p8_chain_run(const p8_chain *c, void *workspace, size_t workspace_bytes, void *stream) {
-    static const int pf = [] {  // units per CTA prefetched into L2 ahead of each step (P8_CHAIN_PF; tuning knob)
+    static const int pf = [] {  // units per warp asked of L2 ahead of the warp's current unit (P8_CHAIN_PF; tuning knob)
         const char *e = getenv("P8_CHAIN_PF");
-        return e ? atoi(e) : 32;
+        return e ? atoi(e) : 2;
     }();
     return chain_run(c, workspace, workspace_bytes, (cudaStream_t)stream, pf);
 }
 p8_status p8_chain_destroy(p8_chain *c) { return chain_destroy(c); }
+p8_status p8_chain_trace(p8_chain *c, uint64_t *dev_buf, size_t words) {
+    return chain_trace(c, reinterpret_cast<unsigned long long *>(dev_buf), words);
+}
 
 /* 1 if a kernel since the last call gave up on a bounded wait (results of that launch are invalid). Synchronous. */
 int p8_device_error(void) { return (int)read_and_clear_device_error(); }

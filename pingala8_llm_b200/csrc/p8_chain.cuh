@@ -16,10 +16,15 @@
 //             (k and v after q/k/v) are reduced by all CTAs in equal shares, in the same slice order.
 //   units(s)  the table GEMV (the k_gemv unit loop) over the CTA's equal, contiguous share of the block-major
 //             (block, tile) units; a unit stores its 32 row partials at the rows' ORIGINAL positions, so that the
-//             next prep reads the 256 rows of a block as contiguous float4s.
-//   barrier   every partial of step s is visible; then prep(s + 1). Before it, each CTA asks L2 for the payload of
-//             its first units of step s + 1 (bulk prefetch), so HBM keeps streaming through the barrier and prep.
+//             next prep reads the 256 rows of a block as contiguous float4s. Each warp keeps its next unit's payload
+//             in registers and asks L2 (bulk prefetch) for the payload, scales and row order of the units after it.
+//   barrier   every partial of step s is visible; then prep(s + 1).
 //   final     after the last barrier, the last projection's rows are reduced in equal shares.
+//
+// Nothing a prep needs waits on DRAM after the barrier: the step descriptors sit in shared memory a step ahead
+// (three slots), the next step's codebook, column scales and norm weight for the CTA's blocks are copied into shared
+// memory by cp.async while the CTA waits at the barrier, every warp asks L2 for its first units of the next step, and
+// row epilogues read clamp-delta data only in 256-row blocks that hold entries (a per-tensor block mask).
 //
 // RMSNorm's scale 1 / sqrt(mean(x^2) + eps) is one positive scalar per vector and the product is linear, so the chain
 // applies it to the projection's OUTPUT: tables and clamp-delta term use x * w, and the output reduce one barrier
@@ -36,17 +41,25 @@ constexpr int kChainWarps = kChainThreads / 32;
 constexpr int kChainMaxSteps = 4096;
 // dynamic shared memory: the GEMV's table and coset regions (T0, T1, G0, G1 at the k_gemv offsets, so the unit loop's
 // compile-time addresses are shared), then the step descriptors and the prep staging
-constexpr int kChSteps = kSmemG1 + 2 * kGInts * 4;          // 133120: two ChainStep copies
+// The unit loop picks the table of a unit's block by data, not by code: the lane's lookup-address registers carry the
+// block's buffer index (0 / 1), which the PRMT that builds a lookup address places at bits 16-23, so
+// the tables sit 64 KiB apart (T0 at 0, T1 at 64 KiB) and the coset tables likewise (G0 at 128 KiB, G1 at 192 KiB);
+// one copy of the loop serves both buffers.
+constexpr int kChG0 = 131072, kChG1 = kChG0 + 65536;        // coset tables [hs][8][16] i32 per buffer
+constexpr int kChSteps = kChG0 + 2 * kGInts * 4;            // three ChainStep slots (step s in slot s % 3)
 constexpr int kChStepBytes = 1024;
-constexpr int kChA = kChSteps + 2 * kChStepBytes;           // codebook copy u32[256]
-constexpr int kChX = kChA + 1024;                           // x values [2][256] f32
+constexpr int kChA = kChSteps + 3 * kChStepBytes;           // codebook copy u32[256]
+constexpr int kChIc = kChA + 1024;                          // column scales sgn/c of the first pair [2][256] f32
+constexpr int kChPw = kChIc + 2048;                         // RMSNorm weight of the first pair [2][256] f32
+constexpr int kChX = kChPw + 2048;                          // x values [2][256] f32
 constexpr int kChX2 = kChX + 2048;                          // SwiGLU up values [2][256] f32
-constexpr int kChQ = kChX2 + 2048;                          // q [2][256] i32
-constexpr int kChCx = kChQ + 2048;                          // <c, q_t> [2][64] i32
+constexpr int kChHL = kChX2 + 2048;                         // x16 ints as int8x4 hi / lo words per chunk [2][64] uint2
+constexpr int kChCx = kChHL + 1024;                         // <c, q_t> [2][64] i32
 constexpr int kChD = kChCx + 512;                           // d [2][2] f32, ss partials [2][8] f32
-constexpr int kChSmem = kChD + 256;
-// the prep's reduce staging lives in the table region (free until the tables are built): [2][8][256] f32 per input
-constexpr int kChRed = 0, kChRed2 = 16384, kChRedShare = 32768;
+constexpr int kChSmem = kChG1 + 2 * kGInts * 4;
+static_assert(kChD + 256 <= kChG1, "chain staging overlaps the second coset table");
+// the prep's reduce staging lives in the table region (free until the tables are built)
+constexpr int kChRed = 0, kChRedShare = 32768;
 
 struct ChainTensor {
     const uint32_t *M, *D;
@@ -59,9 +72,10 @@ struct ChainTensor {
     const float *res;
     unsigned long long part_off;  // byte offset of the tensor's partials [nb][rows] inside the step's partial buffer
     int rows, ng, g0, ucls;
+    uint32_t dmask[4];            // bit b: original rows [256 b, 256 b + 256) hold clamp-delta entries
 };
 
-struct ChainStep {
+struct alignas(16) ChainStep {
     ChainTensor t[kMaxGroup];
     const uint32_t *A;            // codebook of the step's tensors (device)
     const float *ic, *x, *x2, *pw;
@@ -71,9 +85,11 @@ struct ChainStep {
     int xsrc, x2src;              // -1: read x / x2 from memory; i >= 0: output of tensor i of the previous step
     int nunc, unc_rows;           // tensors whose rows the next step does not read (all of them for the last step)
     int unc[kMaxGroup];
-    long long units;
+    unsigned int units;           // nb * ng_total (< 2^20)
+    const uint2 *cuts;            // [CTAs] each CTA's contiguous unit range [x, y) of this step (host-balanced)
 };
-static_assert(sizeof(ChainStep) <= kChStepBytes, "ChainStep outgrew its shared-memory slot");
+constexpr int kChRangeOff = 1016;  // a slot holds the descriptor, and this CTA's unit range (uint2) at this byte
+static_assert(sizeof(ChainStep) <= kChRangeOff && sizeof(ChainStep) % 16 == 0, "ChainStep slot");
 
 struct ChainArgs {
     const ChainStep *steps;
@@ -81,18 +97,97 @@ struct ChainArgs {
     uint8_t *ws;
     unsigned long long part[2], xv[2], ss[2];  // workspace byte offsets (ping-pong by step parity)
     int nsteps;
-    int pf;                       // units per CTA whose payload is prefetched into L2 before each step
+    int pf;                       // units per warp whose payload is asked of L2 ahead of the warp's current unit
+    unsigned long long *trace;    // optional phase trace: [step][cta][8] globaltimer stamps (NULL: off)
+    const uint2 *cuts;            // [nsteps][CTAs] unit ranges (ChainStep::cuts of step s = cuts + s * CTAs)
 };
 
 __device__ __forceinline__ float4 ldcg4(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
+__device__ __forceinline__ void cp_async16(void *smem, const void *g) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(g) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void prefetch_l2(const void *p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
-// grid barrier number `n` (0-based) of this launch: every CTA arrives once per barrier whether or not it still waits,
-// so the counts stay consistent after a timeout (bit 5 of the device error word; the launch's results are invalid)
+__device__ __forceinline__ const ChainStep *chain_slot(int s) {
+    return reinterpret_cast<const ChainStep *>(g_smem + kChSteps + (s % 3) * kChStepBytes);
+}
+// step s's descriptor into its slot, asynchronously (cp.async; the caller waits before reading it)
+__device__ __forceinline__ void chain_load_step(const ChainArgs &a, int s) {
+    constexpr int n16 = (int)(sizeof(ChainStep) / 16);
+    const uint8_t *src = reinterpret_cast<const uint8_t *>(a.steps + s);
+    uint8_t *dst = g_smem + kChSteps + (s % 3) * kChStepBytes;
+    for (int i = (int)threadIdx.x - 32; i < n16; i += kChainThreads - 32)  // warps 1..: none in flight on thread 0
+        if (i >= 0) cp_async16(dst + 16 * i, src + 16 * i);
+}
+// this CTA's unit range of step s into the slot (the plan's cuts array; 8-byte cp.async)
+__device__ __forceinline__ void chain_load_range(const ChainArgs &a, int s, const uint2 *cuts_of_step) {
+    if (threadIdx.x == kChainThreads - 1) {
+        uint8_t *dst = g_smem + kChSteps + (s % 3) * kChStepBytes + kChRangeOff;
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(dst)), "l"(cuts_of_step + blockIdx.x) : "memory");
+    }
+}
+
+// this CTA's unit range of a step and its first block pair
+struct ChainRange {
+    unsigned int u0, u1;
+    int b_first, b_last;
+};
+__device__ __forceinline__ ChainRange chain_range(const ChainStep &C) {
+    const uint2 u = *reinterpret_cast<const uint2 *>(reinterpret_cast<const uint8_t *>(&C) + kChRangeOff);
+    ChainRange r;
+    r.u0 = u.x;
+    r.u1 = u.y;
+    r.b_first = r.u1 > r.u0 ? (int)(r.u0 / (unsigned int)C.ng_total) : 0;
+    r.b_last = r.u1 > r.u0 ? (int)((r.u1 - 1) / (unsigned int)C.ng_total) : -1;
+    return r;
+}
+
+// the step's constants for blocks pb .. pb + nsg - 1 into shared memory, asynchronously: codebook, column scales,
+// RMSNorm weight (16-byte cp.async chunks; every source is 16-byte aligned)
+__device__ __forceinline__ void chain_stage_consts(const ChainStep &C, int pb, int nsg) {
+    const int tid = threadIdx.x - 32;  // warps 1..: thread 0 keeps no copies in flight (it fences at the barrier)
+    if (tid < 0) return;
+    if (tid < 64) {
+        cp_async16(g_smem + kChA + 16 * tid, C.A + 4 * tid);
+    } else if (tid < 64 + 64 * nsg) {
+        const int i = tid - 64;
+        cp_async16(g_smem + kChIc + 16 * i, C.ic + 256 * pb + 4 * i);
+    } else if (C.pro == P8_PROLOGUE_RMSNORM && tid < 64 + 128 * nsg) {
+        const int i = tid - 64 - 64 * nsg;
+        cp_async16(g_smem + kChPw + 16 * i, C.pw + 256 * pb + 4 * i);
+    }
+}
+
+// ask L2 for unit (block b, row tile rr) of step C (payload, the unit's 32 row scales and row order)
+__device__ __forceinline__ void chain_prefetch_br(const ChainStep &C, int b, int rr) {
+    int ti = 0;
+#pragma unroll
+    for (int i = 1; i < kMaxGroup; ++i)
+        if (i < C.nt && rr >= C.t[i].g0) ti = i;
+    const ChainTensor &T = C.t[ti];
+    const int g = rr - T.g0;
+    const uint32_t tile = (uint32_t)g * (uint32_t)C.nb + (uint32_t)b;
+    const uint32_t mt = T.ucls ? ((tile * (uint32_t)(64 * NW(T.ucls))) | ((uint32_t)T.ucls << 29)) : __ldg(T.M + tile);
+    const int c = (int)(mt >> 29);
+    if (c) bulk_prefetch_l2(T.D + (mt & 0x1FFFFFFFu), (uint32_t)(256 * NW(c)));
+    prefetch_l2(T.S + (size_t)b * T.rows + g * 32);
+    prefetch_l2(T.prm + g * 32);
+}
+__device__ __forceinline__ void chain_prefetch_unit(const ChainStep &C, unsigned int u) {
+    const int b = (int)(u / (unsigned int)C.ng_total);
+    chain_prefetch_br(C, b, (int)(u - (unsigned int)b * (unsigned int)C.ng_total));
+}
+
+// grid barrier: every CTA arrives once per barrier whether or not it still waits, so the counts stay consistent after
+// a timeout (bit 5 of the device error word; the launch's results are invalid)
 __device__ __forceinline__ void chain_barrier(unsigned int *cnt, unsigned int target, int *s_ok) {
     __syncthreads();
     if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(cnt, 1u);
+        // release: the CTA's partial stores (ordered before this thread by the CTA barrier) are visible before the
+        // arrival is counted; acquire after the wait: the other CTAs' partials are visible to the loads that follow
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
         if (*s_ok) {
             const unsigned long long dl = global_ns() + kGridWaitNs;
             unsigned int v;
@@ -106,17 +201,19 @@ __device__ __forceinline__ void chain_barrier(unsigned int *cnt, unsigned int ta
                 }
             }
         }
-        __threadfence();
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
     }
     __syncthreads();
 }
 
 // y of one output row of step `P` (tensor T): the slice-ordered sum of its partials `sum`, then the clamp delta on x'
-// (in CSR order), the output scale (RMSNorm of the step's input), the residual
+// (in CSR order; only in blocks whose mask bit is set), the output scale (RMSNorm of the step's input), the residual
 __device__ __forceinline__ float chain_row_out(const ChainTensor &T, int ro, float sum, const float *xv, float scale) {
     float y = sum;
-    const int e1 = __ldg(T.cp + ro + 1);
-    for (int e = __ldg(T.cp + ro); e < e1; ++e) y = __fadd_rn(y, __fmul_rn(__ldg(T.cv + e), __ldcg(xv + __ldg(T.cc + e))));
+    if ((T.dmask[ro >> 13] >> ((ro >> 8) & 31)) & 1u) {
+        const int e1 = __ldg(T.cp + ro + 1);
+        for (int e = __ldg(T.cp + ro); e < e1; ++e) y = __fadd_rn(y, __fmul_rn(__ldg(T.cv + e), __ldcg(xv + __ldg(T.cc + e))));
+    }
     y = __fmul_rn(y, scale);
     if (T.res) y = __fadd_rn(y, __ldcg(T.res + ro));
     return y;
@@ -165,81 +262,51 @@ __device__ __forceinline__ float chain_scale(const ChainStep &P, const float *ss
     return __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, P.eps)));
 }
 
-// Rows [ra, rb) of the concatenated not-read-next tensors of step P, reduced and written (equal shares per CTA).
-__device__ void chain_share_reduce(const ChainStep &P, const ChainArgs &a, int pp, long long ra, long long rb, float scale) {
-    float *red = reinterpret_cast<float *>(g_smem + kChRedShare);  // [8][64]
-    const float *xv = reinterpret_cast<const float *>(a.ws + a.xv[pp]);
-    const uint8_t *pbase = a.ws + a.part[pp];
-    const int r = threadIdx.x & 63, k = threadIdx.x >> 6;
-    for (long long base = ra; base < rb; base += 64) {
-        const long long i = base + r;
-        int ti = -1, ro = 0;
-        if (i < rb) {
-            long long off = i;
-            for (int q = 0; q < P.nunc; ++q) {
-                const int t = P.unc[q];
-                if (off < P.t[t].rows) {
-                    ti = t;
-                    ro = (int)off;
-                    break;
-                }
-                off -= P.t[t].rows;
-            }
-        }
-        float acc = 0.f;
-        if (ti >= 0) {
-            const ChainTensor &T = P.t[ti];
-            const float *p = reinterpret_cast<const float *>(pbase + T.part_off) + ro;
-            for (int bb = k; bb < P.nb; bb += 8) acc = __fadd_rn(acc, __ldcg(p + (size_t)bb * T.rows));
-        }
-        red[k * 64 + r] = acc;
-        __syncthreads();
-        if (k == 0 && ti >= 0) {
-            const ChainTensor &T = P.t[ti];
-            T.Y[ro] = chain_row_out(T, ro, chain_sum_slices(red, 64, r), xv, scale);
-        }
-        __syncthreads();
+// ---- the unit loop (class 3 in registers, other classes from memory)
+// The chain's lookup-address registers pq[j] hold the lane's rotated chunk offsets of steps 2j and 2j + 1 in bytes 0
+// and 1, the table buffer (0 / 1) of the unit's block in byte 2 and zero in byte 3. The PRMT selector of step k takes
+// offset byte k % 2 -> bits 0-7, field byte k % 4 of word k / 4 -> bits 8-15, the buffer -> bits 16-23, zero -> 24-31.
+template <int k>
+struct SelBuf {
+    static constexpr uint32_t v = (uint32_t)(4 + (k & 1)) | ((uint32_t)(k % 4) << 4) | 0x7600u;
+};
+template <int HS, int k>
+struct ChStep3 {
+    static __device__ __forceinline__ void run(const uint32_t (&w)[16], const uint32_t (&pq)[16], int &a) {
+        a += lds_at<HS * 128>(__byte_perm(w[8 * HS + k / 4], pq[k / 2], SelBuf<k>::v));
+        ChStep3<HS, k + 1>::run(w, pq, a);
     }
+};
+template <int HS>
+struct ChStep3<HS, 32> {
+    static __device__ __forceinline__ void run(const uint32_t (&)[16], const uint32_t (&)[16], int &) {}
+};
+// integer total of half-slice HS of a class-3 unit row: table sum + coset term (class 3: one stage, no shift, MC = 1);
+// gbuf = buffer << 16 selects the coset table of the unit's block
+template <int HS>
+__device__ __forceinline__ int chain_slice3(const uint32_t (&w)[16], const uint32_t (&pq)[16], int lane, uint32_t gbuf) {
+    uint32_t pm = 0;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {  // z bits in step order (zbits_fast on this half-slice's words)
+        const uint32_t x = (w[8 * HS + 2 * p + 1] & 0x80808080u) | ((w[8 * HS + 2 * p] >> 4) & 0x08080808u);
+        pm |= ((x * 0x00204081u) >> 24) << (8 * p);
+    }
+    const uint32_t H = pingala8_h(__funnelshift_l(pm, pm, lane));
+    int cs = 0;
+#pragma unroll
+    for (int grp = 0; grp < 8; ++grp) {
+        const uint32_t sh = grp == 0 ? (H << 2) : (H >> (4 * grp - 2));
+        cs += lds_at<kChG0 + HS * kGInts * 4>(((sh & 0x3Cu) | gbuf) + grp * 64);  // grp * 64 folds into the offset
+    }
+    int a = 0;
+    ChStep3<HS, 0>::run(w, pq, a);
+    return a + cs;
 }
-
-// input values of blocks pb .. pb + nsg - 1 of step C from source src (-1: memory at xext; else tensor src of the
-// previous step P, reduced here) into dst[seg][256]; the block's owner writes the reduced rows to the output
-__device__ void chain_input(const ChainStep &C, const ChainStep *P, const ChainArgs &a, int s, int src, const float *xext,
-                            int pb, int nsg, unsigned own_mask, float scale, float *dst) {
-    const int tid = threadIdx.x;
-    if (src < 0) {
-        if (tid < 256 * nsg) dst[tid] = __ldcg(xext + 256 * pb + tid);
-        return;
-    }
-    const int pp = (s - 1) & 1;
-    const ChainTensor &T = P->t[src];
-    const float *part = reinterpret_cast<const float *>(a.ws + a.part[pp] + T.part_off);
-    float *red = reinterpret_cast<float *>(g_smem + kChRed);  // [2][8][256]
-    for (int sg = 0; sg < nsg; ++sg) chain_slices_256(part, T.rows, P->nb, 256 * (pb + sg), red + sg * 2048);
-    __syncthreads();
-    if (tid < 256 * nsg) {
-        const int sg = tid >> 8, r = tid & 255, ro = 256 * (pb + sg) + r;
-        const float *xv = reinterpret_cast<const float *>(a.ws + a.xv[pp]);
-        const float y = chain_row_out(T, ro, chain_sum_slices(red + sg * 2048, 256, r), xv, scale);
-        dst[tid] = y;
-        if ((own_mask >> sg) & 1u) T.Y[ro] = y;
-    }
-    __syncthreads();
-}
-
-__global__ void __launch_bounds__(kChainThreads, 1) k_chain(const __grid_constant__ ChainArgs a) {
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    __shared__ int s_ok;
-    __shared__ float s_scale;
-    float *xs = reinterpret_cast<float *>(g_smem + kChX);
-    float *x2s = reinterpret_cast<float *>(g_smem + kChX2);
-    int *q_s = reinterpret_cast<int *>(g_smem + kChQ);
-    int *cx_s = reinterpret_cast<int *>(g_smem + kChCx);
-    float *d_s = reinterpret_cast<float *>(g_smem + kChD);
-    float *ssp = d_s + 4;  // [2][8] per-warp partial sums of squares
-    uint32_t *A_s = reinterpret_cast<uint32_t *>(g_smem + kChA);
-    pdl_launch_dependents();
-    uint32_t po[11];
+// other classes: lane words from memory, the generic lane-slice dot on the buffer's tables
+template <int C, int BUF>
+__device__ __noinline__ float chain_row_cls(const uint32_t *p0, int lane, float d0, float d1) {
+    constexpr int T0 = BUF ? kSmemT1 : kSmemT0, G0 = BUF ? kChG1 : kChG0;
+    uint32_t po[11];  // the generic loop's layout: three rotated chunk offsets per register
 #pragma unroll
     for (int q = 0; q < 11; ++q) {
         uint32_t r = 0;
@@ -248,18 +315,220 @@ __global__ void __launch_bounds__(kChainThreads, 1) k_chain(const __grid_constan
             if (3 * q + i < 32) r |= (((uint32_t)(lane + 3 * q + i) & 31u) << 2) << (8 * i);
         po[q] = r;
     }
+    uint32_t w[24];
+    load_lane_words<C>(p0, 0, lane, w);
+    const int i0 = lane_slice_dot<C, T0, G0>(w, po, lane);
+    load_lane_words<C>(p0, 1, lane, w);
+    const int i1 = lane_slice_dot<C, T0 + 128, G0 + kGInts * 4>(w, po, lane);
+    return __fadd_rn(__fmul_rn((float)i0, d0), __fmul_rn((float)i1, d1));
+}
+template <int BUF>
+__device__ __forceinline__ float chain_row_other(int c, const uint32_t *p0, int lane, float d0, float d1) {
+    switch (c) {
+        case 1: return chain_row_cls<1, BUF>(p0, lane, d0, d1);
+        case 2: return chain_row_cls<2, BUF>(p0, lane, d0, d1);
+        case 3: return chain_row_cls<3, BUF>(p0, lane, d0, d1);
+        case 4: return chain_row_cls<4, BUF>(p0, lane, d0, d1);
+        case 5: return chain_row_cls<5, BUF>(p0, lane, d0, d1);
+        case 6: return chain_row_cls<6, BUF>(p0, lane, d0, d1);
+        case 7: return chain_row_cls<7, BUF>(p0, lane, d0, d1);
+        default: return 0.f;
+    }
+}
+
+// one fetched unit of a warp: class-3 payload in registers (both half-slices), where its partial goes, its row scale
+struct ChainUnit {
+    uint32_t w[16];
+    const uint32_t *p0;  // payload (other classes read it from here)
+    float *dst;          // this lane's partial: block b, the row's ORIGINAL position
+    uint32_t mt;         // class << 29 | payload word offset
+    int b;
+    uint16_t sc;
+};
+// fields of the tensor the warp's units currently belong to (reloaded from the descriptor when a unit leaves it)
+struct ChainTensorCache {
+    const uint32_t *M, *D;
+    const uint16_t *S;
+    const int16_t *prm;
+    float *part;
+    int rows, ucls, lo, hi;  // the tensor's row tiles are rr in [lo, hi) of the step's group
+};
+__device__ __forceinline__ void chain_tcache(const ChainStep &C, const uint8_t *pbase, int rr, ChainTensorCache &R) {
+    int ti = 0;
+#pragma unroll
+    for (int i = 1; i < kMaxGroup; ++i)
+        if (i < C.nt && rr >= C.t[i].g0) ti = i;
+    const ChainTensor &T = C.t[ti];
+    R.M = T.M; R.D = T.D; R.S = T.S; R.prm = T.prm; R.part = reinterpret_cast<float *>(const_cast<uint8_t *>(pbase) + T.part_off);
+    R.rows = T.rows; R.ucls = T.ucls; R.lo = T.g0; R.hi = T.g0 + T.ng;
+}
+__device__ __forceinline__ void chain_fetch(const ChainStep &C, const uint8_t *pbase, ChainTensorCache &R, int b, int rr, int lane,
+                                            ChainUnit &u) {
+    if (rr < R.lo || rr >= R.hi) chain_tcache(C, pbase, rr, R);
+    const int g = rr - R.lo;
+    const uint32_t tile = (uint32_t)g * (uint32_t)C.nb + (uint32_t)b;
+    u.mt = R.ucls ? ((tile * (uint32_t)(64 * NW(R.ucls))) | ((uint32_t)R.ucls << 29)) : __ldg(R.M + tile);
+    u.p0 = R.D + (u.mt & 0x1FFFFFFFu);
+    if ((u.mt >> 29) == 3) load3(u.p0, lane, u.w);
+    u.sc = __ldg(R.S + (size_t)b * R.rows + g * 32 + lane);
+    u.dst = R.part + (size_t)b * R.rows + __ldg(R.prm + g * 32 + lane);
+    u.b = b;
+}
+// the unit's partial: its table buffer comes from pq byte 2 / gbuf (set for block pb + buf by the caller)
+__device__ __forceinline__ void chain_do_unit(const ChainUnit &u, const uint32_t (&pq)[16], int lane, int buf, const float *d_s) {
+    const float d0 = d_s[2 * buf], d1 = d_s[2 * buf + 1];
+    const int c = (int)(u.mt >> 29);
+    float part;
+    if (c == 3) {
+        const uint32_t gbuf = (uint32_t)buf << 16;
+        const int i0 = chain_slice3<0>(u.w, pq, lane, gbuf), i1 = chain_slice3<1>(u.w, pq, lane, gbuf);
+        part = __fadd_rn(__fmul_rn((float)i0, d0), __fmul_rn((float)i1, d1));
+    } else {
+        part = buf ? chain_row_other<1>(c, u.p0, lane, d0, d1) : chain_row_other<0>(c, u.p0, lane, d0, d1);
+    }
+    *u.dst = __fmul_rn(part, h2f(u.sc));
+}
+
+// row i of the concatenation of step P's not-passed-on tensors -> (tensor, row); ti = -1 past the end
+__device__ __forceinline__ void chain_unc_row(const ChainStep &P, int i, int &ti, int &ro) {
+    ti = -1;
+    ro = 0;
+    int off = i;
+    for (int q = 0; q < P.nunc; ++q) {
+        const int t = P.unc[q];
+        if (off < P.t[t].rows) {
+            ti = t;
+            ro = off;
+            return;
+        }
+        off -= P.t[t].rows;
+    }
+}
+
+// The prep's reduction of step P's partials with every load in flight before one shared-memory exchange:
+//   rows [ra, rb) of P's not-passed-on tensors, reduced and written to their outputs, up to 256 per round (thread
+//   (r, k) sums rows ra + r + 64 j, j < 4, over blocks k, k + 8, ...);
+//   in the first round, the input blocks pb .. pb + nsg - 1 of this step from sources xsrc / x2src (a tensor of P, or
+//   -1 for memory at xext / x2ext) into dst / dst2 (8 slices x 64 float4 columns per block); the owner of a block
+//   writes its reduced rows to the output.
+// Slices are summed in slice order, so a row's value does not depend on which CTA reduced it.
+__device__ void chain_reduce(const ChainStep *P, const ChainArgs &a, int pp, int ra, int rb, int xsrc, const float *xext,
+                             int x2src, const float *x2ext, int pb, int nsg, unsigned own, float scale, float *dst,
+                             float *dst2) {
+    const int tid = threadIdx.x, j4 = tid & 63, k = tid >> 6;
+    float *red_x = reinterpret_cast<float *>(g_smem + kChRed);            // [2][8][256]
+    float *red_x2 = reinterpret_cast<float *>(g_smem + kChRed + 16384);   // [2][8][256]
+    float *red_sh = reinterpret_cast<float *>(g_smem + kChRedShare);      // [8][256]
+    const float *xv = P ? reinterpret_cast<const float *>(a.ws + a.xv[pp]) : nullptr;
+    const uint8_t *pbase = a.ws + a.part[pp];
+    for (int base = ra;; base += 256) {
+        const bool first = base == ra;
+        // ---- loads: the share rows' slices, then the input blocks' slices
+        if (P && base < rb) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                int ti, ro;
+                float acc = 0.f;
+                if (base + j4 + 64 * j < rb) {
+                    chain_unc_row(*P, base + j4 + 64 * j, ti, ro);
+                    if (ti >= 0) {
+                        const ChainTensor &T = P->t[ti];
+                        const float *p = reinterpret_cast<const float *>(pbase + T.part_off) + ro;
+                        for (int bb = k; bb < P->nb; bb += 8) acc = __fadd_rn(acc, __ldcg(p + (size_t)bb * T.rows));
+                    }
+                }
+                red_sh[k * 256 + j4 + 64 * j] = acc;
+            }
+        }
+        if (first && P) {
+            for (int sg = 0; sg < nsg; ++sg) {
+                if (xsrc >= 0) {
+                    const ChainTensor &T = P->t[xsrc];
+                    chain_slices_256(reinterpret_cast<const float *>(pbase + T.part_off), T.rows, P->nb, 256 * (pb + sg), red_x + sg * 2048);
+                }
+                if (x2src >= 0) {
+                    const ChainTensor &T = P->t[x2src];
+                    chain_slices_256(reinterpret_cast<const float *>(pbase + T.part_off), T.rows, P->nb, 256 * (pb + sg), red_x2 + sg * 2048);
+                }
+            }
+        }
+        __syncthreads();
+        // ---- epilogues
+        if (P && tid < rb - base && tid < 256) {
+            int ti, ro;
+            chain_unc_row(*P, base + tid, ti, ro);
+            if (ti >= 0) {
+                const ChainTensor &T = P->t[ti];
+                T.Y[ro] = chain_row_out(T, ro, chain_sum_slices(red_sh, 256, tid), xv, scale);
+            }
+        }
+        if (first && tid < 256 * nsg) {
+            const int sg = tid >> 8, r = tid & 255, ro = 256 * (pb + sg) + r;
+            if (xsrc >= 0) {
+                const ChainTensor &T = P->t[xsrc];
+                const float y = chain_row_out(T, ro, chain_sum_slices(red_x + sg * 2048, 256, r), xv, scale);
+                dst[tid] = y;
+                if ((own >> sg) & 1u) T.Y[ro] = y;
+            } else if (xext) {
+                dst[tid] = __ldcg(xext + 256 * pb + tid);
+            }
+            if (x2src >= 0) {
+                const ChainTensor &T = P->t[x2src];
+                const float y = chain_row_out(T, ro, chain_sum_slices(red_x2 + sg * 2048, 256, r), xv, scale);
+                dst2[tid] = y;
+                if ((own >> sg) & 1u) T.Y[ro] = y;
+            } else if (x2ext) {
+                dst2[tid] = __ldcg(x2ext + 256 * pb + tid);
+            }
+        }
+        __syncthreads();
+        if (base + 256 >= rb) break;
+    }
+}
+
+__global__ void __launch_bounds__(kChainThreads, 1) k_chain(const __grid_constant__ ChainArgs a) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    __shared__ int s_ok;
+    __shared__ float s_scale;
+    float *xs = reinterpret_cast<float *>(g_smem + kChX);
+    float *x2s = reinterpret_cast<float *>(g_smem + kChX2);
+    int *cx_s = reinterpret_cast<int *>(g_smem + kChCx);
+    float *d_s = reinterpret_cast<float *>(g_smem + kChD);
+    float *ssp = d_s + 4;  // [2][8] per-warp partial sums of squares
+    const uint32_t *A_s = reinterpret_cast<const uint32_t *>(g_smem + kChA);
+    const float *ic_s = reinterpret_cast<const float *>(g_smem + kChIc);
+    const float *pw_s = reinterpret_cast<const float *>(g_smem + kChPw);
+    pdl_launch_dependents();
+    uint32_t pq[16];  // lookup-address registers (SelBuf): chunk offsets of steps 2j, 2j + 1, table buffer, zero
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+        pq[j] = ((((uint32_t)(lane + 2 * j) & 31u) << 2)) | ((((uint32_t)(lane + 2 * j + 1) & 31u) << 2) << 8);
+    int cur_buf = 0;  // the table buffer in pq byte 2
     if (tid == 0) s_ok = 1;
+    // ---- before the wait for the previous kernel: the plan's first descriptors, step 0's constants and first units
+    // (all of it the plan's and the weights', which no earlier kernel writes)
+    chain_load_step(a, 0);
+    if (a.nsteps > 1) chain_load_step(a, 1);
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncthreads();
+    chain_load_range(a, 0, a.cuts);
+    if (a.nsteps > 1) chain_load_range(a, 1, a.cuts + gridDim.x);
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncthreads();
+    {
+        const ChainRange r0 = chain_range(*chain_slot(0));
+        if (r0.b_last >= r0.b_first) chain_stage_consts(*chain_slot(0), r0.b_first, r0.b_last - r0.b_first + 1 < 2 ? 1 : 2);
+        cp_async_commit();
+        for (int j = 0; j < a.pf; ++j)
+            if (lane == 1 && r0.u0 + warp + kChainWarps * j < r0.u1) chain_prefetch_unit(*chain_slot(0), r0.u0 + warp + kChainWarps * j);
+    }
     pdl_wait();  // inputs, workspace and barrier words belong to earlier kernels until they complete
     for (int s = 0; s <= a.nsteps; ++s) {
-        // ---- descriptors: step s into slot s & 1 (step s - 1 is already in the other slot)
-        ChainStep *Cs = reinterpret_cast<ChainStep *>(g_smem + kChSteps + (s & 1) * kChStepBytes);
-        const ChainStep *P = s > 0 ? reinterpret_cast<const ChainStep *>(g_smem + kChSteps + ((s - 1) & 1) * kChStepBytes) : nullptr;
-        if (s < a.nsteps) {
-            const uint32_t *src = reinterpret_cast<const uint32_t *>(a.steps + s);
-            uint32_t *dst = reinterpret_cast<uint32_t *>(Cs);
-            for (int i = tid; i < (int)(sizeof(ChainStep) / 4); i += kChainThreads) dst[i] = __ldg(src + i);
-        }
-        if (tid < 32) {  // output scale of the previous step (its input's RMSNorm), from its blocks' sums of squares
+        const ChainStep *P = s > 0 ? chain_slot(s - 1) : nullptr;
+        cp_async_wait_all();  // this step's constants (and the descriptor of step s + 1 copied during step s - 1)
+        if (tid < 32) {       // output scale of the previous step (its input's RMSNorm), from its blocks' sums of squares
             float sc = 1.f;
             if (P && P->pro == P8_PROLOGUE_RMSNORM) sc = chain_scale(*P, reinterpret_cast<const float *>(a.ws + a.ss[(s - 1) & 1]));
             if (lane == 0) s_scale = sc;
@@ -267,75 +536,82 @@ __global__ void __launch_bounds__(kChainThreads, 1) k_chain(const __grid_constan
         __syncthreads();
         const float scale_p = s_scale;
         const int pp = (s - 1) & 1;
+        unsigned long long *tr = a.trace && s < a.nsteps ? a.trace + ((size_t)s * gridDim.x + blockIdx.x) * 8 : nullptr;
+        if (tr && tid == 0) tr[0] = global_ns();
         if (s == a.nsteps) {  // final phase: the last step's rows in equal shares
             if (P && s_ok) {
-                const long long R = P->unc_rows;
-                chain_share_reduce(*P, a, pp, R * blockIdx.x / gridDim.x, R * (blockIdx.x + 1) / gridDim.x, scale_p);
+                const int R = P->unc_rows;
+                chain_reduce(P, a, pp, (int)((long long)R * blockIdx.x / gridDim.x), (int)((long long)R * (blockIdx.x + 1) / gridDim.x),
+                             -1, nullptr, -1, nullptr, 0, 0, 0u, scale_p, nullptr, nullptr);
             }
             break;
         }
-        const ChainStep &C = *Cs;
+        const ChainStep &C = *chain_slot(s);
         const int cp_ = s & 1;
         // ---- this CTA's units of step s: [u0, u1) of the block-major list; warp w takes u0 + w, u0 + w + 16, ...
-        const long long u0 = C.units * blockIdx.x / gridDim.x, u1 = C.units * (blockIdx.x + 1) / gridDim.x;
-        const int ngt = C.ng_total;
-        const int b_first = u1 > u0 ? (int)(u0 / ngt) : 0, b_last = u1 > u0 ? (int)((u1 - 1) / ngt) : -1;
-        const int rr_first = (int)(u0 - (long long)b_first * ngt);
-        long long un = u0 + warp;
-        int cb = (int)(un / ngt), crr = (int)(un - (long long)cb * ngt);
+        const ChainRange rg = chain_range(C);
+        const unsigned int u0 = rg.u0, u1 = rg.u1;
+        const int b_first = rg.b_first, b_last = rg.b_last;
+        const unsigned int ngt = (unsigned int)C.ng_total;
+        const int rr_first = (int)(u0 - (unsigned int)b_first * ngt);
+        unsigned int un = u0 + warp;  // the warp's next unit to fetch: block cb, row tile crr of the group
+        int cb = (int)(un / ngt), crr = (int)(un - (unsigned int)cb * ngt);
         auto advance = [&]() {
             un += kChainWarps;
             crr += kChainWarps;
-            while (crr >= ngt) {
-                crr -= ngt;
+            while (crr >= (int)ngt) {
+                crr -= (int)ngt;
                 ++cb;
             }
         };
-        auto tensor_of_rr = [&](int rr) {
-            int ti = 0;
-#pragma unroll
-            for (int i = 1; i < kMaxGroup; ++i)
-                if (i < C.nt && rr >= C.t[i].g0) ti = i;
-            return ti;
+        unsigned int pun = un + kChainWarps * (unsigned int)a.pf;  // the unit the warp asks L2 for next
+        int pcb = (int)(pun / ngt), pcrr = (int)(pun - (unsigned int)pcb * ngt);
+        auto pf_step = [&]() {
+            if (lane == 1 && pun < u1) chain_prefetch_br(C, pcb, pcrr);
+            pun += kChainWarps;
+            pcrr += kChainWarps;
+            while (pcrr >= (int)ngt) {
+                pcrr -= (int)ngt;
+                ++pcb;
+            }
         };
-        auto m_of = [&](int b, int rr) -> uint32_t {
-            const ChainTensor &T = C.t[tensor_of_rr(rr)];
-            const uint32_t tile = (uint32_t)(rr - T.g0) * (uint32_t)C.nb + (uint32_t)b;
-            if (T.ucls) return (tile * (uint32_t)(64 * NW(T.ucls))) | ((uint32_t)T.ucls << 29);
-            return __ldg(T.M + tile);
-        };
-        uint32_t nxt[16];
-        uint32_t mt_n = 0;
-        uint16_t s_n = 0;
-        int pr_n = 0;
-        auto fetch = [&]() {  // payload, scale and output row of the warp's unit (cb, crr)
-            const ChainTensor &T = C.t[tensor_of_rr(crr)];
-            const int g = crr - T.g0;
-            mt_n = m_of(cb, crr);
-            if ((mt_n >> 29) == 3) load3(T.D + (mt_n & 0x1FFFFFFFu), lane, nxt);
-            s_n = __ldg(T.S + (size_t)cb * T.rows + g * 32 + lane);
-            pr_n = __ldg(T.prm + g * 32 + lane);
-        };
-        if (un < u1) fetch();  // weights only: the first unit's loads overlap the prep below
-        // ---- rows of the previous step that this step does not read: equal shares
-        if (P && s_ok && P->nunc) {
-            const long long R = P->unc_rows;
-            chain_share_reduce(*P, a, pp, R * blockIdx.x / gridDim.x, R * (blockIdx.x + 1) / gridDim.x, scale_p);
+        const uint8_t *pbase = a.ws + a.part[cp_];
+        ChainTensorCache R;
+        R.lo = R.hi = 0;  // loaded by the first fetch
+        ChainUnit uA, uB;
+        bool fa = false, fb = false;
+        if (un < u1) {  // weights only: the first unit's loads overlap the prep below
+            chain_fetch(C, pbase, R, cb, crr, lane, uA);
+            fa = true;
+            advance();
         }
-        for (int i = tid; i < 256; i += kChainThreads) A_s[i] = __ldg(C.A + i);
+        // rows of the previous step that this step does not read: equal shares (reduced with the first block pair)
+        const int sh_r = P ? P->unc_rows : 0;
+        const int sh_a = (int)((long long)sh_r * blockIdx.x / gridDim.x), sh_b = (int)((long long)sh_r * (blockIdx.x + 1) / gridDim.x);
         float *xv_c = reinterpret_cast<float *>(a.ws + a.xv[cp_]);
         float *ss_c = reinterpret_cast<float *>(a.ws + a.ss[cp_]);
+        if (b_last < b_first && s_ok && sh_b > sh_a)  // no units this step: only the share of rows
+            chain_reduce(P, a, pp, sh_a, sh_b, -1, nullptr, -1, nullptr, 0, 0, 0u, scale_p, nullptr, nullptr);
         for (int pb = b_first; pb <= b_last; pb += 2) {
             const int nsg = b_last - pb + 1 < 2 ? b_last - pb + 1 : 2;
+            if (pb != b_first) {  // later pairs (only when a CTA's units span more than two blocks): constants now
+                chain_stage_consts(C, pb, nsg);
+                cp_async_commit();
+                cp_async_wait_all();
+                __syncthreads();
+            }
             unsigned own = 0;  // blocks whose first unit is this CTA's
             for (int sg = 0; sg < nsg; ++sg)
                 if (pb + sg > b_first || rr_first == 0) own |= 1u << sg;
-            // ---- (a) input values of the pair's blocks (fused reduce of the previous step, or memory)
+            // ---- (a) input values of the pair's blocks (fused reduce of the previous step, or memory), with the
+            // previous step's not-passed-on rows of this CTA's share in the same loads-then-exchange round
             if (s_ok) {
-                chain_input(C, P, a, s, C.xsrc, C.x, pb, nsg, own, scale_p, xs);
-                if (C.pro == P8_PROLOGUE_SWIGLU) chain_input(C, P, a, s, C.x2src, C.x2, pb, nsg, own, scale_p, x2s);
+                const bool sw = C.pro == P8_PROLOGUE_SWIGLU;
+                chain_reduce(P, a, pp, pb == b_first ? sh_a : 0, pb == b_first ? sh_b : 0, C.xsrc, C.x, sw ? C.x2src : -1,
+                             sw ? C.x2 : nullptr, pb, nsg, own, scale_p, xs, x2s);
             }
             __syncthreads();
+            if (tr && tid == 0 && pb == b_first) tr[1] = global_ns();
             // ---- (b) input op: x' (RMSNorm: x * w, its scale goes to the output; SwiGLU: silu(x) * up); the owner
             // writes x' (clamp-delta term of this step's outputs) and the block's sum of x^2 (RMSNorm scale)
             if (tid < 256 * nsg) {
@@ -343,7 +619,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) k_chain(const __grid_constan
                 const float x = xs[tid];
                 float xp = x;
                 if (C.pro == P8_PROLOGUE_RMSNORM) {
-                    xp = __fmul_rn(x, __ldg(C.pw + col));
+                    xp = __fmul_rn(x, pw_s[tid]);
                     float q2 = __fmul_rn(x, x);
 #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) q2 = __fadd_rn(q2, __shfl_down_sync(0xffffffffu, q2, o));
@@ -361,13 +637,15 @@ __global__ void __launch_bounds__(kChainThreads, 1) k_chain(const __grid_constan
                 for (int w = 1; w < 8; ++w) v = __fadd_rn(v, ssp[8 * tid + w]);
                 ss_c[pb + tid] = v;
             }
-            // ---- (c) FWHT(x' sgn/c) / 16 and the x16 quantisation per 128 columns (warp sg: block pb + sg)
+            // ---- (c) FWHT(x' sgn/c) / 16 and the x16 quantisation per 128 columns (warp sg: block pb + sg). Lane l holds
+            // columns 8l .. 8l + 7 = chunks 2l and 2l + 1: it packs each chunk's ints as int8x4 hi / lo words (q = 128 hi
+            // + lo, both within int8) for the table's dp4a, and computes the chunks' coset products <c, q_t>.
             if (warp < nsg) {
-                const float *icp = C.ic + 256 * (pb + warp) + 8 * lane;
-                const float4 i0 = __ldg(reinterpret_cast<const float4 *>(icp)), i1 = __ldg(reinterpret_cast<const float4 *>(icp + 4));
+                const float *icp = ic_s + 256 * warp + 8 * lane;
                 const float *xp = xs + 256 * warp + 8 * lane;
-                float v[8] = {__fmul_rn(xp[0], i0.x), __fmul_rn(xp[1], i0.y), __fmul_rn(xp[2], i0.z), __fmul_rn(xp[3], i0.w),
-                              __fmul_rn(xp[4], i1.x), __fmul_rn(xp[5], i1.y), __fmul_rn(xp[6], i1.z), __fmul_rn(xp[7], i1.w)};
+                float v[8];
+#pragma unroll
+                for (int m = 0; m < 8; ++m) v[m] = __fmul_rn(xp[m], icp[m]);
                 fwht256_warp(v, lane);
                 float am = 0.f;
 #pragma unroll
@@ -375,48 +653,40 @@ __global__ void __launch_bounds__(kChainThreads, 1) k_chain(const __grid_constan
 #pragma unroll
                 for (int o = 1; o < 16; o <<= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
                 const float d = __fdiv_rn(am, 8191.f), id = d > 0.f ? __fdiv_rn(1.f, d) : 0.f;
+                uint32_t hl[4] = {0u, 0u, 0u, 0u};  // chunk 2l: hi, lo; chunk 2l + 1: hi, lo
+                int cx[2] = {0, 0};
 #pragma unroll
-                for (int m = 0; m < 8; ++m) q_s[256 * warp + 8 * lane + m] = __float2int_rn(__fmul_rn(v[m], id));
+                for (int m = 0; m < 8; ++m) {
+                    const int q = __float2int_rn(__fmul_rn(v[m], id));
+                    const int hi = (q + 64) >> 7, lo = q - 128 * hi;
+                    hl[2 * (m >> 2)] |= ((uint32_t)hi & 0xffu) << (8 * (m & 3));
+                    hl[2 * (m >> 2) + 1] |= ((uint32_t)lo & 0xffu) << (8 * (m & 3));
+                    cx[m >> 2] += (int)(int8_t)(C.cs >> (8 * (m & 3))) * q;
+                }
+                *reinterpret_cast<uint4 *>(g_smem + kChHL + 512 * warp + 16 * lane) = make_uint4(hl[0], hl[1], hl[2], hl[3]);
+                *reinterpret_cast<int2 *>(cx_s + 64 * warp + 2 * lane) = make_int2(cx[0], cx[1]);
                 if ((lane & 15) == 0) d_s[2 * warp + (lane >> 4)] = d;
             }
             __syncthreads();
-            if (tid < 64 * nsg) {  // <c, q_t> per chunk
-                int cx = 0;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) cx += (int)(int8_t)(C.cs >> (8 * e)) * q_s[4 * tid + e];
-                cx_s[tid] = cx;
-            }
-            __syncthreads();
+            if (tr && tid == 0 && pb == b_first) tr[2] = global_ns();
             if (tid < 256 * nsg) {  // coset nibble tables: G[hs][grp][m] = sum over set bits i of m of <c, q_(32 hs + 4 grp + i)>
                 const int sg = tid >> 8, e = tid & 255, hs = e >> 7, grp = (e >> 4) & 7, m = e & 15;
                 int gs = 0;
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
                     if ((m >> i) & 1) gs += cx_s[64 * sg + 32 * hs + 4 * grp + i];
-                reinterpret_cast<int *>(g_smem + (sg ? kSmemG1 : kSmemG0))[hs * kGInts + grp * 16 + m] = gs;
+                reinterpret_cast<int *>(g_smem + (sg ? kChG1 : kChG0))[hs * kGInts + grp * 16 + m] = gs;
             }
-            // ---- (d) the 64 KiB table of each block: T[f][hs * 32 + t] = <A[f], q_(hs, t)>, four consecutive (hs, t)
-            // per thread and 16-byte stores; q = 128 hi + lo with hi, lo in int8 range, so two dp4a per entry are exact
+            // ---- (d) the 64 KiB table of each block: T[f][hs * 32 + t] = <A[f], q_(hs, t)> = 128 dp4a(A[f], hi) +
+            // dp4a(A[f], lo), exact; four consecutive chunks per thread and 16-byte stores
             {
                 const int h4 = tid & 15, fr = tid >> 4;
                 for (int sg = 0; sg < nsg; ++sg) {
-                    int H[4], Lo[4];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const int4 qv = *reinterpret_cast<const int4 *>(q_s + 256 * sg + 4 * (4 * h4 + j));
-                        const int qq[4] = {qv.x, qv.y, qv.z, qv.w};
-                        uint32_t hp = 0, lp = 0;
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int hi = (qq[e] + 64) >> 7, lo = qq[e] - 128 * hi;
-                            hp |= ((uint32_t)hi & 0xffu) << (8 * e);
-                            lp |= ((uint32_t)lo & 0xffu) << (8 * e);
-                        }
-                        H[j] = (int)hp;
-                        Lo[j] = (int)lp;
-                    }
+                    const uint4 p0 = *reinterpret_cast<const uint4 *>(g_smem + kChHL + 512 * sg + 32 * h4);
+                    const uint4 p1 = *reinterpret_cast<const uint4 *>(g_smem + kChHL + 512 * sg + 32 * h4 + 16);
+                    const int H[4] = {(int)p0.x, (int)p0.z, (int)p1.x, (int)p1.z}, Lo[4] = {(int)p0.y, (int)p0.w, (int)p1.y, (int)p1.w};
                     int *T = reinterpret_cast<int *>(g_smem + (sg ? kSmemT1 : kSmemT0));
-#pragma unroll 2
+#pragma unroll 4
                     for (int i = 0; i < 8; ++i) {
                         const int f = fr + 32 * i;
                         const int av = (int)A_s[f];
@@ -430,62 +700,68 @@ __global__ void __launch_bounds__(kChainThreads, 1) k_chain(const __grid_constan
                 }
             }
             __syncthreads();
-            // ---- (e) units of the pair's blocks
-            while (s_ok && un < u1 && cb < pb + nsg) {
-                const int sg = cb - pb, b = cb, rr = crr;
-                const float d0 = d_s[2 * sg], d1 = d_s[2 * sg + 1];
-                const uint32_t mt = mt_n;
-                const uint16_t sc = s_n;
-                const int ro = pr_n;
-                uint32_t cur[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) cur[i] = nxt[i];
+            if (tr && tid == 0 && pb == b_first) tr[3] = global_ns();
+            // ---- (e) units of the pair's blocks, two register buffers in turn (the next unit's loads are in flight
+            // while one computes); each warp keeps pf units ahead of itself asked of L2
+            if (!fa && un < u1 && cb < pb + nsg) {
+                chain_fetch(C, pbase, R, cb, crr, lane, uA);
+                fa = true;
                 advance();
-                if (un < u1) fetch();
-                const ChainTensor &T = C.t[tensor_of_rr(rr)];
-                const int c = (int)(mt >> 29);
-                float part;
-                if (c == 3) {
-                    uint32_t w0[24], w1[24];
+            }
+            auto set_buf = [&](int buf) {  // table buffer of the unit's block into pq byte 2
+                if (buf != cur_buf) {
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        w0[2 * i] = cur[2 * i]; w0[2 * i + 1] = cur[2 * i + 1];
-                        w1[2 * i] = cur[8 + 2 * i]; w1[2 * i + 1] = cur[8 + 2 * i + 1];
-                    }
-#pragma unroll
-                    for (int i = 8; i < 24; ++i) { w0[i] = 0; w1[i] = 0; }
-                    part = sg ? tile_row_dot_w<3, 1>(w0, w1, po, lane, d0, d1) : tile_row_dot_w<3, 0>(w0, w1, po, lane, d0, d1);
-                } else {
-                    const uint32_t *p0 = T.D + (mt & 0x1FFFFFFFu);
-                    part = sg ? tile_row_other<1>(c, p0, po, lane, d0, d1) : tile_row_other<0>(c, p0, po, lane, d0, d1);
+                    for (int j = 0; j < 16; ++j) pq[j] = (pq[j] & 0x0000FFFFu) | ((uint32_t)buf << 16);
+                    cur_buf = buf;
                 }
-                float *pt = reinterpret_cast<float *>(a.ws + a.part[cp_] + T.part_off);
-                pt[(size_t)b * T.rows + ro] = __fmul_rn(part, h2f(sc));
+            };
+            while (s_ok) {
+                if (!fa || uA.b >= pb + nsg) break;
+                fb = un < u1 && cb < pb + nsg;
+                if (fb) {
+                    chain_fetch(C, pbase, R, cb, crr, lane, uB);
+                    advance();
+                }
+                pf_step();
+                set_buf(uA.b - pb);
+                chain_do_unit(uA, pq, lane, uA.b - pb, d_s);
+                fa = false;
+                if (!fb) break;
+                fa = un < u1 && cb < pb + nsg;
+                if (fa) {
+                    chain_fetch(C, pbase, R, cb, crr, lane, uA);
+                    advance();
+                }
+                pf_step();
+                set_buf(uB.b - pb);
+                chain_do_unit(uB, pq, lane, uB.b - pb, d_s);
+                fb = false;
+                if (!fa) break;
             }
             __syncthreads();
         }
-        // ---- ask L2 for the payload of this CTA's first units of the next step (weights: no dependency)
-        if (warp == 0 && s + 1 < a.nsteps && a.pf > 0) {
-            const ChainStep *N = a.steps + s + 1;
-            const long long nu = __ldg(&N->units);
-            const long long v0 = nu * blockIdx.x / gridDim.x, v1 = nu * (blockIdx.x + 1) / gridDim.x;
-            const int ng2 = __ldg(&N->ng_total), nb2 = __ldg(&N->nb), nt2 = __ldg(&N->nt);
-            for (long long u = v0 + lane; u < v1 && u < v0 + a.pf; u += 32) {
-                const int b = (int)(u / ng2), rr = (int)(u - (long long)b * ng2);
-                int ti = 0;
-                for (int i = 1; i < nt2; ++i)
-                    if (rr >= __ldg(&N->t[i].g0)) ti = i;
-                const ChainTensor *T = N->t + ti;  // plan memory: written once at creation, read with plain loads
-                const uint32_t tile = (uint32_t)(rr - T->g0) * (uint32_t)nb2 + (uint32_t)b;
-                const int uc = T->ucls;
-                const uint32_t mt = uc ? ((tile * (uint32_t)(64 * NW(uc))) | ((uint32_t)uc << 29)) : __ldg(T->M + tile);
-                const int c = (int)(mt >> 29);
-                if (c) bulk_prefetch_l2(T->D + (mt & 0x1FFFFFFFu), (uint32_t)(256 * NW(c)));
-            }
+        if (tr && tid == 0) tr[4] = global_ns();
+        // ---- the next steps, while this CTA waits at the barrier. Step s + 2's descriptor goes to the slot of step
+        // s - 1, which nothing reads any more; step s + 1's (copied during step s - 1) is here: ask L2 for every
+        // warp's first units and copy the step's constants for this CTA's blocks into shared memory
+        if (s + 2 < a.nsteps) {
+            chain_load_step(a, s + 2);
+            chain_load_range(a, s + 2, a.cuts + (size_t)(s + 2) * gridDim.x);
+        }
+        if (s + 1 < a.nsteps) {
+            const ChainStep &N = *chain_slot(s + 1);
+            const ChainRange rn = chain_range(N);
+            if (lane == 1)  // lane 1: thread 0 keeps no prefetch in flight when it fences at the barrier
+                for (int j = 0; j < a.pf; ++j)
+                    if (rn.u0 + warp + kChainWarps * j < rn.u1) chain_prefetch_unit(N, rn.u0 + warp + kChainWarps * j);
+            if (rn.b_last >= rn.b_first) chain_stage_consts(N, rn.b_first, rn.b_last - rn.b_first + 1 < 2 ? 1 : 2);
+            cp_async_commit();
         }
         chain_barrier(a.sync, (unsigned int)(s + 1) * gridDim.x, &s_ok);
+        if (tr && tid == 0) tr[5] = global_ns();
     }
     // ---- exit: the last CTA out resets the barrier words for the next launch (every CTA has passed every barrier)
+    cp_async_wait_all();
     __syncthreads();
     if (tid == 0) {
         __threadfence();
@@ -503,7 +779,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) k_chain(const __grid_constan
 
 struct p8_chain {
     uint32_t magic;
-    int device, nsteps;
+    int device, nsteps, ctas;
+    uint2 *d_cuts;              // [nsteps][ctas] unit ranges
+    unsigned long long *trace;  // optional phase trace buffer (device), set by p8_chain_trace
     p8::ChainStep *d_steps;
     unsigned int *d_sync;
     unsigned long long part[2], xv[2], ss[2];
@@ -513,6 +791,34 @@ struct p8_chain {
 namespace p8 {
 
 constexpr uint32_t kChainMagic = 0x50384348u;
+
+// Contiguous ranges of a step's block-major unit list for G CTAs that minimise the largest per-CTA cost: a unit counts
+// 1 and each 256-column block a CTA touches counts tc more (the table it builds and the block's input it reduces).
+// Binary search on the cost bound with greedy packing; every CTA of the result holds a contiguous, possibly empty range.
+static void chain_partition(unsigned units, unsigned ngt, int G, unsigned tc, uint2 *out) {
+    auto pack = [&](unsigned cap, uint2 *o) -> bool {
+        unsigned a = 0;
+        for (int c = 0; c < G; ++c) {
+            unsigned e = a, cost = 0;
+            while (e < units && cost + tc < cap) {
+                const unsigned bend = (e / ngt + 1) * ngt;
+                const unsigned take = std::min(cap - cost - tc, bend - e);
+                e += take;
+                cost += tc + take;
+                if (e < bend) break;
+            }
+            if (o) o[c] = make_uint2(a, e);
+            a = e;
+        }
+        return a >= units;
+    };
+    unsigned lo = 1, hi = units + tc * (units / ngt + 1) + 1;  // one CTA holding everything fits hi
+    while (lo < hi) {
+        const unsigned mid = lo + (hi - lo) / 2;
+        if (pack(mid, nullptr)) hi = mid; else lo = mid + 1;
+    }
+    pack(lo, out);
+}
 
 static bool overlaps(const void *a, size_t na, const void *b, size_t nb) {
     const uintptr_t x = (uintptr_t)a, y = (uintptr_t)b;
@@ -558,11 +864,12 @@ p8_status chain_create(const p8_chain_step *st, int n, p8_chain **out) {
             T.M = t->M; T.D = t->D; T.S = t->S; T.prm = t->prm; T.cp = t->cp; T.cc = t->cc; T.cv = t->cv;
             T.Y = q.y[i]; T.res = q.res[i]; T.part_off = poff;
             T.rows = t->rows; T.ng = t->ng; T.g0 = g0; T.ucls = t->uniform_class;
+            memcpy(T.dmask, t->delta_blocks, sizeof(T.dmask));
             poff += ((size_t)t->nb * t->rows * 4 + 255) & ~(size_t)255;
             g0 += t->ng;
         }
         c.ng_total = g0;
-        c.units = (long long)g0 * c.nb;
+        c.units = (unsigned int)g0 * (unsigned int)c.nb;  // <= 4092 tiles x 255 blocks
         part_max = poff > part_max ? poff : part_max;
         k_max = (size_t)c.K > k_max ? (size_t)c.K : k_max;
         nb_max = (size_t)c.nb > nb_max ? (size_t)c.nb : nb_max;
@@ -598,21 +905,41 @@ p8_status chain_create(const p8_chain_step *st, int n, p8_chain **out) {
             }
         }
     }
+    int cur = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess || cur != dev) return P8_ERR_ARG;  // the tensors' device must be current
+    const int G = sm_count();
+    const unsigned tc = [] {  // table cost in units for the range balance (P8_CHAIN_TC; tuning knob)
+        const char *e = getenv("P8_CHAIN_TC");
+        return e ? (unsigned)atoi(e) : 10u;
+    }();
+    std::vector<uint2> cuts((size_t)n * G);
+    for (int s = 0; s < n; ++s)
+        chain_partition(hs[(size_t)s].units, (unsigned)hs[(size_t)s].ng_total, G, tc, cuts.data() + (size_t)s * G);
     p8_chain *p = new p8_chain();
     p->magic = kChainMagic;
     p->device = dev;
     p->nsteps = n;
+    p->ctas = G;
     size_t o = 0;
     for (int i = 0; i < 2; ++i) { p->part[i] = o; o += part_max; }
     for (int i = 0; i < 2; ++i) { p->xv[i] = o; o += (4 * k_max + 255) & ~(size_t)255; }
     for (int i = 0; i < 2; ++i) { p->ss[i] = o; o += (4 * nb_max + 255) & ~(size_t)255; }
     p->ws_bytes = o;
-    if (cudaMalloc((void **)&p->d_steps, sizeof(ChainStep) * (size_t)n) != cudaSuccess ||
-        cudaMalloc((void **)&p->d_sync, 256) != cudaSuccess ||
-        cudaMemcpy(p->d_steps, hs.data(), sizeof(ChainStep) * (size_t)n, cudaMemcpyHostToDevice) != cudaSuccess ||
-        cudaMemset(p->d_sync, 0, 256) != cudaSuccess) {
+    p->d_steps = nullptr;
+    p->d_sync = nullptr;
+    p->d_cuts = nullptr;
+    p->trace = nullptr;
+    bool ok = cudaMalloc((void **)&p->d_cuts, sizeof(uint2) * cuts.size()) == cudaSuccess;
+    for (int s = 0; ok && s < n; ++s) hs[(size_t)s].cuts = p->d_cuts + (size_t)s * G;
+    ok = ok && cudaMalloc((void **)&p->d_steps, sizeof(ChainStep) * (size_t)n) == cudaSuccess &&
+         cudaMalloc((void **)&p->d_sync, 256) == cudaSuccess &&
+         cudaMemcpy(p->d_cuts, cuts.data(), sizeof(uint2) * cuts.size(), cudaMemcpyHostToDevice) == cudaSuccess &&
+         cudaMemcpy(p->d_steps, hs.data(), sizeof(ChainStep) * (size_t)n, cudaMemcpyHostToDevice) == cudaSuccess &&
+         cudaMemset(p->d_sync, 0, 256) == cudaSuccess;
+    if (!ok) {
         cudaFree(p->d_steps);
         cudaFree(p->d_sync);
+        cudaFree(p->d_cuts);
         delete p;
         return P8_ERR_CUDA;
     }
@@ -624,6 +951,7 @@ p8_status chain_destroy(p8_chain *p) {
     if (!p || p->magic != kChainMagic) return P8_ERR_ARG;
     cudaFree(p->d_steps);
     cudaFree(p->d_sync);
+    cudaFree(p->d_cuts);
     p->magic = 0;
     delete p;
     return P8_OK;
@@ -631,13 +959,20 @@ p8_status chain_destroy(p8_chain *p) {
 
 size_t chain_workspace(const p8_chain *p) { return p && p->magic == kChainMagic ? p->ws_bytes : 0; }
 
+p8_status chain_trace(p8_chain *p, unsigned long long *buf, size_t words) {
+    if (!p || p->magic != kChainMagic) return P8_ERR_ARG;
+    if (buf && words < (size_t)p->nsteps * (size_t)p->ctas * 8) return P8_ERR_WORKSPACE;
+    p->trace = buf;
+    return P8_OK;
+}
+
 p8_status chain_run(const p8_chain *p, void *ws, size_t ws_bytes, cudaStream_t st, int pf) {
     if (!p || p->magic != kChainMagic) return P8_ERR_ARG;
     if (!ws || ws_bytes < p->ws_bytes || ((uintptr_t)ws & 255)) return P8_ERR_WORKSPACE;
     static std::atomic<bool> attr[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return P8_ERR_CUDA;
-    if (dev != p->device) return P8_ERR_ARG;
+    if (dev != p->device || sm_count() != p->ctas) return P8_ERR_ARG;
     if (dev < 0 || dev >= 64 || !attr[dev].load(std::memory_order_acquire)) {
         if (cudaFuncSetAttribute(k_chain, cudaFuncAttributeMaxDynamicSharedMemorySize, kChSmem) != cudaSuccess) return P8_ERR_CUDA;
         if (dev >= 0 && dev < 64) attr[dev].store(true, std::memory_order_release);
@@ -650,8 +985,10 @@ p8_status chain_run(const p8_chain *p, void *ws, size_t ws_bytes, cudaStream_t s
     for (int i = 0; i < 2; ++i) { a.part[i] = p->part[i]; a.xv[i] = p->xv[i]; a.ss[i] = p->ss[i]; }
     a.nsteps = p->nsteps;
     a.pf = pf < 0 ? 0 : pf;
+    a.trace = p->trace;
+    a.cuts = p->d_cuts;
     void *args[] = {&a};
-    return launch_pdl((const void *)k_chain, dim3((unsigned)sm_count()), dim3(kChainThreads), kChSmem, st, args) == cudaSuccess
+    return launch_pdl((const void *)k_chain, dim3((unsigned)p->ctas), dim3(kChainThreads), kChSmem, st, args) == cudaSuccess
                ? P8_OK
                : P8_ERR_CUDA;
 }

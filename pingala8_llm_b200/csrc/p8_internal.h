@@ -33,6 +33,7 @@ struct p8_tensor {
     uint32_t class_mask;      // bit c set if some tile has class c
     int uniform_class;        // c if every tile has class c and tile i's payload starts at word i * 64 NW(c), else 0
     uint64_t hist[8];
+    uint32_t delta_blocks[4]; // bit b: some clamp-delta entry lies in original rows [256 b, 256 b + 256)
     uint64_t act_hash;        // FNV-1a of (sgn/c per column, codebook, coset): tensors with equal hashes share a prepared x
     std::vector<uint32_t> A_host;
 };
@@ -101,4 +102,5 @@ p8_status chain_create(const p8_chain_step *steps, int n, p8_chain **out);
 p8_status chain_destroy(p8_chain *c);
 size_t chain_workspace(const p8_chain *c);
 p8_status chain_run(const p8_chain *c, void *ws, size_t ws_bytes, cudaStream_t st, int pf);
+p8_status chain_trace(p8_chain *c, unsigned long long *buf, size_t words);
 }  // namespace p8

@@ -4,7 +4,10 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <stdlib.h>
 
+#include <algorithm>
+#include <type_traits>
 #include <atomic>
 
 #include "p8_device.cuh"
@@ -528,9 +531,14 @@ template <int C, int TOFF, int GOFF>
 __device__ __forceinline__ int lane_slice_dot(const uint32_t (&w)[24], const uint32_t (&po)[11], int lane) {
     const uint32_t pm = zbits_fast<C>(w);
     const uint32_t H = pingala8_h(__funnelshift_l(pm, pm, lane));
+    // coset term: nibble grp of H indexes a 16-entry table of group grp; (H >> (4 grp - 2)) & 0x3C is that nibble
+    // times 4 (two ops), and grp * 64 folds into the load's offset
     int cs = 0;
 #pragma unroll
-    for (int grp = 0; grp < 8; ++grp) cs += lds_at<GOFF>(grp * 64 + (((H >> (4 * grp)) & 15u) << 2));
+    for (int grp = 0; grp < 8; ++grp) {
+        const uint32_t sh = grp == 0 ? (H << 2) : (H >> (4 * grp - 2));
+        cs += lds_at<GOFF>((sh & 0x3Cu) + grp * 64);
+    }
     int a1 = 0, a2 = 0, a3 = 0;
     StepLoop<C, TOFF, 0>::run(w, po, lane, a1, a2, a3);
     return a1 * (1 << SH1(C)) + a2 * (1 << SH2(C)) + a3 + MC(C) * cs;

@@ -288,6 +288,13 @@ class Chain:
             workspace = self._ws
         check(lib().p8_chain_run(self._h, _ptr(workspace), workspace.numel(), _stream(stream)), "p8_chain_run")
 
+    def trace(self, buf):
+        """record per-step, per-CTA phase stamps of later runs into buf (int64 CUDA, nsteps x SMs x 8; None: off)"""
+        if buf is None:
+            check(lib().p8_chain_trace(self._h, None, 0), "p8_chain_trace")
+        else:
+            check(lib().p8_chain_trace(self._h, _ptr(buf), buf.numel()), "p8_chain_trace")
+
     def close(self):
         if getattr(self, "_h", None) is not None:
             lib().p8_chain_destroy(self._h)
