@@ -298,7 +298,7 @@ def run_b200(args, rank, world, local_rank):
     # one grid barrier each). Launches split where attention sits in a real decoder layer (between q/k/v and o):
     # [q/k/v 0], [o L-1, gate/up L-1, down L-1, q/k/v L] for L = 1..31, [o 31, gate/up 31, down 31]
     chains = None
-    if world == 1 and args.decode == "chain":
+    if world == 1 and (args.decode == "chain" or not args.no_chain):
         from pingala8_llm_b200.ops import Chain
 
         def cstep(L, grp):
@@ -311,7 +311,7 @@ def run_b200(args, rank, world, local_rank):
         plan_c.append([cstep(nL - 1, g) for g in groups[1:]])
         chains = [Chain(c) for c in plan_c]
         cws = torch.empty(max(c.workspace_size() for c in chains), dtype=torch.uint8, device=dev)
-    launches_per_step = len(chains) if chains is not None else launches_ops
+    launches_per_step = len(chains) if args.decode == "chain" and chains is not None else launches_ops
 
     def step_chain(stream):
         for c in chains:
@@ -333,7 +333,8 @@ def run_b200(args, rank, world, local_rank):
                 fn(stream)
         torch.cuda.synchronize()
         graphs[name] = g
-    graph = graphs["chain"] if chains is not None else graphs["ops"]
+    graph = graphs[args.decode] if args.decode in graphs else graphs["ops"]
+    other = ("ops" if args.decode == "chain" else "chain") if len(graphs) > 1 else None
 
     def barrier():
         # the device is idle before the collective: a collective kernel that waits for other ranks must never share
@@ -379,19 +380,20 @@ def run_b200(args, rank, world, local_rank):
     barrier()
     t_e2e = e2.elapsed_time(e3) / 1e3
     # ---- the other decode path at 1 GPU (per-op calls when the headline is the chain), device-timed
-    t_ops = None
-    if chains is not None:
-        for _ in range(args.warmup):
-            graphs["ops"].replay()
+    t_other = None
+    if other is not None:
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                graphs[other].replay()
         torch.cuda.synchronize()
         eo0, eo1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         eo0.record(stream)
         with torch.cuda.stream(stream):
             for _ in range(args.steps):
-                graphs["ops"].replay()
+                graphs[other].replay()
         eo1.record(stream)
         torch.cuda.synchronize()
-        t_ops = eo0.elapsed_time(eo1) / 1e3
+        t_other = eo0.elapsed_time(eo1) / 1e3
     # ---- roofline per call type: the 32 calls of one group type (one per layer, distinct weights) captured as a
     # graph and replayed; per-call duration = replay time / 32, against the call's algorithmic bytes
     dims = dict(local)
@@ -554,6 +556,45 @@ def run_b200(args, rank, world, local_rank):
             del gp
         flop = sum(2.0 * r * k * ntok for _, r, k in shapes) * model["layers"]
         prefill = (ntok, t_pf["grouped"], flop, t_pf["separate"])
+    # ---- (1 GPU) model-level decode: a random-init model of the named architecture with every projection Pingala-8
+    # (pingala8_llm_b200.decode: fused input ops, torch SDPA attention on a static KV cache, Q8_0 embeddings and head),
+    # a seeded prompt through the batched product, then greedy tokens as graph replays; device-timed
+    model_dec = None
+    if world == 1 and not args.no_model:
+        model_dec = {}
+        from pingala8_llm_b200 import decode
+
+        for mc, T, n_new in ((decode.QWEN3_4B, 512, 128), (decode.LLAMA31_8B, 1024, 64)):
+            m = decode.Model(mc, seed=3)
+            g = torch.Generator(device=dev)
+            g.manual_seed(11)
+            prompt = torch.randint(0, mc.vocab, (T,), device=dev, generator=g)
+            m.generate(prompt[:16], 4)  # capture the step graph, warm every path
+            m.alloc(T + n_new)
+            m.capture()
+            m.kv.zero_()
+            ep0, ep1, ep2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            torch.cuda.synchronize()
+            with torch.cuda.stream(m.stream):
+                ep0.record(m.stream)
+                lg = m.prefill(prompt)
+                ep1.record(m.stream)
+                m.tok.copy_(torch.argmax(lg).view(1))
+                m.pos.fill_(T)
+                for _ in range(n_new):
+                    m.graph.replay()
+                    m.pos += 1
+                ep2.record(m.stream)
+            torch.cuda.synchronize()
+            t_pf, t_dec = ep0.elapsed_time(ep1) / 1e3, ep1.elapsed_time(ep2) / 1e3
+            pbytes = sum(algo_bytes_gemv(r, k) for _, r, k in decode.proj_shapes(mc)) * mc.layers
+            model_dec[mc.name] = {
+                "layers": mc.layers, "prompt_tokens": T, "new_tokens": n_new, "prefill_ms": round(t_pf * 1e3, 2),
+                "prefill_tok_s": round(T / t_pf, 1), "decode_tok_s": round(n_new / t_dec, 1),
+                "decode_ms_per_token": round(1e3 * t_dec / n_new, 3),
+                "pingala8_bytes_per_token": pbytes, "head_bytes_per_token": mc.vocab * mc.hidden * 2}
+            del m
+            torch.cuda.empty_cache()
     # ---- max over ranks
     gnames = list(per_group)
     times = torch.tensor([t_dev, t_e2e] + [per_group[g][0] for g in gnames], dtype=torch.float64, device=dev)
@@ -581,7 +622,7 @@ def run_b200(args, rank, world, local_rank):
     achieved = dom_bytes / dom_s / 1e9
     per_call = {g: {"us": round(per_group[g][0] * 1e6, 3), "gbs": round(per_group[g][1] / per_group[g][0] / 1e9, 1)}
                 for g in gnames}
-    if chains is not None:  # the step is nothing but chain launches: the kernel's bytes and time are the step's
+    if args.decode == "chain" and chains is not None:  # the step is nothing but chain launches: the kernel's bytes and time are the step's
         dom_s = t_dev / args.steps / len(chains)
         dom_bytes = bytes_token / len(chains)
         roof = {"kernel": f"k_chain (p8_chain_run: {len(chains)} launches per token, 4 projections per launch in layers "
@@ -615,10 +656,22 @@ def run_b200(args, rank, world, local_rank):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clk.summary(),
     }
-    if t_ops is not None:
-        line["per_op_decode"] = {"tok_s": round(args.steps / t_ops, 3), "ms_per_step": round(1e3 * t_ops / args.steps, 4),
+    if t_other is not None and other == "ops":
+        line["per_op_decode"] = {"tok_s": round(args.steps / t_other, 3), "ms_per_step": round(1e3 * t_other / args.steps, 4),
                                  "kernels": "p8_mul_mat_vec_group per group call (k_act_prep + k_gemv), 256 launches per token",
                                  "per_call_type": per_call}
+    if t_other is not None and other == "chain":
+        line["chain_decode"] = {"tok_s": round(args.steps / t_other, 3), "ms_per_step": round(1e3 * t_other / args.steps, 4),
+                                "kernels": f"k_chain (p8_chain_run): {len(chains)} launches per token, the projections between two "
+                                           "attention points in one launch with one grid barrier per projection",
+                                "hbm_gbs_step": round(bytes_token / (t_other / args.steps) / 1e9, 1)}
+    if model_dec is not None:
+        line["model_decode"] = {
+            "what": "random-init model, every projection Pingala-8 class 3 (p8_mul_mat_vec_group with fused RMSNorm / "
+                    "SwiGLU; the prompt via p8_mul_mat_group), torch SDPA attention on a static KV cache, Q8_0 "
+                    "embeddings and head (fp16 head GEMV), greedy; one decode step = one CUDA graph replay",
+            "parity": "tests/test_gpu_decode.py: logits within 5e-3 of an fp32 torch forward on the oracle's dequantised "
+                      "weights", **model_dec}
     if batched is not None:
         line["batched_decode"] = {
             "kernel": "p8_mul_mat_group per input (k_gx_max + k_gx_prep once, then k_gemm + k_splitk_reduce per projection)",
@@ -920,6 +973,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true", help="skip the batched-product (prefill) measurement")
     ap.add_argument("--no-layer", action="store_true", help="skip the fused-prologue layer measurement")
     ap.add_argument("--no-batched", action="store_true", help="skip the batched-decode (bs 8/32/64) measurement")
+    ap.add_argument("--no-chain", action="store_true", help="skip the chained-launch decode measurement")
+    ap.add_argument("--no-model", action="store_true", help="skip the model-level decode (C2 Qwen3-4B, Llama-3.1-8B)")
     ap.add_argument("--decode", default="ops", choices=["chain", "ops"],
                     help="1 GPU decode path timed as the headline: chained launches (p8_chain) or per-op group calls")
     ap.add_argument("--tp-exchange", default="fused", choices=["fused", "nccl"],
