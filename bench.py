@@ -40,6 +40,10 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 LLAMA8B = dict(name="llama3.1-8b", layers=32, hidden=4096, ffn=14336, q=4096, kv=1024)
+QWEN14B = dict(name="qwen3-14b", layers=40, hidden=5120, ffn=17408, q=5120, kv=1024)
+# a small layer whose o split at 2 ranks is not whole 256-column blocks (5 query heads = 640 columns per rank): the
+# shared-boundary-block path that Qwen3-14B takes at 8 ranks, checked at 2
+UNALIGNED2 = dict(name="10-head-2-kv (o split 640 | 640)", layers=1, hidden=1280, ffn=2560, q=1280, kv=256)
 METRIC = "decode tok/s bs1 (Llama-3.1-8B shape, 2-bit); dequant-GEMV HBM GB/s % of peak"
 
 
@@ -227,6 +231,182 @@ def run_reference(args, rank, world):
     return 0
 
 
+# ------------------------------------------------------------------------------------------------ tensor parallel
+def tp_dims(model):
+    from pingala8_llm_b200 import tp
+
+    return tp.LayerDims(hidden=model["hidden"], ffn=model["ffn"], heads=model["q"] // 128, kv_heads=model["kv"] // 128,
+                        head_dim=128)
+
+
+def tp_parity(model, world, rank, dev, comm):
+    """One layer's q and gate (column-parallel) and o and down (row-parallel) of `model`, as full slots with the same
+    bytes on every rank, sharded by tp.layer_plan with the host shard transforms and run through the TP path (the
+    row-parallel sum inside the GEMV over peer memory when comm is given, else an NCCL all-reduce), against the
+    unsharded tensor's GEMV on the same GPU. Returns (relative L2 error per tensor, the bar): 1e-5 when every
+    row-parallel split is whole 256-column blocks (the same integer sums, float order only), 1e-3 when a boundary
+    block is shared (each rank quantises its own masked half of the block, x16)."""
+    import torch
+
+    from pingala8_llm_b200 import synth, tp
+    from pingala8_llm_b200.ops import P8Tensor
+
+    plan = tp.layer_plan(tp_dims(model), world, rank)
+    shapes = {n: (r, k) for n, r, k in layer_shapes(model)}
+    errs = {}
+    aligned = True
+    for i, nm in enumerate(("q", "o", "gate", "down")):
+        rows, K = shapes[nm]
+        slot = synth.make_slot(rows, K, seed=4242 + i, nd=5)  # the same bytes on every rank
+        g = torch.Generator(device=dev)
+        g.manual_seed(77 + i)
+        x = torch.randn(K, device=dev, generator=g)
+        y_full = P8Tensor(slot, K, rows).mul_mat_vec(x)
+        e = plan[nm]
+        if e.kind == "col":
+            sh = tp.shard_for(e, slot, world, rank)
+            y = P8Tensor(sh.slot, K, sh.rows).mul_mat_vec(x) if sh.rows else torch.empty(0, device=dev)
+            ref = y_full[e.lo:e.hi]
+        else:
+            aligned = aligned and e.lo % 256 == 0 and e.hi % 256 == 0
+            rp = tp.RowParallel(slot, K, rows, world, rank, comm=comm, cols=(e.lo, e.hi))
+            y = rp(x[e.lo:e.hi].contiguous())
+            ref = y_full
+        torch.cuda.synchronize()
+        errs[nm] = float((y.double() - ref.double()).norm() / ref.double().norm()) if ref.numel() else 0.0
+    return errs, (1e-5 if aligned else 1e-3)
+
+
+def tp_model_decode(model, args, rank, world, dev, comm, stream):
+    """BASELINE config C5 on this model: every projection split over the ranks by tp.layer_plan (q/k/v/gate/up
+    column-parallel, o/down row-parallel; an o split that is not whole 256-column blocks shares its boundary block,
+    the rank's input zero-padded), each rank's shards synthesised directly (seeded random codes). bs 1: the grouped
+    GEMV chain as a CUDA graph, row-parallel sums inside the GEMV over peer memory (comm) or NCCL; bs 16: the batched
+    product, row-parallel partials summed by an NCCL all-reduce, launched eagerly. Device-timed; max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from pingala8_llm_b200 import synth, tp
+    from pingala8_llm_b200.ops import P8Tensor, group_workspace_size, mul_mat_group, mul_mat_vec_group
+
+    plan = tp.layer_plan(tp_dims(model), world, rank)
+    shapes = layer_shapes(model)
+    local = {nm: (plan[nm].shard_rows, plan[nm].shard_K) for nm, _, _ in shapes}
+    layers = []
+    for L in range(model["layers"]):
+        ts = {}
+        for i, (nm, _, _) in enumerate(shapes):
+            rows, K = local[nm]
+            perm_seed = 5000 * L + 17 * i + 31 if plan[nm].kind == "row" else None
+            ts[nm] = P8Tensor(synth.make_slot_device(rows, K, seed=5000 * L + 17 * i + 7919 * rank, device=dev, perm_seed=perm_seed), K, rows)
+        layers.append(ts)
+    h = model["hidden"]
+    eo = plan["o"]
+    off, qn, oK = eo.lo - 256 * eo.b0, plan["q"].shard_rows, eo.shard_K
+    groups = [("q", "k", "v"), ("o",), ("gate", "up"), ("down",)]
+    ws = torch.empty(max(group_workspace_size([ts[n] for n in g]) for ts in layers for g in groups), dtype=torch.uint8, device=dev)
+    buf = {nm: torch.empty(local[nm][0], device=dev) for nm, _, _ in shapes}
+    buf["x"] = torch.randn(h, device=dev)
+    oin = torch.zeros(oK, device=dev)
+
+    def o_input(q):  # the rank's q rows placed into its o shard's blocks (zero elsewhere)
+        if off == 0 and oK == qn:
+            return q
+        oin[off:off + qn].copy_(q)
+        return oin
+
+    def row(t, x, out, st):
+        if comm is not None and world > 1:
+            t.mul_mat_vec_allreduce(x, comm, out=out, workspace=ws, stream=st)
+        else:
+            t.mul_mat_vec(x, out=out, workspace=ws, stream=st)
+            if world > 1:
+                tp.reduce_partials(out)
+
+    def step1(st):
+        x = buf["x"]
+        for ts in layers:
+            mul_mat_vec_group([ts["q"], ts["k"], ts["v"]], x, outs=[buf["q"], buf["k"], buf["v"]], workspace=ws, stream=st)
+            row(ts["o"], o_input(buf["q"]), buf["o"], st)
+            mul_mat_vec_group([ts["gate"], ts["up"]], buf["o"], outs=[buf["gate"], buf["up"]], workspace=ws, stream=st)
+            row(ts["down"], buf["gate"], buf["down"], st)
+            x = buf["down"]
+
+    with torch.cuda.stream(stream):
+        step1(stream)
+    torch.cuda.synchronize()
+    g1 = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(g1, stream=stream):
+            step1(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    n1 = max(10, args.steps)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            g1.replay()
+        e0.record(stream)
+        for _ in range(n1):
+            g1.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    t1 = e0.elapsed_time(e1) / 1e3 / n1
+    del g1
+    torch.cuda.synchronize()
+    # bs 16: the batched product per projection, NCCL for the row-parallel partials, eager
+    B = 16
+    X = torch.randn(B, h, device=dev)
+    Y = {nm: torch.empty(B, local[nm][0], device=dev) for nm, _, _ in shapes}
+    Xo = torch.zeros(B, oK, device=dev)
+    bws = torch.empty(max(group_workspace_size([ts[n] for n in g], B) for ts in layers for g in groups), dtype=torch.uint8, device=dev)
+
+    def step16():
+        x = X
+        for ts in layers:
+            mul_mat_group([ts["q"], ts["k"], ts["v"]], x, outs=[Y["q"], Y["k"], Y["v"]], workspace=bws)
+            xo = Y["q"] if (off == 0 and oK == qn) else Xo
+            if xo is Xo:
+                Xo[:, off:off + qn].copy_(Y["q"])
+            ts["o"].mul_mat(xo, out=Y["o"], workspace=bws)
+            if world > 1:
+                tp.reduce_partials(Y["o"])
+            mul_mat_group([ts["gate"], ts["up"]], Y["o"], outs=[Y["gate"], Y["up"]], workspace=bws)
+            ts["down"].mul_mat(Y["gate"], out=Y["down"], workspace=bws)
+            if world > 1:
+                tp.reduce_partials(Y["down"])
+            x = Y["down"]
+
+    step16()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n16 = 3
+    e2.record()
+    for _ in range(n16):
+        step16()
+    e3.record()
+    torch.cuda.synchronize()
+    t16 = e2.elapsed_time(e3) / 1e3 / n16
+    tt = torch.tensor([t1, t16], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    t1, t16 = tt[0].item(), tt[1].item()
+    nbytes = sum(algo_bytes_gemv(r, k) for _, r, k in shapes) * model["layers"]
+    return {"model": model["name"], "layers": model["layers"], "parallelism": f"tp{world}",
+            "bs1": {"tok_s": round(1.0 / t1, 1), "ms_per_token": round(t1 * 1e3, 4),
+                    "hbm_gbs_step_all_ranks": round(nbytes / t1 / 1e9, 1),
+                    "row_parallel_sum": "inside the GEMV over peer memory" if comm is not None and world > 1 else
+                                        ("NCCL all-reduce" if world > 1 else "none (1 GPU)")},
+            "bs16": {"tok_s": round(B / t16, 1), "ms_per_step": round(t16 * 1e3, 3), "launch": "eager (host launches)",
+                     "row_parallel_sum": "NCCL all-reduce" if world > 1 else "none (1 GPU)"},
+            "o_split": {"cols": [eo.lo, eo.hi], "blocks": [eo.b0, eo.b1]},
+            "weights": "seeded random class-3 codes per rank shard; the prompt phase is not part of this number"}
+
+
 # ------------------------------------------------------------------------------------------------ GPU leg
 def run_b200(args, rank, world, local_rank):
     import torch
@@ -274,7 +454,8 @@ def run_b200(args, rank, world, local_rank):
         return {("q", "k", "v"): x, ("o",): buf["q"], ("gate", "up"): buf["o"], ("down",): buf["gate"]}
 
     # row-parallel sums: inside the GEMV (fused exchange over peer memory) or an NCCL all-reduce after it
-    comm = tp.TpComm.connect(max_rows=h, timeout_ms=5000) if world > 1 and args.tp_exchange == "fused" else None
+    comm = (tp.TpComm.connect(max_rows=max(h, QWEN14B["hidden"]), timeout_ms=5000)
+            if world > 1 and args.tp_exchange == "fused" else None)
 
     def call(ts, grp, src, stream):
         if comm is not None and reduce_after.get(grp):
@@ -394,6 +575,40 @@ def run_b200(args, rank, world, local_rank):
         eo1.record(stream)
         torch.cuda.synchronize()
         t_other = eo0.elapsed_time(eo1) / 1e3
+    # ---- (N > 1) the step time of every rank over 200 replays (min / median / max), and the tensor-parallel path
+    # against the unsharded GEMV (one layer of the headline model and of C5's Qwen3-14B; exit status 1 above the bar)
+    tp_par, spread, par_fail = None, None, False
+    if world > 1:
+        barrier()
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(201)]
+        with torch.cuda.stream(stream):
+            evs[0].record(stream)
+            for i in range(200):
+                graph.replay()
+                evs[i + 1].record(stream)
+        torch.cuda.synchronize()
+        per = [evs[i].elapsed_time(evs[i + 1]) for i in range(200)]
+        st_ = torch.tensor([min(per), statistics.median(per), max(per)], dtype=torch.float64, device=dev)
+        gathered = [torch.zeros_like(st_) for _ in range(world)]
+        barrier()
+        dist.all_gather(gathered, st_)
+        spread = [{"rank": r, "min": round(g[0].item(), 4), "median": round(g[1].item(), 4), "max": round(g[2].item(), 4)}
+                  for r, g in enumerate(gathered)]
+        tp_par = {}
+        for mdl in (LLAMA8B, QWEN14B) + ((UNALIGNED2,) if world == 2 else ()):
+            barrier()
+            errs, bar = tp_parity(mdl, world, rank, dev, comm)
+            et = torch.tensor([errs[n] for n in sorted(errs)], dtype=torch.float64, device=dev)
+            barrier()
+            dist.all_reduce(et, op=dist.ReduceOp.MAX)
+            per_t = {n: float(f"{v:.3e}") for n, v in zip(sorted(errs), et.tolist())}
+            tp_par[mdl["name"]] = {"max_rel": max(per_t.values()), "bar": bar, "per_tensor": per_t}
+            par_fail = par_fail or max(per_t.values()) > bar
+    c5 = None
+    if not args.no_c5:
+        barrier()
+        c5 = tp_model_decode(QWEN14B, args, rank, world, dev, comm, stream)
+        barrier()
     # ---- roofline per call type: the 32 calls of one group type (one per layer, distinct weights) captured as a
     # graph and replayed; per-call duration = replay time / 32, against the call's algorithmic bytes
     dims = dict(local)
@@ -614,7 +829,7 @@ def run_b200(args, rank, world, local_rank):
         per_group[g] = (times[2 + i].item(), per_group[g][1])
     bytes_token = sum(algo_bytes_gemv(r, k) for _, r, k in shapes) * model["layers"]
     if rank != 0:
-        return 0
+        return 1 if par_fail else 0
     peak, peak_kind = measured_peaks()
     # dominant call type by device time per step
     dom = max(gnames, key=lambda g: per_group[g][0])
@@ -665,6 +880,14 @@ def run_b200(args, rank, world, local_rank):
                                 "kernels": f"k_chain (p8_chain_run): {len(chains)} launches per token, the projections between two "
                                            "attention points in one launch with one grid barrier per projection",
                                 "hbm_gbs_step": round(bytes_token / (t_other / args.steps) / 1e9, 1)}
+    if tp_par is not None:
+        line["tp_parity"] = {"what": "one layer's q, gate (column-parallel) and o, down (row-parallel) sharded by the plan "
+                                     "and run through the TP path, against the unsharded GEMV on the same GPU; relative "
+                                     "L2, max over ranks", **tp_par}
+    if spread is not None:
+        line["per_rank_step_ms"] = {"steps": 200, "ranks": spread}
+    if c5 is not None:
+        line["c5_tp_decode"] = c5
     if model_dec is not None:
         line["model_decode"] = {
             "what": "random-init model, every projection Pingala-8 class 3 (p8_mul_mat_vec_group with fused RMSNorm / "
@@ -701,7 +924,7 @@ def run_b200(args, rank, world, local_rank):
                                 "sample": f"5 tokens, each all {model['layers'] * 7} projections (distinct slots, 1.80 GB), median; "
                                           f"{isa} vr-native-cpu-core.h, {cores} OpenMP threads"}
     print(json.dumps(line), flush=True)
-    return 0
+    return 1 if par_fail else 0
 
 
 # ------------------------------------------------------------------------------------------------ profiling cases
@@ -975,6 +1198,7 @@ def main():
     ap.add_argument("--no-batched", action="store_true", help="skip the batched-decode (bs 8/32/64) measurement")
     ap.add_argument("--no-chain", action="store_true", help="skip the chained-launch decode measurement")
     ap.add_argument("--no-model", action="store_true", help="skip the model-level decode (C2 Qwen3-4B, Llama-3.1-8B)")
+    ap.add_argument("--no-c5", action="store_true", help="skip the C5 Qwen3-14B tensor-parallel decode block")
     ap.add_argument("--decode", default="ops", choices=["chain", "ops"],
                     help="1 GPU decode path timed as the headline: chained launches (p8_chain) or per-op group calls")
     ap.add_argument("--tp-exchange", default="fused", choices=["fused", "nccl"],
