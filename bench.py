@@ -175,17 +175,12 @@ def measured_peaks():
 _REF_CACHE = {}
 
 
-def cpu_reference_token(model, reps, warmup, seed=0):
-    """The reference's own CPU core (oracle/_ref: vr-native-cpu-core.h with the vrc_tg glue, x16 activations) over one
-    decode token: every projection of every layer, 32 x 7 distinct class-3 slots (1.80 GB, far larger than any host
-    cache, so weights stream from DRAM as on the GPU). Slots are built with numpy (oracle/synth_np.py): this leg never
-    loads the product library. OpenMP threads = all host cores, set explicitly (torchrun exports OMP_NUM_THREADS=1).
-    Returns (median seconds per token, threads, ISA)."""
+def ref_slots(model, seed=0):
+    """The reference legs' decode token: 32 x 7 distinct class-3 slots built with numpy (oracle/synth_np.py), each
+    held by a RefOracle (the reference CPU core's view of it), and one seeded x per input width."""
     from oracle import synth_np
     from oracle.oracle import RefOracle
 
-    ncores = os.cpu_count() or 1
-    RefOracle.set_threads(ncores)
     key = (model["name"], seed)
     if key not in _REF_CACHE:
         mats = []
@@ -194,7 +189,20 @@ def cpu_reference_token(model, reps, warmup, seed=0):
                 mats.append(RefOracle(synth_np.make_slot(rows, K, seed=seed + 1000 * L + 17 * i), rows, K))
         xs = {K: np.random.default_rng(K).normal(0, 1, K).astype(np.float32) for _, _, K in layer_shapes(model)}
         _REF_CACHE[key] = (mats, xs)
-    mats, xs = _REF_CACHE[key]
+    return _REF_CACHE[key]
+
+
+def cpu_reference_token(model, reps, warmup, seed=0):
+    """The reference's own CPU core (oracle/_ref: vr-native-cpu-core.h with the vrc_tg glue, x16 activations) over one
+    decode token: every projection of every layer, 32 x 7 distinct class-3 slots (1.80 GB, far larger than any host
+    cache, so weights stream from DRAM as on the GPU). Slots are built with numpy (oracle/synth_np.py): this leg never
+    loads the product library. OpenMP threads = all host cores, set explicitly (torchrun exports OMP_NUM_THREADS=1).
+    Returns (median seconds per token, threads, ISA)."""
+    from oracle.oracle import RefOracle
+
+    ncores = os.cpu_count() or 1
+    RefOracle.set_threads(ncores)
+    mats, xs = ref_slots(model, seed)
 
     def token():
         for r in mats:
@@ -208,6 +216,99 @@ def cpu_reference_token(model, reps, warmup, seed=0):
         token()
         ts.append(time.perf_counter() - t0)
     return statistics.median(ts), RefOracle.threads(), RefOracle.isa()
+
+
+def gpu_reference_token(model, steps, warmup, seed=0):
+    """The reference's own CUDA GEMV (oracle/_ref/libp8ref_gpu.so: k_vr_qx_real + cudaMemset + k_vr<1, V, 8, 108>, cut
+    from its patch) over the same decode token as cpu_reference_token: the same 224 numpy-built slots, uploaded once,
+    one call per projection (the reference has no grouped call), captured as one CUDA graph per variant (llama.cpp
+    replays its decode graph the same way) and replayed per step, timed with CUDA events on the capture stream. V 5 is
+    the shipped instance (GGML_VRC_V=5), V 7 the code default. Per projection type: the 32 per-layer calls in a graph
+    of their own, per-call duration against the call's algorithmic bytes, as the b200 arm's roofline does.
+    Weights (1.80 GB) exceed L2, so replays stream from HBM. Slots, x and y live on cuda:0; nothing of the product
+    library is loaded."""
+    import torch
+    from oracle.oracle import RefGpu
+
+    if not torch.cuda.is_available():
+        return {"unavailable": "no CUDA device"}
+    if not RefGpu.available():
+        return {"unavailable": "oracle/_ref/libp8ref_gpu.so not built (needs the reference patch at build time)"}
+    mats, xs = ref_slots(model, seed)
+    dev = torch.device("cuda", 0)
+    RefGpu.set_tables(mats[0].slot)
+    shapes = layer_shapes(model)
+    slots = [torch.from_numpy(r.slot).to(dev) for r in mats]
+    xd = {K: torch.from_numpy(v).to(dev) for K, v in xs.items()}
+    ys = [torch.empty(r.rows, device=dev) for r in mats]
+    kmax = max(xs)
+    xq = torch.empty(kmax, dtype=torch.int8, device=dev)
+    xsc = torch.empty(kmax // 128, device=dev)
+    st = torch.cuda.Stream(dev)
+
+    def call(i, V):
+        r = mats[i]
+        RefGpu.gemv(slots[i].data_ptr(), r.slot.size, r.rows, r.K, 0, xd[r.K].data_ptr(), ys[i].data_ptr(),
+                    xq.data_ptr(), xsc.data_ptr(), V=V, RL=1, stream=st.cuda_stream)
+
+    def graph_of(idx, V):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(st):
+            for i in idx:  # one eager pass first (module load, first-launch set-up)
+                call(i, V)
+            torch.cuda.synchronize()
+            with torch.cuda.graph(g, stream=st):
+                for i in idx:
+                    call(i, V)
+        return g
+
+    def timed(g, n):
+        ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(st):
+            for _ in range(warmup):
+                g.replay()
+            torch.cuda.synchronize()
+            ea.record(st)
+            for _ in range(n):
+                g.replay()
+            eb.record(st)
+        torch.cuda.synchronize()
+        return ea.elapsed_time(eb) / 1e3 / n
+
+    out = {"kernels": "k_vr_qx_real + k_vr<1, V, 8, 108> (reference CU:3003-3018, CU:2662-2727), one call per projection",
+           "graph": True, "l2": "weights 1.80 GB > L2", "variants": {}}
+    allidx = list(range(len(mats)))
+    per_tok_bytes = sum(algo_bytes_gemv(r.rows, r.K) for r in mats)
+    peak, peak_kind = measured_peaks()
+    for V in (5, 7):
+        g = graph_of(allidx, V)
+        t = timed(g, max(3, steps))
+        del g
+        out["variants"][f"V{V}"] = {"tok_s": round(1.0 / t, 2), "ms_per_token": round(1e3 * t, 4),
+                                    "weight_gbs": round(per_tok_bytes / t / 1e9, 1)}
+        if V == 5:
+            calls = {}
+            for j, (nm, rows, K) in enumerate(shapes):
+                idx = [L * len(shapes) + j for L in range(model["layers"])]
+                gj = graph_of(idx, V)
+                tc = timed(gj, max(3, steps // 4)) / len(idx)
+                del gj
+                gbs = algo_bytes_gemv(rows, K) / tc / 1e9
+                calls[nm] = {"us_per_call": round(1e6 * tc, 2), "gbs": round(gbs, 1), "frac": round(gbs / peak, 3)}
+            out["per_call_V5"] = calls
+    # one sanity figure: the reference kernels' y against the CPU reference core on the same slot and x (int8 x' in
+    # the kernel vs x16 in the core: relative L2 near 1e-2 is expected)
+    torch.cuda.synchronize()
+    r0 = mats[0]
+    yc = r0.gemv(xs[r0.K])
+    yg = ys[0].cpu().numpy()
+    out["rel_l2_vs_cpu_core"] = float(np.linalg.norm(yg - yc) / np.linalg.norm(yc))
+    out["tok_s"] = out["variants"]["V5"]["tok_s"]
+    out["hbm_peak_gbs"] = peak
+    out["peak_kind"] = peak_kind
+    del slots
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_reference(args, rank, world):
@@ -227,6 +328,11 @@ def run_reference(args, rank, world):
                                    f"median of {max(1, args.steps)}; {isa} vr-native-cpu-core.h, {cores} OpenMP threads"},
         "e2e": {"value": round(tok_s, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_ref_gpu:
+        try:
+            line["reference_gpu"] = gpu_reference_token(model, steps=max(3, args.steps), warmup=max(1, args.warmup))
+        except Exception as e:  # reported, never fatal: the CPU line above is the reference arm's measurement
+            line["reference_gpu"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -1199,6 +1305,8 @@ def main():
     ap.add_argument("--no-chain", action="store_true", help="skip the chained-launch decode measurement")
     ap.add_argument("--no-model", action="store_true", help="skip the model-level decode (C2 Qwen3-4B, Llama-3.1-8B)")
     ap.add_argument("--no-c5", action="store_true", help="skip the C5 Qwen3-14B tensor-parallel decode block")
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="--impl reference: skip the reference's own CUDA GEMV timed on this GPU beside its CPU core")
     ap.add_argument("--decode", default="ops", choices=["chain", "ops"],
                     help="1 GPU decode path timed as the headline: chained launches (p8_chain) or per-op group calls")
     ap.add_argument("--tp-exchange", default="fused", choices=["fused", "nccl"],

@@ -1,10 +1,11 @@
-"""ctypes access to the two CPU oracles. TEST INFRASTRUCTURE ONLY.
+"""ctypes access to the two CPU oracles and the reference's GPU kernels. TEST INFRASTRUCTURE ONLY.
 
-Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import this module. The product package
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg and reference arm import this module. The product package
 (pingala8_llm_b200) never imports it and has no CPU fallback.
 
   Oracle    -- our plain-C restatement of the reference CPU path (oracle/p8_oracle.c -> oracle/libp8oracle.so)
   RefOracle -- the reference's own CPU core compiled from its patch (oracle/_ref/libp8ref_{vnni,avx2}.so)
+  RefGpu    -- the reference's own CUDA GEMV kernels compiled from its patch (oracle/_ref/libp8ref_gpu.so)
 """
 import ctypes as C
 import os
@@ -242,3 +243,57 @@ class RefOracle:
         out = np.full(kbytes, 0xA5, np.uint8)
         cls.lib().ref_vr3_expand(_ptr(f, _u8p), f.size, rows, K, _ptr(out, _u8p))
         return out
+
+
+class RefGpu:
+    """The reference's own batch-1 GEMV kernels (k_vr_qx_real + k_vr, cut from its patch) on the GPU, built by
+    oracle/build_ref.py into oracle/_ref/libp8ref_gpu.so. A comparison arm for timing and a sanity check, never the
+    product path. Arguments are raw device pointers (the caller owns the memory and the stream)."""
+
+    _lib = None
+
+    @classmethod
+    def available(cls):
+        try:
+            cls.lib()
+            return True
+        except (OSError, FileNotFoundError):
+            return False
+
+    @classmethod
+    def lib(cls):
+        if cls._lib is None:
+            path = os.path.join(HERE, "_ref", "libp8ref_gpu.so")
+            if not os.path.exists(path):
+                raise FileNotFoundError(f"{path} missing (built from the reference patch by oracle/build_ref.py)")
+            L = C.CDLL(path)
+            L.refgpu_set_tables.argtypes = [C.POINTER(C.c_uint32), C.POINTER(C.c_int8)]
+            L.refgpu_set_tables.restype = C.c_int
+            L.refgpu_gemv.argtypes = [C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p,
+                                      C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]
+            L.refgpu_gemv.restype = C.c_int
+            L.refgpu_error_string.argtypes = [C.c_int]
+            L.refgpu_error_string.restype = C.c_char_p
+            cls._lib = L
+        return cls._lib
+
+    @classmethod
+    def _check(cls, rc, what):
+        if rc:
+            raise RuntimeError(f"{what}: {cls.lib().refgpu_error_string(rc).decode()} ({rc})")
+
+    @classmethod
+    def set_tables(cls, slot):
+        """Codebook A/B, coset c (slot words 0-512) and the slot's Hadamard signs (32 + 256 bytes before its end) into
+        the kernels' symbols, as the reference's native prepare does once per model."""
+        slot = np.ascontiguousarray(slot, np.uint8)
+        hdr = np.ascontiguousarray(slot[:513 * 4].view(np.uint32))
+        signs = np.ascontiguousarray(slot[slot.size - 288 : slot.size - 32].view(np.int8))
+        cls._check(cls.lib().refgpu_set_tables(_ptr(hdr, C.POINTER(C.c_uint32)), _ptr(signs, C.POINTER(C.c_int8))),
+                   "refgpu_set_tables")
+
+    @classmethod
+    def gemv(cls, slot_ptr, nbytes, rows, K, nd, x_ptr, y_ptr, xq_ptr, xs_ptr, V=5, RL=1, stream=0):
+        """y[rows] = W x through k_vr_qx_real and k_vr<RL, V, 8, 108>, enqueued on `stream` (a cudaStream_t)."""
+        cls._check(cls.lib().refgpu_gemv(slot_ptr, nbytes, rows, K, nd, x_ptr, y_ptr, xq_ptr, xs_ptr, V, RL, stream),
+                   "refgpu_gemv")
