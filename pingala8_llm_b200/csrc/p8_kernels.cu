@@ -210,8 +210,9 @@ cudaError_t launch_get_rows(const p8_tensor *t, const int32_t *ids, int64_t n, f
 //
 // y[prm[r]] = sum_b S[b][r] * sum_hs d[hs] * ( sum_k T[f_k][hs][t_k] << SH  +  MC * sum_t h_t <c, q_t> ) + (Delta x)
 // with q = x16 activation (14-bit ints per 128-col half-slice, the reference CPU default) and the table
-// T[f][hs][t] = <A[f], q_t> (exact int32). The integer sums equal the reference's exact integer dot products, so the
-// only difference to the CPU result is float rounding in the final scale-and-sum.
+// T[f][hs][t] = <A[f], q_t> (an exact integer, |T| < 2^23, stored as a float: exact). The lane sums run in fp32 on the
+// FP32 pipe, which leaves the integer ALU to the address PRMTs; they equal the reference's exact integer dot products
+// up to fp32 rounding of the running sum (<= 2^-24 relative per add), as does the final scale-and-sum.
 //
 //   k_act_prep  grid (nb, 8), 256 thr: waits for the producer of x; x -> FWHT(x sgn/c)/16 -> q, d per 128-col
 //               half-slice; 1/8 of the
@@ -368,17 +369,19 @@ __global__ void __launch_bounds__(256) k_act_prep(PrepArgs a) {
 #pragma unroll
         for (int i = 0; i < 4; ++i)
             if ((m >> i) & 1) gsum += cx_s[hs * 32 + 4 * grp + i];
-        a.G[(2 * b + hs) * kGInts + grp * 16 + m] = gsum;
+        reinterpret_cast<float *>(a.G)[(2 * b + hs) * kGInts + grp * 16 + m] = (float)gsum;  // exact (|gsum| < 2^24)
     }
     // this CTA's 32 codebook entries x 64 (hs, t): thread = (f-quarter, hs, t), 8 entries each, coalesced stores
     const int ht = tid & 63;
     const int q0 = q_s[4 * ht], q1 = q_s[4 * ht + 1], q2 = q_s[4 * ht + 2], q3 = q_s[4 * ht + 3];
-    int *T = a.T + (size_t)b * kTabInts + (32 * fg) * 64;
+    float *T = reinterpret_cast<float *>(a.T) + (size_t)b * kTabInts + (32 * fg) * 64;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int f = (tid >> 6) + 4 * i;
         const uint32_t w = A_s[f];
-        T[f * 64 + ht] = (int)(int8_t)w * q0 + (int)(int8_t)(w >> 8) * q1 + (int)(int8_t)(w >> 16) * q2 + (int)(int8_t)(w >> 24) * q3;
+        // the exact integer <A[f], q_t> (|.| < 2^22), stored as a float: exact
+        T[f * 64 + ht] = (float)((int)(int8_t)w * q0 + (int)(int8_t)(w >> 8) * q1 + (int)(int8_t)(w >> 16) * q2 +
+                                 (int)(int8_t)(w >> 24) * q3);
     }
 }
 
@@ -473,9 +476,9 @@ struct Sel {
 
 // shared-memory int at a compile-time offset plus a register byte offset: indexing the extern __shared__ symbol
 // directly lets the compiler fold the offset into the load's immediate (no address add per lookup)
-template <int OFF>
-__device__ __forceinline__ int lds_at(uint32_t byte_off) {
-    return *reinterpret_cast<const int *>(g_smem + OFF + byte_off);
+template <int OFF, typename V = int>
+__device__ __forceinline__ V lds_at(uint32_t byte_off) {
+    return *reinterpret_cast<const V *>(g_smem + OFF + byte_off);
 }
 
 template <int C, int k>
@@ -497,18 +500,24 @@ __device__ __forceinline__ uint32_t stage_addr(const uint32_t (&w)[24], const ui
     return (f << 8) | off;
 }
 
-template <int C, int TOFF, int k>
+// V = int: exact integer tables (the chain kernel); V = float: the same integers stored as floats (k_gemv), so the
+// per-chunk accumulate runs on the FP32 pipe instead of the integer ALU that the address PRMT already occupies. Stage 1
+// alternates two accumulators (even / odd steps) to halve the dependent-add chain; the order is fixed, so the result
+// is deterministic.
+template <int C, int TOFF, int k, typename V>
 struct StepLoop {
-    static __device__ __forceinline__ void run(const uint32_t (&w)[24], const uint32_t (&po)[11], int lane, int &a1, int &a2, int &a3) {
-        a1 += lds_at<TOFF>(stage_addr<C, k>(w, po, lane, 0));
-        if (W2(C)) a2 += lds_at<TOFF>(stage_addr<C, k>(w, po, lane, 1));
-        if (W3(C)) a3 += lds_at<TOFF>(stage_addr<C, k>(w, po, lane, 2));
-        StepLoop<C, TOFF, k + 1>::run(w, po, lane, a1, a2, a3);
+    static __device__ __forceinline__ void run(const uint32_t (&w)[24], const uint32_t (&po)[11], int lane, V &a1, V &a1b, V &a2,
+                                               V &a3) {
+        if (k & 1) a1b += lds_at<TOFF, V>(stage_addr<C, k>(w, po, lane, 0));
+        else a1 += lds_at<TOFF, V>(stage_addr<C, k>(w, po, lane, 0));
+        if (W2(C)) a2 += lds_at<TOFF, V>(stage_addr<C, k>(w, po, lane, 1));
+        if (W3(C)) a3 += lds_at<TOFF, V>(stage_addr<C, k>(w, po, lane, 2));
+        StepLoop<C, TOFF, k + 1, V>::run(w, po, lane, a1, a1b, a2, a3);
     }
 };
-template <int C, int TOFF>
-struct StepLoop<C, TOFF, 32> {
-    static __device__ __forceinline__ void run(const uint32_t (&)[24], const uint32_t (&)[11], int, int &, int &, int &) {}
+template <int C, int TOFF, typename V>
+struct StepLoop<C, TOFF, 32, V> {
+    static __device__ __forceinline__ void run(const uint32_t (&)[24], const uint32_t (&)[11], int, V &, V &, V &, V &) {}
 };
 
 // z bits (stage-1 MSBs) in step order. For W1 = 8: the byte MSBs of words 2p+1 (bits 7, 15, 23, 31) and 2p (shifted to
@@ -526,31 +535,33 @@ __device__ __forceinline__ uint32_t zbits_fast(const uint32_t (&w)[24]) {
     return pm;
 }
 
-// integer total of one lane-slice; TOFF / GOFF: shared-memory byte offsets of its table and coset tables
-template <int C, int TOFF, int GOFF>
-__device__ __forceinline__ int lane_slice_dot(const uint32_t (&w)[24], const uint32_t (&po)[11], int lane) {
+// total of one lane-slice (integer tables: exact; float tables: the same integers summed in fp32, |entry| < 2^22, so each
+// add rounds by at most 2^-24 of the running sum); TOFF / GOFF: shared-memory byte offsets of its table and coset tables
+template <int C, int TOFF, int GOFF, typename V = int>
+__device__ __forceinline__ V lane_slice_dot(const uint32_t (&w)[24], const uint32_t (&po)[11], int lane) {
     const uint32_t pm = zbits_fast<C>(w);
     const uint32_t H = pingala8_h(__funnelshift_l(pm, pm, lane));
     // coset term: nibble grp of H indexes a 16-entry table of group grp; (H >> (4 grp - 2)) & 0x3C is that nibble
     // times 4 (two ops), and grp * 64 folds into the load's offset
-    int cs = 0;
+    V cs = 0;
 #pragma unroll
     for (int grp = 0; grp < 8; ++grp) {
         const uint32_t sh = grp == 0 ? (H << 2) : (H >> (4 * grp - 2));
-        cs += lds_at<GOFF>((sh & 0x3Cu) + grp * 64);
+        cs += lds_at<GOFF, V>((sh & 0x3Cu) + grp * 64);
     }
-    int a1 = 0, a2 = 0, a3 = 0;
-    StepLoop<C, TOFF, 0>::run(w, po, lane, a1, a2, a3);
-    return a1 * (1 << SH1(C)) + a2 * (1 << SH2(C)) + a3 + MC(C) * cs;
+    V a1 = 0, a1b = 0, a2 = 0, a3 = 0;
+    StepLoop<C, TOFF, 0, V>::run(w, po, lane, a1, a1b, a2, a3);
+    return (a1 + a1b) * (V)(1 << SH1(C)) + a2 * (V)(1 << SH2(C)) + a3 + (V)MC(C) * cs;
 }
 
+// k_gemv's lane-slice sums come from float tables (V = float); the result is scaled by the half-slice scales d0, d1
 template <int C, int BUF>
 __device__ __forceinline__ float tile_row_dot_w(const uint32_t (&w0)[24], const uint32_t (&w1)[24], const uint32_t (&po)[11], int lane, float d0,
                                                 float d1) {
     constexpr int T0 = BUF ? kSmemT1 : kSmemT0, G0 = BUF ? kSmemG1 : kSmemG0;
-    const int i0 = lane_slice_dot<C, T0, G0>(w0, po, lane);
-    const int i1 = lane_slice_dot<C, T0 + 128, G0 + kGInts * 4>(w1, po, lane);
-    return __fadd_rn(__fmul_rn((float)i0, d0), __fmul_rn((float)i1, d1));
+    const float i0 = lane_slice_dot<C, T0, G0, float>(w0, po, lane);
+    const float i1 = lane_slice_dot<C, T0 + 128, G0 + kGInts * 4, float>(w1, po, lane);
+    return __fadd_rn(__fmul_rn(i0, d0), __fmul_rn(i1, d1));
 }
 
 template <int C, int BUF>
@@ -558,10 +569,10 @@ __device__ __noinline__ float tile_row_dot(const uint32_t *p0, const uint32_t (&
     constexpr int T0 = BUF ? kSmemT1 : kSmemT0, G0 = BUF ? kSmemG1 : kSmemG0;
     uint32_t w[24];
     load_lane_words<C>(p0, 0, lane, w);
-    const int i0 = lane_slice_dot<C, T0, G0>(w, po, lane);
+    const float i0 = lane_slice_dot<C, T0, G0, float>(w, po, lane);
     load_lane_words<C>(p0, 1, lane, w);
-    const int i1 = lane_slice_dot<C, T0 + 128, G0 + kGInts * 4>(w, po, lane);
-    return __fadd_rn(__fmul_rn((float)i0, d0), __fmul_rn((float)i1, d1));
+    const float i1 = lane_slice_dot<C, T0 + 128, G0 + kGInts * 4, float>(w, po, lane);
+    return __fadd_rn(__fmul_rn(i0, d0), __fmul_rn(i1, d1));
 }
 
 template <int BUF>
@@ -603,8 +614,10 @@ struct WarpCursor {
 };
 
 // TPX: the row-parallel exchange in the epilogue (a separate instantiation, so the plain GEMV carries none of it)
+// 104 registers: 16 warps (53,248 registers) still leave room for one k_act_prep CTA (256 threads x <= 40) beside the
+// CTA, so the next call's prep starts while this GEMV runs
 template <bool TPX>
-__global__ void __maxnreg__(96) k_gemv(const __grid_constant__ GemvArgs a) {
+__global__ void __maxnreg__(104) k_gemv(const __grid_constant__ GemvArgs a) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     uint64_t *bar = reinterpret_cast<uint64_t *>(g_smem + kSmemBar);
     __shared__ unsigned int s_done[2];  // warps done with table buffer 0 / 1, counted over the kernel (monotonic)
