@@ -15,8 +15,8 @@
 
 namespace p8 {
 
-// device-side error word (that launch's results are invalid): bit 0 GEMV table wait, bit 1 GEMV grid barrier, bit 2 GEMM
-// pipeline wait timed out; bit 3 row-parallel exchange wait timed out, bit 4 exchange entry with a foreign tag
+// device-side error word (that launch's results are invalid): bit 2 GEMM pipeline wait timed out, bit 3 row-parallel
+// exchange wait timed out, bit 4 exchange entry with a foreign tag, bit 5 chain-kernel grid barrier (bits 0-1 unused)
 __device__ unsigned int g_p8_device_error = 0;
 
 // ================================================================================================================
@@ -214,19 +214,19 @@ cudaError_t launch_get_rows(const p8_tensor *t, const int32_t *ids, int64_t n, f
 // FP32 pipe, which leaves the integer ALU to the address PRMTs; they equal the reference's exact integer dot products
 // up to fp32 rounding of the running sum (<= 2^-24 relative per add), as does the final scale-and-sum.
 //
-//   k_act_prep  grid (nb, 8), 256 thr: waits for the producer of x; x -> FWHT(x sgn/c)/16 -> q, d per 128-col
-//               half-slice; 1/8 of the
-//               table T[b] (64 KB per 256-col block) per CTA; coset nibble tables G.
-//   k_gemv      persistent, one 512-thread CTA per SM. The work is the list of (block b, tile g) units of up to four
-//               tensors that read the same x, ordered block-major and cut into equal contiguous ranges, so a CTA
-//               touches at most a few blocks. Block tables arrive by bulk copy (TMA engine, mbarrier), double
-//               buffered; the payload words of a warp's next unit are loaded into registers while the current unit
-//               computes. Each lane owns one row: per chunk 1 PRMT (field byte + rotated chunk offset -> table byte
-//               address) + 1 LDS + 1 add. A unit stores its 32 row partials (plain coalesced stores, [b][rows]).
-//               After a grid barrier (the grid is one CTA per SM, all resident) every CTA sums an equal share of the
-//               rows over the blocks in block order, adds the clamp delta and scatters y[prm[r]] (deterministic,
-//               no float atomics).
-// Both kernels use programmatic dependent launch.
+//   k_gemv         at most one 512-thread CTA per SM. The work is the list of (block b, tile g) units of up to four
+//                  tensors that read the same x, ordered block-major and cut into contiguous CTA ranges balanced on
+//                  the host (a CTA touches one or two blocks). After the wait for the producer of x, each CTA builds
+//                  the tables of its blocks in its own shared memory: x -> input op -> FWHT(x sgn/c)/16 -> x16 ints
+//                  and scales per half-slice -> T (64 KB per block) and the coset nibble tables G. No table goes
+//                  through global memory and no second kernel sits between x and the units. The payload words of a
+//                  warp's next unit are loaded into registers while the current unit computes; each lane owns one
+//                  row: per chunk 1 PRMT (field byte + rotated chunk offset -> table byte address) + 1 LDS + 1 FADD.
+//                  A unit stores its 32 row partials (coalesced, [b][rows]).
+//   k_gemv_reduce  the rows: y[prm[r]] = sum_b part[b][r] in block order + clamp delta (deterministic, no float
+//                  atomics); the row-parallel exchange for the fused tensor-parallel call.
+// Both kernels use programmatic dependent launch: each is resident and waiting before its predecessor ends, and a
+// call is two kernel hand-offs (producer of x -> k_gemv -> k_gemv_reduce) with no grid barrier.
 // ================================================================================================================
 constexpr int kTabInts = 256 * 64;          // T ints per 256-column block: [f][hs][t]
 constexpr int kTabBytes = kTabInts * 4;      // 64 KB
@@ -234,11 +234,11 @@ constexpr int kGInts = 128;                  // per half-slice: 8 nibble groups 
 constexpr int kGemvThreads = 512;
 constexpr int kGemvWarps = kGemvThreads / 32;
 constexpr int kMaxGroup = 4;
-constexpr uint32_t kWaitPolls = 1u << 20;  // a healthy table copy lands within a few polls
-constexpr unsigned long long kGridWaitNs = 20000000ull;  // grid-barrier deadline: 20 ms
-// dynamic shared memory of k_gemv: two table buffers, two G buffers (both half-slices), two mbarriers
+constexpr int kGemvMaxCtas = 256;           // CTA ranges carried in the launch arguments
+constexpr unsigned long long kGridWaitNs = 20000000ull;  // grid-barrier deadline of the chain kernel: 20 ms
+// dynamic shared memory of k_gemv: two table buffers, two G buffers (both half-slices)
 constexpr int kSmemT0 = 0, kSmemT1 = kTabBytes, kSmemG0 = 2 * kTabBytes, kSmemG1 = kSmemG0 + 2 * kGInts * 4,
-              kSmemBar = kSmemG1 + 2 * kGInts * 4, kGemvSmem = kSmemBar + 16;
+              kGemvSmem = kSmemG1 + 2 * kGInts * 4;
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -256,30 +256,40 @@ struct GemvTensor {
     int ucls;                // uniform class (payload of tile i at word i * 64 NW), 0 if the M words must be read
 };
 
-struct PrepArgs {
+struct GemvArgs {
+    GemvTensor t[kMaxGroup];
+    int rows_total;
+    int ntensors;
+    // the group's one input: x, column scales sgn/c, codebook, coset word, input op
     const float *X;
     const float *ic;
     const uint32_t *A;
     uint32_t cs;
-    int K, nb, nsl, ntensors;
-    int *T;     // [nb][16384]
-    int *G;     // [nsl][128]
-    float *d;   // [nsl]
-    unsigned int *arrive;  // the GEMV's grid-barrier counter
-    unsigned int *epoch;   // row-parallel exchange: the call counter to advance (nullptr without an exchange)
-    // activation prologue (PRO != P8_PROLOGUE_NONE): x' from x and w (RMSNorm weight) or x2 (SwiGLU up), written to xv
-    const float *pw, *x2;
+    int K, nb, nsl, ng_total;
+    long long units;       // nb * ng_total
+    const float *pw, *x2;  // input op (k_gemv<PRO>): RMSNorm weight / SwiGLU up
     float eps;
-    float *xv;
+    float *xv;             // x' of the input op for the clamp-delta term (written by the first CTA of each block)
+    unsigned int *epoch;   // row-parallel exchange: this rank's call counter (advanced by CTA 0), else nullptr
+    int ustart[kGemvMaxCtas + 1];  // CTA c takes the units [ustart[c], ustart[c + 1]) of the block-major list
+};
+
+// the row reduction after k_gemv: y[prm[r]] = sum_b part[b][r] (block order) + clamp delta (+ row-parallel exchange)
+struct ReduceArgs {
+    GemvTensor t[kMaxGroup];
+    int rows_total, ntensors, nb;
+    const float *X;  // x, or x' of the input op: the clamp delta multiplies it
+    TpExchange tp;   // row-parallel exchange (tp.world > 1), single tensor only
 };
 
 // x'[i] = (x[i] * scale) * w[i], scale = 1 / sqrt(mean(x^2) + eps): ggml's rms_norm (sum of squares, mean by float
 // division, 1 / sqrtf) followed by the weight multiply. Every CTA sums the whole vector in the same fixed order
-// (per-thread strided float4 sums, then a shared-memory tree), so all CTAs get the same scale.
+// (per-thread strided float4 sums, then a shared-memory tree over the CTA's threads), so all CTAs get the same scale.
+template <int NT>
 __device__ __forceinline__ float rms_scale(const float *x, int K, float eps, float *red) {
     const int tid = threadIdx.x;
     float ss = 0.f;
-    for (int k = 4 * tid; k < K; k += 4 * 256) {
+    for (int k = 4 * tid; k < K; k += 4 * NT) {
         const float4 v = *reinterpret_cast<const float4 *>(x + k);
         ss = __fmaf_rn(v.x, v.x, ss);
         ss = __fmaf_rn(v.y, v.y, ss);
@@ -289,114 +299,13 @@ __device__ __forceinline__ float rms_scale(const float *x, int K, float eps, flo
     red[tid] = ss;
     __syncthreads();
 #pragma unroll
-    for (int h = 128; h > 0; h >>= 1) {
+    for (int h = NT / 2; h > 0; h >>= 1) {
         if (tid < h) red[tid] = __fadd_rn(red[tid], red[tid + h]);
         __syncthreads();
     }
     const float mean = __fdiv_rn(red[0], (float)K);
     return __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, eps)));
 }
-
-template <int PRO>
-__global__ void __launch_bounds__(256) k_act_prep(PrepArgs a) {
-    __shared__ int q_s[256];
-    __shared__ uint32_t A_s[32];
-    __shared__ int cx_s[64];
-    __shared__ float red_s[PRO == P8_PROLOGUE_RMSNORM ? 256 : 1];
-    const int b = blockIdx.x, fg = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
-    pdl_launch_dependents();
-    if (tid < 32) A_s[tid] = a.A[32 * fg + tid];
-    float4 i0 = make_float4(0.f, 0.f, 0.f, 0.f), i1 = i0;
-    if (tid < 32) {  // the column scales belong to the tensor, not to the previous kernel: loaded before the wait
-        const float *ic = a.ic + b * 256 + 8 * lane;
-        i0 = *reinterpret_cast<const float4 *>(ic);
-        i1 = *reinterpret_cast<const float4 *>(ic + 4);
-    }
-    pdl_wait();  // x and the workspace belong to the previous kernel until it completes
-    if (b == 0 && fg == 0 && tid == 0) {
-        *a.arrive = 0u;
-        if (a.epoch) *a.epoch += 1u;  // the GEMV reads it after this kernel completes
-    }
-    float scale = 1.f;
-    if (PRO == P8_PROLOGUE_RMSNORM) scale = rms_scale(a.X, a.K, a.eps, red_s);
-    if (tid < 32) {
-        const float *x = a.X + b * 256 + 8 * lane;
-        float4 x0 = *reinterpret_cast<const float4 *>(x), x1 = *reinterpret_cast<const float4 *>(x + 4);
-        if (PRO == P8_PROLOGUE_RMSNORM) {
-            const float4 w0 = *reinterpret_cast<const float4 *>(a.pw + b * 256 + 8 * lane);
-            const float4 w1 = *reinterpret_cast<const float4 *>(a.pw + b * 256 + 8 * lane + 4);
-            x0 = make_float4(__fmul_rn(__fmul_rn(x0.x, scale), w0.x), __fmul_rn(__fmul_rn(x0.y, scale), w0.y),
-                             __fmul_rn(__fmul_rn(x0.z, scale), w0.z), __fmul_rn(__fmul_rn(x0.w, scale), w0.w));
-            x1 = make_float4(__fmul_rn(__fmul_rn(x1.x, scale), w1.x), __fmul_rn(__fmul_rn(x1.y, scale), w1.y),
-                             __fmul_rn(__fmul_rn(x1.z, scale), w1.z), __fmul_rn(__fmul_rn(x1.w, scale), w1.w));
-        } else if (PRO == P8_PROLOGUE_SWIGLU) {  // silu(gate) * up = gate / (1 + exp(-gate)) * up
-            const float4 u0 = *reinterpret_cast<const float4 *>(a.x2 + b * 256 + 8 * lane);
-            const float4 u1 = *reinterpret_cast<const float4 *>(a.x2 + b * 256 + 8 * lane + 4);
-            auto sw = [](float g, float u) { return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u); };
-            x0 = make_float4(sw(x0.x, u0.x), sw(x0.y, u0.y), sw(x0.z, u0.z), sw(x0.w, u0.w));
-            x1 = make_float4(sw(x1.x, u1.x), sw(x1.y, u1.y), sw(x1.z, u1.z), sw(x1.w, u1.w));
-        }
-        if (PRO != P8_PROLOGUE_NONE && fg == 0) {  // x' for the GEMV's clamp-delta term
-            *reinterpret_cast<float4 *>(a.xv + b * 256 + 8 * lane) = x0;
-            *reinterpret_cast<float4 *>(a.xv + b * 256 + 8 * lane + 4) = x1;
-        }
-        float v[8] = {__fmul_rn(x0.x, i0.x), __fmul_rn(x0.y, i0.y), __fmul_rn(x0.z, i0.z), __fmul_rn(x0.w, i0.w),
-                      __fmul_rn(x1.x, i1.x), __fmul_rn(x1.y, i1.y), __fmul_rn(x1.z, i1.z), __fmul_rn(x1.w, i1.w)};
-        fwht256_warp(v, lane);
-        float am = 0.f;
-#pragma unroll
-        for (int m = 0; m < 8; ++m) am = fmaxf(am, fabsf(v[m]));
-#pragma unroll
-        for (int o = 1; o < 16; o <<= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));  // per 16-lane half
-        const float d = __fdiv_rn(am, 8191.f), id = d > 0.f ? __fdiv_rn(1.f, d) : 0.f;
-#pragma unroll
-        for (int m = 0; m < 8; ++m) q_s[8 * lane + m] = __float2int_rn(__fmul_rn(v[m], id));
-        if (fg == 0 && (lane & 15) == 0) a.d[2 * b + (lane >> 4)] = d;
-    }
-    __syncthreads();
-    if (fg == 0) {
-        if (tid < 64) {  // <c, q_t> for the 64 chunks of the block
-            int cx = 0;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) cx += (int)(int8_t)(a.cs >> (8 * e)) * q_s[4 * tid + e];
-            cx_s[tid] = cx;
-        }
-        __syncthreads();
-        // G[hs][grp][m] = sum over the set bits i of the nibble m of <c, q_t>, t = 4 grp + i. A 16-entry group table
-        // spans 16 banks, so the warp's lookups never conflict (equal m broadcast).
-        const int hs = tid >> 7, grp = (tid >> 4) & 7, m = tid & 15;
-        int gsum = 0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-            if ((m >> i) & 1) gsum += cx_s[hs * 32 + 4 * grp + i];
-        reinterpret_cast<float *>(a.G)[(2 * b + hs) * kGInts + grp * 16 + m] = (float)gsum;  // exact (|gsum| < 2^24)
-    }
-    // this CTA's 32 codebook entries x 64 (hs, t): thread = (f-quarter, hs, t), 8 entries each, coalesced stores
-    const int ht = tid & 63;
-    const int q0 = q_s[4 * ht], q1 = q_s[4 * ht + 1], q2 = q_s[4 * ht + 2], q3 = q_s[4 * ht + 3];
-    float *T = reinterpret_cast<float *>(a.T) + (size_t)b * kTabInts + (32 * fg) * 64;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int f = (tid >> 6) + 4 * i;
-        const uint32_t w = A_s[f];
-        // the exact integer <A[f], q_t> (|.| < 2^22), stored as a float: exact
-        T[f * 64 + ht] = (float)((int)(int8_t)w * q0 + (int)(int8_t)(w >> 8) * q1 + (int)(int8_t)(w >> 16) * q2 +
-                                 (int)(int8_t)(w >> 24) * q3);
-    }
-}
-
-struct GemvArgs {
-    GemvTensor t[kMaxGroup];
-    unsigned int *arrive;  // grid-barrier counter, zeroed by the prep kernel
-    int rows_total;
-    int ntensors;
-    const int *T, *G;
-    const float *d;
-    const float *X;
-    int nb, nsl, ng_total;
-    long long units;  // nb * ng_total
-    TpExchange tp;    // row-parallel exchange (tp.world > 1), single tensor only
-};
 
 extern __shared__ __align__(1024) uint8_t g_smem[];
 
@@ -613,32 +522,120 @@ struct WarpCursor {
     int b, rr;  // current unit (256-column block, row tile of the group); exhausted once past the CTA's range
 };
 
-// TPX: the row-parallel exchange in the epilogue (a separate instantiation, so the plain GEMV carries none of it)
-// 104 registers: 16 warps (53,248 registers) still leave room for one k_act_prep CTA (256 threads x <= 40) beside the
-// CTA, so the next call's prep starts while this GEMV runs
-template <bool TPX>
+// table-build scratch of one k_gemv CTA (static shared memory): x16 ints and coset dot products of up to two blocks,
+// the codebook, the per-half-slice scales of each table buffer, the RMSNorm reduction
+struct BuildSmem {
+    int q[2][256];
+    int cx[2][64];
+    uint32_t A[256];
+    float d[2][2];  // [buffer][half-slice]
+    float red[kGemvThreads];
+};
+
+// The activation tables of blocks bA .. bA + nbld - 1 (nbld <= 2) into table buffers 0 .. nbld - 1 of this CTA's
+// shared memory; every thread of the CTA takes part (CTA-uniform call). Per block: x' = x (after the input op) times
+// sgn/c, FWHT256 / 16, x16 quantisation per 128-column half-slice (d = amax / 8191, q = rint(x' / d): the reference CPU
+// default, vrc_prep_block16 CP:584-616), then
+//   T[f][hs][t] = <A[f], q_t> as a float (exact: |T| < 2^23), two dp4a on the split q = 128 hi + lo (hi, lo int8)
+//   G[hs][grp][m] = sum over the set bits i of nibble m of <c, q_{4 grp + i}> (coset nibble tables, exact)
+// The first CTA of a block (the one holding the block's first unit) stores x' for the clamp-delta term.
+template <int PRO>
+__device__ __forceinline__ void build_tables(const GemvArgs &a, BuildSmem &s, int bA, int nbld, float scale, long long u0,
+                                             long long u1) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (warp < nbld) {
+        const int i = warp, b = bA + i;
+        const float *x = a.X + b * 256 + 8 * lane;
+        float4 x0 = *reinterpret_cast<const float4 *>(x), x1 = *reinterpret_cast<const float4 *>(x + 4);
+        const float *icp = a.ic + b * 256 + 8 * lane;
+        const float4 i0 = *reinterpret_cast<const float4 *>(icp), i1 = *reinterpret_cast<const float4 *>(icp + 4);
+        if (PRO == P8_PROLOGUE_RMSNORM) {
+            const float4 w0 = *reinterpret_cast<const float4 *>(a.pw + b * 256 + 8 * lane);
+            const float4 w1 = *reinterpret_cast<const float4 *>(a.pw + b * 256 + 8 * lane + 4);
+            x0 = make_float4(__fmul_rn(__fmul_rn(x0.x, scale), w0.x), __fmul_rn(__fmul_rn(x0.y, scale), w0.y),
+                             __fmul_rn(__fmul_rn(x0.z, scale), w0.z), __fmul_rn(__fmul_rn(x0.w, scale), w0.w));
+            x1 = make_float4(__fmul_rn(__fmul_rn(x1.x, scale), w1.x), __fmul_rn(__fmul_rn(x1.y, scale), w1.y),
+                             __fmul_rn(__fmul_rn(x1.z, scale), w1.z), __fmul_rn(__fmul_rn(x1.w, scale), w1.w));
+        } else if (PRO == P8_PROLOGUE_SWIGLU) {  // silu(gate) * up = gate / (1 + exp(-gate)) * up
+            const float4 u0v = *reinterpret_cast<const float4 *>(a.x2 + b * 256 + 8 * lane);
+            const float4 u1v = *reinterpret_cast<const float4 *>(a.x2 + b * 256 + 8 * lane + 4);
+            auto sw = [](float g, float u) { return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u); };
+            x0 = make_float4(sw(x0.x, u0v.x), sw(x0.y, u0v.y), sw(x0.z, u0v.z), sw(x0.w, u0v.w));
+            x1 = make_float4(sw(x1.x, u1v.x), sw(x1.y, u1v.y), sw(x1.z, u1v.z), sw(x1.w, u1v.w));
+        }
+        const long long bu = (long long)b * a.ng_total;  // the block's first unit
+        if (PRO != P8_PROLOGUE_NONE && u0 <= bu && bu < u1) {
+            *reinterpret_cast<float4 *>(a.xv + b * 256 + 8 * lane) = x0;
+            *reinterpret_cast<float4 *>(a.xv + b * 256 + 8 * lane + 4) = x1;
+        }
+        float v[8] = {__fmul_rn(x0.x, i0.x), __fmul_rn(x0.y, i0.y), __fmul_rn(x0.z, i0.z), __fmul_rn(x0.w, i0.w),
+                      __fmul_rn(x1.x, i1.x), __fmul_rn(x1.y, i1.y), __fmul_rn(x1.z, i1.z), __fmul_rn(x1.w, i1.w)};
+        fwht256_warp(v, lane);
+        float am = 0.f;
+#pragma unroll
+        for (int m = 0; m < 8; ++m) am = fmaxf(am, fabsf(v[m]));
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));  // per 16-lane half
+        const float d = __fdiv_rn(am, 8191.f), id = d > 0.f ? __fdiv_rn(1.f, d) : 0.f;
+#pragma unroll
+        for (int m = 0; m < 8; ++m) s.q[i][8 * lane + m] = __float2int_rn(__fmul_rn(v[m], id));
+        if ((lane & 15) == 0) s.d[i][lane >> 4] = d;
+    }
+    __syncthreads();
+    if (tid < 64 * nbld) {  // <c, q_t> for the 64 chunks of each block
+        const int i = tid >> 6, t = tid & 63;
+        int cx = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) cx += (int)(int8_t)(a.cs >> (8 * e)) * s.q[i][4 * t + e];
+        s.cx[i][t] = cx;
+    }
+    __syncthreads();
+    if (tid < 256 * nbld) {  // a 16-entry group table spans 16 banks: the lookups never conflict (equal m broadcast)
+        const int i = tid >> 8, hs = (tid >> 7) & 1, grp = (tid >> 4) & 7, m = tid & 15;
+        int gsum = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if ((m >> k) & 1) gsum += s.cx[i][hs * 32 + 4 * grp + k];
+        reinterpret_cast<float *>(g_smem + (i ? kSmemG1 : kSmemG0))[hs * kGInts + grp * 16 + m] = (float)gsum;
+    }
+    // thread = (f mod 8, hs, t): 32 codebook entries f = tid / 64 + 8 j per block, consecutive threads consecutive t
+    const int ht = tid & 63, f0 = tid >> 6;
+    for (int i = 0; i < nbld; ++i) {
+        int hi = 0, lo = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int q = s.q[i][4 * ht + e];
+            const int h = (q + 64) >> 7;  // q = 128 h + l with h in [-64, 64], l in [-64, 63] for |q| <= 8191
+            hi |= (h & 0xFF) << (8 * e);
+            lo |= ((q - 128 * h) & 0xFF) << (8 * e);
+        }
+        float *T = reinterpret_cast<float *>(g_smem + (i ? kSmemT1 : kSmemT0));
+#pragma unroll 8
+        for (int j = 0; j < 32; ++j) {
+            const int f = f0 + 8 * j;
+            const int w = (int)s.A[f];
+            T[f * 64 + ht] = (float)(128 * __dp4a(w, hi, 0) + __dp4a(w, lo, 0));
+        }
+    }
+    __syncthreads();
+}
+
+// One CTA per SM at most (512 threads, 104 registers: 16 warps leave room for a k_gemv_reduce CTA beside it). Each
+// CTA takes the contiguous range [ustart[c], ustart[c + 1]) of the block-major unit list (host-balanced: a unit
+// counts one, every extra block touched counts the cost of building its table) and builds the tables of the blocks
+// it touches in its own shared memory, two at a time; warp w takes units u0 + w, u0 + w + 16, ... The row partials
+// go to part[b][rows]; k_gemv_reduce (the next kernel) sums them.
+template <int PRO>
 __global__ void __maxnreg__(104) k_gemv(const __grid_constant__ GemvArgs a) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    uint64_t *bar = reinterpret_cast<uint64_t *>(g_smem + kSmemBar);
-    __shared__ unsigned int s_done[2];  // warps done with table buffer 0 / 1, counted over the kernel (monotonic)
-    __shared__ int s_issued;            // tables issued so far (segments 0 .. s_issued - 1)
-    __shared__ int s_ok;
-    // contiguous, equal share of the block-major unit list; warp w takes units u0 + w, u0 + w + W, ... in order, so
-    // the warps' shares differ by at most one unit and no warp waits for another at a block boundary
-    const long long u0 = a.units * blockIdx.x / gridDim.x, u1 = a.units * (blockIdx.x + 1) / gridDim.x;
+    __shared__ BuildSmem bs;
+    const long long u0 = a.ustart[blockIdx.x], u1 = a.ustart[blockIdx.x + 1];
+    pdl_launch_dependents();
+    if (u1 <= u0) return;
     const int b_first = (int)(u0 / a.ng_total), b_last = (int)((u1 - 1) / a.ng_total);
     const int rr_first = (int)(u0 - (long long)b_first * a.ng_total);             // first unit's rr in block b_first
     const int rr_last_end = (int)(u1 - (long long)b_last * a.ng_total);           // end rr in block b_last
     const int nseg = b_last - b_first + 1;
-    pdl_launch_dependents();
-    if (tid == 0) {
-        mbar_init(bar, 1);
-        mbar_init(bar + 1, 1);
-        fence_mbar_init();
-        s_done[0] = 0u;
-        s_done[1] = 0u;
-        s_issued = 0;
-    }
     uint32_t po[11];
 #pragma unroll
     for (int q = 0; q < 11; ++q) {
@@ -648,27 +645,9 @@ __global__ void __maxnreg__(104) k_gemv(const __grid_constant__ GemvArgs a) {
             if (3 * q + i < 32) r |= (((uint32_t)(lane + 3 * q + i) & 31u) << 2) << (8 * i);
         po[q] = r;
     }
-    // ---- reduce-phase split and the combining threads' row metadata (permutation, clamp-delta range): independent
-    // of the computation, loaded now so the dependent loads are off the tail of the kernel
-    const int r0 = (int)((long long)a.rows_total * blockIdx.x / gridDim.x), r1 = (int)((long long)a.rows_total * (blockIdx.x + 1) / gridDim.x);
-    const int n_rows = r1 - r0;
-    const int R = n_rows < kGemvThreads ? n_rows : kGemvThreads;
-    int S = R > 0 ? kGemvThreads / R : 1;
-    if (S > a.nb) S = a.nb;
-    const int rl = R > 0 ? tid % R : 0, sl = R > 0 ? tid / R : S;
-    int c_ti = 0, c_ro = 0, c_e0 = 0, c_e1 = 0;
-    if (tid < R) {
-        const int rt = r0 + tid;
-#pragma unroll
-        for (int i = 1; i < kMaxGroup; ++i)
-            if (i < a.ntensors && rt >= a.t[i].row0) c_ti = i;
-        const GemvTensor &T = a.t[c_ti];
-        c_ro = T.prm[rt - T.row0];
-        c_e0 = T.cp[c_ro];
-        c_e1 = T.cp[c_ro + 1];
-    }
+    if (tid < 256) bs.A[tid] = a.A[tid];  // the codebook belongs to the tensors: loaded before the wait
     // ---- this warp's cursor (global order) and its first units' M words, payload and scale. The weights are not
-    // written by earlier kernels of the stream, so these loads are issued before the wait for the prep kernel.
+    // written by earlier kernels of the stream, so these loads are issued before the wait for the producer of x.
     auto in_range = [&](const WarpCursor &c) { return c.b < b_last || (c.b == b_last && c.rr < rr_last_end); };
     auto advance = [&](WarpCursor c) -> WarpCursor {
         c.rr += kGemvWarps;
@@ -705,127 +684,93 @@ __global__ void __maxnreg__(104) k_gemv(const __grid_constant__ GemvArgs a) {
         nc2 = advance(nc);
         if (in_range(nc2)) mt_nn = m_of(nc2);
     }
-    pdl_wait();  // tables and x come from the preceding prep kernel
-    __syncthreads();
-    auto issue_table = [&](int seg) {  // segment seg (block b_first + seg) -> buffer seg & 1
-        const int bb = b_first + seg, buf = seg & 1;
-        mbar_expect_tx(bar + buf, kTabBytes + 2 * kGInts * 4);
-        bulk_g2s(g_smem + (buf ? kSmemT1 : kSmemT0), a.T + (size_t)bb * kTabInts, kTabBytes, bar + buf);
-        bulk_g2s(g_smem + (buf ? kSmemG1 : kSmemG0), a.G + (size_t)2 * bb * kGInts, 2 * kGInts * 4, bar + buf);
-    };
-    if (tid == 0) {
-        issue_table(0);
-        if (nseg > 1) issue_table(1);
-        s_issued = nseg > 1 ? 2 : 1;
-    }
-    bool ok = true;
-    int waited = -1;    // the last segment whose table this warp has waited for
-    int signaled = 0;   // this warp is done with segments [0, signaled)
-    auto wait_table = [&](int sg) {
-        if (waited >= sg || !ok) return;
-        // warp-uniform outcome (every lane polls; a lane that gave up makes the whole warp take the error path)
-        const bool landed = __all_sync(0xffffffffu, mbar_wait_bounded(bar + (sg & 1), (uint32_t)((sg >> 1) & 1), kWaitPolls));
-        if (!landed) {
-            if (lane == 0) atomicOr(&g_p8_device_error, 1u);
-            ok = false;
-        }
-        waited = sg;
-    };
-    // Done with segments [signaled, end): a warp signals a segment only after its table arrived, so a buffer's count
-    // grows segment by segment; the warp that completes a segment's count refills its buffer with segment + 2.
-    auto signal_through = [&](int end) {
-        for (; signaled < end; ++signaled) {
-            const int sg = signaled;
-            wait_table(sg);
-            __syncwarp();
-            if (lane == 0) {
-                __threadfence_block();  // this warp's table reads are ordered before its count
-                const unsigned int old = atomicAdd(&s_done[sg & 1], 1u);
-                if (old + 1u == (unsigned int)((sg >> 1) + 1) * kGemvWarps && sg + 2 < nseg && ok) {
-                    __threadfence_block();
-                    fence_proxy_async();  // every warp's generic-proxy reads of the buffer before the bulk copy
-                    issue_table(sg + 2);
-                    atomicMax(&s_issued, sg + 3);
+    pdl_wait();  // x (and the row-parallel call counter) belong to the preceding kernel until it completes
+    if (a.epoch && blockIdx.x == 0 && tid == 0) *a.epoch += 1u;  // k_gemv_reduce reads it after this kernel completes
+    float scale = 1.f;
+    if (PRO == P8_PROLOGUE_RMSNORM) scale = rms_scale<kGemvThreads>(a.X, a.K, a.eps, bs.red);
+    // segments (blocks) two at a time: build their tables (buffers 0, 1), run the warp's units in them; a CTA spans
+    // more than two blocks only when nb > the number of CTAs
+    for (int ph = 0; 2 * ph < nseg; ++ph) {
+        if (ph > 0) __syncthreads();  // every warp is done with the previous pair of tables
+        build_tables<PRO>(a, bs, b_first + 2 * ph, nseg - 2 * ph < 2 ? nseg - 2 * ph : 2, scale, u0, u1);
+        const int seg_end = 2 * ph + 2;
+        while (in_range(nc) && nc.b - b_first < seg_end) {
+            const int seg = nc.b - b_first;
+            const int b = nc.b, rr = nc.rr;
+            const float d0 = bs.d[seg & 1][0], d1 = bs.d[seg & 1][1];
+            const uint32_t mt = mt_n;
+            const uint16_t sc = s_n;
+            uint32_t cur[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) cur[i] = nxt[i];
+            nc = nc2;
+            mt_n = mt_nn;
+            if (in_range(nc)) {
+                fetch(nc, mt_n);  // possibly in the next segment
+                nc2 = advance(nc);
+                if (in_range(nc2)) mt_nn = m_of(nc2);
+            }
+            const int ti = tensor_of(a, rr), g = rr - a.t[ti].g0;
+            const GemvTensor &T = a.t[ti];
+            const int c = (int)(mt >> 29);
+            float part;
+            if (c == 3) {
+                uint32_t w0[24], w1[24];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    w0[2 * i] = cur[2 * i]; w0[2 * i + 1] = cur[2 * i + 1];
+                    w1[2 * i] = cur[8 + 2 * i]; w1[2 * i + 1] = cur[8 + 2 * i + 1];
                 }
+#pragma unroll
+                for (int i = 8; i < 24; ++i) { w0[i] = 0; w1[i] = 0; }
+                part = (seg & 1) ? tile_row_dot_w<3, 1>(w0, w1, po, lane, d0, d1) : tile_row_dot_w<3, 0>(w0, w1, po, lane, d0, d1);
+            } else {
+                const uint32_t *p0 = T.D + (mt & 0x1FFFFFFFu);
+                part = (seg & 1) ? tile_row_other<1>(c, p0, po, lane, d0, d1) : tile_row_other<0>(c, p0, po, lane, d0, d1);
             }
-            __syncwarp();
+            const int r = g * 32 + lane;
+            T.part[(size_t)b * T.rows + r] = __fmul_rn(part, h2f(sc));
         }
-    };
-    while (ok && in_range(nc)) {
-        const int seg = nc.b - b_first;
-        signal_through(seg);
-        wait_table(seg);
-        if (!ok) break;
-        const int b = nc.b, rr = nc.rr;
-        const float d0 = a.d[2 * b], d1 = a.d[2 * b + 1];
-        const uint32_t mt = mt_n;
-        const uint16_t sc = s_n;
-        uint32_t cur[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) cur[i] = nxt[i];
-        nc = nc2;
-        mt_n = mt_nn;
-        if (in_range(nc)) {
-            fetch(nc, mt_n);  // possibly in the next segment
-            nc2 = advance(nc);
-            if (in_range(nc2)) mt_nn = m_of(nc2);
-        }
-        const int ti = tensor_of(a, rr), g = rr - a.t[ti].g0;
-        const GemvTensor &T = a.t[ti];
-        const int c = (int)(mt >> 29);
-        float part;
-        if (c == 3) {
-            uint32_t w0[24], w1[24];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                w0[2 * i] = cur[2 * i]; w0[2 * i + 1] = cur[2 * i + 1];
-                w1[2 * i] = cur[8 + 2 * i]; w1[2 * i + 1] = cur[8 + 2 * i + 1];
-            }
-#pragma unroll
-            for (int i = 8; i < 24; ++i) { w0[i] = 0; w1[i] = 0; }
-            part = (seg & 1) ? tile_row_dot_w<3, 1>(w0, w1, po, lane, d0, d1) : tile_row_dot_w<3, 0>(w0, w1, po, lane, d0, d1);
-        } else {
-            const uint32_t *p0 = T.D + (mt & 0x1FFFFFFFu);
-            part = (seg & 1) ? tile_row_other<1>(c, p0, po, lane, d0, d1) : tile_row_other<0>(c, p0, po, lane, d0, d1);
-        }
-        const int r = g * 32 + lane;
-        T.part[(size_t)b * T.rows + r] = __fmul_rn(part, h2f(sc));
     }
-    if (ok) signal_through(nseg);
-    __syncthreads();
-    if (!ok && tid == 0) {  // copies in flight must land before the CTA's shared memory is reused or goes away
-        for (int sg = s_issued - 2; sg < s_issued; ++sg)
-            if (sg >= 0) mbar_wait_bounded(bar + (sg & 1), (uint32_t)((sg >> 1) & 1), kWaitPolls);
+}
+
+// One thread per (row, block slice): a row's blocks are cut into S = ceil(nb / 16) slices of 16 (the last one
+// shorter); slice j sums blocks [16 j, 16 j + 16) of its row in block order with all its loads in flight, then one
+// thread adds the S slice sums in slice order, adds the clamp delta sum_e val_e x[col_e] and stores y[prm[r]] (with
+// the row-parallel exchange first for TPX). The summation order depends on nb alone -- not on the grid, the group or
+// the rows per CTA -- so every entry point that computes a row gets the same bits.
+constexpr int kRedThreads = 256;
+constexpr int kRedRowsPerCta = 32;
+constexpr int kRedSlice = 16;
+
+template <bool TPX>
+__global__ void __launch_bounds__(kRedThreads, 5) k_gemv_reduce(const __grid_constant__ ReduceArgs a) {
+    const int tid = threadIdx.x;
+    __shared__ float red[kRedThreads];
+    pdl_launch_dependents();
+    const int r0 = (int)((long long)a.rows_total * blockIdx.x / gridDim.x), r1 = (int)((long long)a.rows_total * (blockIdx.x + 1) / gridDim.x);
+    const int n_rows = r1 - r0;
+    const int S = (a.nb + kRedSlice - 1) / kRedSlice;  // <= 16 for K <= 65536
+    const int R = min(n_rows, kRedThreads / S);         // rows per pass
+    const int rl = R > 0 ? tid % R : 0, sl = R > 0 ? tid / R : S;
+    // the combining threads' row metadata (permutation, clamp-delta range) belongs to the tensors: loaded before the wait
+    int c_ti = 0, c_ro = 0, c_e0 = 0, c_e1 = 0;
+    if (tid < R) {
+        const int rt = r0 + tid;
+#pragma unroll
+        for (int i = 1; i < kMaxGroup; ++i)
+            if (i < a.ntensors && rt >= a.t[i].row0) c_ti = i;
+        const GemvTensor &T = a.t[c_ti];
+        c_ro = T.prm[rt - T.row0];
+        c_e0 = T.cp[c_ro];
+        c_e1 = T.cp[c_ro + 1];
     }
-    // grid barrier (all CTAs are resident: one per SM; the prep kernel zeroed the counter), then every CTA reduces an
-    // equal share of the rows: y[prm[r]] = sum_b part[b][r] (block order, deterministic) + sum_e val_e x[col_e]
-    __syncthreads();
-    if (tid == 0) {
-        unsigned int n;  // release: this CTA's partial stores are visible before its arrival is counted
-        asm volatile("atom.add.release.gpu.global.u32 %0, [%1], 1;" : "=r"(n) : "l"(a.arrive) : "memory");
-        ++n;
-        // all CTAs are resident in a healthy launch, so the wait is microseconds; the deadline ends it when another
-        // kernel holds SMs (results invalid, error bit 2) instead of spinning for seconds
-        const unsigned long long dl = global_ns() + kGridWaitNs;
-        while (n < gridDim.x) {
-            asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(n) : "l"(a.arrive) : "memory");
-            if (n < gridDim.x && global_ns() > dl) break;
-        }
-        asm volatile("fence.acq_rel.gpu;" ::: "memory");  // acquire: the other CTAs' partials are visible
-        s_ok = n >= gridDim.x;
-        if (!s_ok) atomicOr(&g_p8_device_error, 2u);
-    }
-    __syncthreads();
-    if (!s_ok) return;
-    // R rows x S block slices per pass (R * S <= threads): slice j sums blocks [nb j / S, nb (j + 1) / S) of its row
-    // in block order with all of its loads in flight, then the first R threads add the S slice sums in slice order.
-    // The split depends only on the launch shape, so the result is deterministic.
-    float *red = reinterpret_cast<float *>(g_smem + kSmemT0);  // the table buffers are free now
+    pdl_wait();  // the partials (and x' of an input op) come from k_gemv
     constexpr bool tpx = TPX;
-    const unsigned int par = tpx ? (__ldcg(a.tp.epoch) & 1u) : 0u;  // advanced by the prep kernel of this call
+    const unsigned int par = tpx ? (__ldcg(a.tp.epoch) & 1u) : 0u;  // advanced by this call's k_gemv
     const unsigned long long deadline = tpx ? global_ns() + a.tp.timeout_ns : 0ull;
     bool tp_ok = true;
-    const int b_lo = a.nb * sl / S, b_hi = a.nb * (sl + 1) / S;
+    const int b_lo = kRedSlice * sl, b_hi = min(a.nb, kRedSlice * (sl + 1));
     for (int base = r0; base < r1; base += R) {
         const int rt = base + rl;
         float s = 0.f;
@@ -837,18 +782,18 @@ __global__ void __maxnreg__(104) k_gemv(const __grid_constant__ GemvArgs a) {
             const GemvTensor &T = a.t[ti];
             const float *p = T.part + (rt - T.row0);
             int bb = b_lo;
-            for (; bb + 8 <= b_hi; bb += 8) {
-                float v[8];
+            for (; bb + 16 <= b_hi; bb += 16) {
+                float v[16];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) v[j] = __ldcg(p + (size_t)(bb + j) * T.rows);
+                for (int j = 0; j < 16; ++j) v[j] = __ldcg(p + (size_t)(bb + j) * T.rows);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) s = __fadd_rn(s, v[j]);
+                for (int j = 0; j < 16; ++j) s = __fadd_rn(s, v[j]);
             }
-            float v[8];
+            float v[16];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = bb + j < b_hi ? __ldcg(p + (size_t)(bb + j) * T.rows) : 0.f;
+            for (int j = 0; j < 16; ++j) v[j] = bb + j < b_hi ? __ldcg(p + (size_t)(bb + j) * T.rows) : 0.f;
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
+            for (int j = 0; j < 16; ++j)
                 if (bb + j < b_hi) s = __fadd_rn(s, v[j]);
         }
         if (sl < S) red[sl * R + rl] = s;
@@ -876,9 +821,9 @@ __global__ void __maxnreg__(104) k_gemv(const __grid_constant__ GemvArgs a) {
     }
 }
 
-// workspace layout (bytes, each part 256-aligned): T | G | d | partials ([nb][rows] per tensor)
+// workspace layout (bytes, each part 256-aligned): x' of an input op | partials ([nb][rows] per tensor)
 struct GemvWs {
-    size_t T, G, d, arrive, xv, part, total;
+    size_t xv, part, total;
 };
 static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
 static GemvWs gemv_ws_layout(const p8_tensor *const *ts, int nt) {
@@ -886,11 +831,7 @@ static GemvWs gemv_ws_layout(const p8_tensor *const *ts, int nt) {
     size_t part = 0;
     for (int i = 0; i < nt; ++i) part += al256((size_t)ts[i]->nb * ts[i]->rows * 4);
     GemvWs w;
-    w.T = 0;
-    w.G = w.T + al256((size_t)t->nb * kTabBytes);
-    w.d = w.G + al256((size_t)t->nsl * kGInts * 4);
-    w.arrive = w.d + al256((size_t)t->nsl * 4);
-    w.xv = w.arrive + 256;
+    w.xv = 0;
     w.part = w.xv + al256((size_t)t->K * 4);
     w.total = w.part + part;
     return w;
@@ -924,14 +865,51 @@ static int sm_count() {
     if (!v) {
         cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
         if (v <= 0) v = 148;
-        cudaFuncSetAttribute(k_gemv<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
-        cudaFuncSetAttribute(k_gemv<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
+        cudaFuncSetAttribute(k_gemv<P8_PROLOGUE_NONE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
+        cudaFuncSetAttribute(k_gemv<P8_PROLOGUE_RMSNORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
+        cudaFuncSetAttribute(k_gemv<P8_PROLOGUE_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
         n[dev].store(v, std::memory_order_release);
     }
     return v;
 }
 
-// one column: prep + persistent GEMV over the group
+// Cut the block-major list of `units` units (ng per block) into at most P contiguous CTA ranges that minimise the
+// largest CTA cost, cost = units taken + kTableCost per block touched (a table build costs about that many units of
+// work). Greedy filling under a bound, binary search on the bound. Returns the CTAs used; ustart[0 .. used] is filled.
+constexpr int kTableCost = 5;
+static int partition_units(long long units, long long ng, int P, int *ustart) {
+    auto fill = [&](long long C, int *out) -> int {  // CTAs needed under bound C (P + 1 if more than P)
+        long long s = 0;
+        int c = 0;
+        if (out) out[0] = 0;
+        while (s < units) {
+            if (c == P) return P + 1;
+            long long e = s, cost = 0;
+            while (e < units) {
+                const long long blk_end = std::min(units, (e / ng + 1) * ng);
+                if (cost + kTableCost + 1 > C) break;
+                const long long take = std::min(blk_end - e, C - cost - kTableCost);
+                e += take;
+                cost += kTableCost + take;
+                if (e < blk_end) break;
+            }
+            if (e == s) return P + 1;
+            s = e;
+            ++c;
+            if (out) out[c] = (int)s;
+        }
+        return c;
+    };
+    long long lo = (units + P - 1) / P + kTableCost, hi = units + kTableCost * (units / ng + 2);
+    while (lo < hi) {
+        const long long mid = (lo + hi) / 2;
+        if (fill(mid, nullptr) <= P) hi = mid;
+        else lo = mid + 1;
+    }
+    return fill(lo, ustart);
+}
+
+// one column: k_gemv (tables, units, partials) + k_gemv_reduce (rows), both with programmatic dependent launch
 static p8_status launch_gemv_col(const p8_tensor *const *ts, int nt, const float *x, float *const *Ys, void *ws, size_t ws_bytes,
                                  cudaStream_t st, const TpExchange *tp = nullptr, unsigned int *epoch = nullptr,
                                  const p8_prologue *pro = nullptr) {
@@ -940,27 +918,26 @@ static p8_status launch_gemv_col(const p8_tensor *const *ts, int nt, const float
     if (!ws || ws_bytes < L.total) return P8_ERR_WORKSPACE;
     uint8_t *w = static_cast<uint8_t *>(ws);
     const int nsm = sm_count();
-    PrepArgs pa;
-    memset(&pa, 0, sizeof(pa));
-    pa.X = x; pa.ic = t0->ic; pa.A = t0->A; pa.cs = t0->cs; pa.K = t0->K; pa.nb = t0->nb; pa.nsl = t0->nsl; pa.ntensors = nt;
-    pa.T = reinterpret_cast<int *>(w + L.T);
-    pa.G = reinterpret_cast<int *>(w + L.G);
-    pa.d = reinterpret_cast<float *>(w + L.d);
-    pa.arrive = reinterpret_cast<unsigned int *>(w + L.arrive);
-    pa.epoch = tp ? epoch : nullptr;
     const int pk = pro ? pro->kind : P8_PROLOGUE_NONE;
-    if (pk != P8_PROLOGUE_NONE) {
-        pa.pw = pro->w;
-        pa.x2 = pro->x2;
-        pa.eps = pro->eps;
-        pa.xv = reinterpret_cast<float *>(w + L.xv);
-    }
     GemvArgs ga;
     memset(&ga, 0, sizeof(ga));
-    if (tp) ga.tp = *tp;
-    ga.ntensors = nt; ga.T = pa.T; ga.G = pa.G; ga.d = pa.d; ga.X = pk != P8_PROLOGUE_NONE ? pa.xv : x; ga.nb = t0->nb;
+    ReduceArgs ra;
+    memset(&ra, 0, sizeof(ra));
+    ga.ntensors = nt;
+    ga.X = x;
+    ga.ic = t0->ic;
+    ga.A = t0->A;
+    ga.cs = t0->cs;
+    ga.K = t0->K;
+    ga.nb = t0->nb;
     ga.nsl = t0->nsl;
-    ga.arrive = pa.arrive;
+    if (pk != P8_PROLOGUE_NONE) {
+        ga.pw = pro->w;
+        ga.x2 = pro->x2;
+        ga.eps = pro->eps;
+        ga.xv = reinterpret_cast<float *>(w + L.xv);
+    }
+    ga.epoch = tp ? epoch : nullptr;
     size_t poff = L.part;
     int g0 = 0;
     for (int i = 0; i < nt; ++i) {
@@ -973,20 +950,31 @@ static p8_status launch_gemv_col(const p8_tensor *const *ts, int nt, const float
         g.rows = t->rows; g.ng = t->ng; g.g0 = g0; g.row0 = ga.rows_total; g.ucls = t->uniform_class;
         g0 += t->ng;
         ga.rows_total += t->rows;
+        ra.t[i] = g;
     }
     ga.ng_total = g0;
     ga.units = (long long)g0 * t0->nb;
+    const int P = (int)std::min<long long>(ga.units, std::min(nsm, kGemvMaxCtas));
+    const int grid = partition_units(ga.units, g0, P, ga.ustart);
+    if (grid < 1 || grid > P) return P8_ERR_ARG;
     {
-        void *args[] = {&pa};
-        const void *fn = pk == P8_PROLOGUE_RMSNORM ? (const void *)k_act_prep<P8_PROLOGUE_RMSNORM>
-                         : pk == P8_PROLOGUE_SWIGLU  ? (const void *)k_act_prep<P8_PROLOGUE_SWIGLU>
-                                                     : (const void *)k_act_prep<P8_PROLOGUE_NONE>;
-        if (launch_pdl(fn, dim3(t0->nb, 8), dim3(256), 0, st, args) != cudaSuccess) return P8_ERR_CUDA;
+        void *args[] = {&ga};
+        const void *fn = pk == P8_PROLOGUE_RMSNORM ? (const void *)k_gemv<P8_PROLOGUE_RMSNORM>
+                         : pk == P8_PROLOGUE_SWIGLU  ? (const void *)k_gemv<P8_PROLOGUE_SWIGLU>
+                                                     : (const void *)k_gemv<P8_PROLOGUE_NONE>;
+        if (launch_pdl(fn, dim3(grid), dim3(kGemvThreads), kGemvSmem, st, args) != cudaSuccess) return P8_ERR_CUDA;
     }
-    const unsigned grid = (unsigned)(ga.units < nsm ? ga.units : nsm);
-    void *args[] = {&ga};
-    const void *fn = tp ? (const void *)k_gemv<true> : (const void *)k_gemv<false>;
-    if (launch_pdl(fn, dim3(grid), dim3(kGemvThreads), kGemvSmem, st, args) != cudaSuccess) return P8_ERR_CUDA;
+    ra.rows_total = ga.rows_total;
+    ra.ntensors = nt;
+    ra.nb = t0->nb;
+    ra.X = pk != P8_PROLOGUE_NONE ? ga.xv : x;
+    if (tp) ra.tp = *tp;
+    // at most one CTA per SM: each one beside a k_gemv CTA (256 threads, <= 48 registers fit next to its 16 warps),
+    // resident and waiting before k_gemv ends
+    const int rgrid = std::max(1, std::min((ra.rows_total + kRedRowsPerCta - 1) / kRedRowsPerCta, nsm));
+    void *args[] = {&ra};
+    const void *fn = tp ? (const void *)k_gemv_reduce<true> : (const void *)k_gemv_reduce<false>;
+    if (launch_pdl(fn, dim3(rgrid), dim3(kRedThreads), 0, st, args) != cudaSuccess) return P8_ERR_CUDA;
     return P8_OK;
 }
 
@@ -997,7 +985,7 @@ p8_status launch_gemv_group(const p8_tensor *const *ts, int nt, const float *X, 
     for (int i = 0; i < nt; ++i)  // tensors of one launch share x and its table: same K, column scales, signs and codebook
         if (ts[i]->K != t0->K || ts[i]->act_hash != t0->act_hash) return P8_ERR_ARG;
     (void)sm_count();
-    // columns run one after another (the per-tile counters are per tensor); ncols > 1 is the batched fallback
+    // columns run one after another; ncols > 1 is the batched fallback
     for (int64_t n = 0; n < ncols; ++n) {
         float *Yn[kMaxGroup];
         for (int i = 0; i < nt; ++i) Yn[i] = Ys[i] + n * ldys[i];

@@ -3,20 +3,20 @@
 // For callers that cannot allocate device memory when they run the op and have no scratch buffer to lend it: for
 // example a host application that plans every device allocation up front and gives this op only its weight, input and
 // output buffers, or a code path that must not call cudaMalloc (which can synchronise the device and can fail under
-// memory pressure). The scratch the GEMV needs (activation tables, coset tables, scales, the grid-barrier counter and
-// the row partials) lives in one fixed device array of this file instead of a caller workspace.
+// memory pressure). The scratch the GEMV needs (the row partials per 256-column block, and x' of an input op) lives
+// in one fixed device array of this file instead of a caller workspace.
 //
 // The array is kNoAllocScratchBytes (6 MiB). It is placed on a device when this file's device module is loaded there,
 // and with CUDA's default lazy module loading that happens inside the first p8_mul_mat_vec_noalloc call on that
 // device: that first call makes the 6 MiB device allocation (the driver's, not this library's) and can fail like one
 // (P8_ERR_NOALLOC_SCRATCH), and it must not run inside a stream capture. Make one call on every device during set-up,
 // outside any capture; from then on every GPU that loaded the array holds it until the process exits.
-// A tensor whose GEMV needs more scratch than that (p8_workspace_size(t, 1) > 6 MiB, e.g. K > 16384 or very many rows
-// per 256-column block) is rejected with P8_ERR_WORKSPACE.
+// A tensor whose GEMV needs more scratch than that (p8_workspace_size(t, 1) > 6 MiB: 4 bytes per row and 256-column
+// block plus 4 bytes per column, e.g. more than 1.5 M rows x blocks) is rejected with P8_ERR_WORKSPACE.
 //
-// All calls share the array and it keeps the previous call's contents: the kernels rewrite every table and partial
-// they read and clear the barrier counter at the start of each call, so no state leaks between calls. Calls that can
-// overlap on the GPU (other streams, other host threads) race on the array and must be serialised by the caller.
+// All calls share the array and it keeps the previous call's contents: every partial a call reads is written by the
+// same call first, so no state leaks between calls and nothing needs clearing. Calls that can overlap on the GPU
+// (other streams, other host threads) race on the array and must be serialised by the caller.
 #include <cuda_runtime.h>
 
 #include "p8_internal.h"

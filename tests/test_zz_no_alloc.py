@@ -46,8 +46,8 @@ def test_noalloc_matches_workspace_entry_point_two_calls_in_a_row(rows, K):
 
 
 def test_noalloc_rejects_tensors_beyond_its_scratch():
-    rows, K = 32, 32768  # 128 blocks of 64 KiB activation tables: 8 MiB > the 6 MiB array
-    t = P8Tensor(synth.make_slot(rows, K, seed=5), K, rows)
+    rows, K = 32736, 12544  # row partials per 256-column block: 49 blocks x 32736 rows x 4 B = 6.4 MB > the 6 MiB array
+    t = P8Tensor(synth.make_slot_device(rows, K, seed=5), K, rows)
     assert t.workspace_size(1) > p8.lib().p8_noalloc_scratch_bytes()
     with pytest.raises(p8.P8Error) as e:
         noalloc(t, torch.randn(K, device="cuda"))
