@@ -525,10 +525,10 @@ struct WarpCursor {
 // table-build scratch of one k_gemv CTA (static shared memory): x16 ints and coset dot products of up to two blocks,
 // the codebook, the per-half-slice scales of each table buffer, the RMSNorm reduction
 struct BuildSmem {
+    float4 Af[256];  // the codebook as floats (entry f: its four int8 values)
     int q[2][256];
     int cx[2][64];
-    uint32_t A[256];
-    float d[2][2];  // [buffer][half-slice]
+    float d[2][2];   // [buffer][half-slice]
     float red[kGemvThreads];
 };
 
@@ -536,7 +536,7 @@ struct BuildSmem {
 // shared memory; every thread of the CTA takes part (CTA-uniform call). Per block: x' = x (after the input op) times
 // sgn/c, FWHT256 / 16, x16 quantisation per 128-column half-slice (d = amax / 8191, q = rint(x' / d): the reference CPU
 // default, vrc_prep_block16 CP:584-616), then
-//   T[f][hs][t] = <A[f], q_t> as a float (exact: |T| < 2^23), two dp4a on the split q = 128 hi + lo (hi, lo int8)
+//   T[f][hs][t] = <A[f], q_t> as a float (exact: |T| < 2^23), four fp32 FMAs on the float codebook copy
 //   G[hs][grp][m] = sum over the set bits i of nibble m of <c, q_{4 grp + i}> (coset nibble tables, exact)
 // The first CTA of a block (the one holding the block's first unit) stores x' for the clamp-delta term.
 template <int PRO>
@@ -598,23 +598,18 @@ __device__ __forceinline__ void build_tables(const GemvArgs &a, BuildSmem &s, in
             if ((m >> k) & 1) gsum += s.cx[i][hs * 32 + 4 * grp + k];
         reinterpret_cast<float *>(g_smem + (i ? kSmemG1 : kSmemG0))[hs * kGInts + grp * 16 + m] = (float)gsum;
     }
-    // thread = (f mod 8, hs, t): 32 codebook entries f = tid / 64 + 8 j per block, consecutive threads consecutive t
+    // thread = (f mod 8, hs, t): 32 codebook entries f = tid / 64 + 8 j per block, consecutive threads consecutive t.
+    // fp32 FMAs on integer values: every product (< 2^20) and partial sum (< 2^23) is exact, so T is the exact integer
     const int ht = tid & 63, f0 = tid >> 6;
     for (int i = 0; i < nbld; ++i) {
-        int hi = 0, lo = 0;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int q = s.q[i][4 * ht + e];
-            const int h = (q + 64) >> 7;  // q = 128 h + l with h in [-64, 64], l in [-64, 63] for |q| <= 8191
-            hi |= (h & 0xFF) << (8 * e);
-            lo |= ((q - 128 * h) & 0xFF) << (8 * e);
-        }
+        const float q0 = (float)s.q[i][4 * ht], q1 = (float)s.q[i][4 * ht + 1], q2 = (float)s.q[i][4 * ht + 2],
+                    q3 = (float)s.q[i][4 * ht + 3];
         float *T = reinterpret_cast<float *>(g_smem + (i ? kSmemT1 : kSmemT0));
 #pragma unroll 8
         for (int j = 0; j < 32; ++j) {
             const int f = f0 + 8 * j;
-            const int w = (int)s.A[f];
-            T[f * 64 + ht] = (float)(128 * __dp4a(w, hi, 0) + __dp4a(w, lo, 0));
+            const float4 w = s.Af[f];
+            T[f * 64 + ht] = __fmaf_rn(w.x, q0, __fmaf_rn(w.y, q1, __fmaf_rn(w.z, q2, __fmul_rn(w.w, q3))));
         }
     }
     __syncthreads();
@@ -645,7 +640,10 @@ __global__ void __maxnreg__(104) k_gemv(const __grid_constant__ GemvArgs a) {
             if (3 * q + i < 32) r |= (((uint32_t)(lane + 3 * q + i) & 31u) << 2) << (8 * i);
         po[q] = r;
     }
-    if (tid < 256) bs.A[tid] = a.A[tid];  // the codebook belongs to the tensors: loaded before the wait
+    if (tid < 256) {  // the codebook belongs to the tensors: converted before the wait
+        const uint32_t w = __ldg(a.A + tid);
+        bs.Af[tid] = make_float4((float)(int8_t)w, (float)(int8_t)(w >> 8), (float)(int8_t)(w >> 16), (float)(int8_t)(w >> 24));
+    }
     // ---- this warp's cursor (global order) and its first units' M words, payload and scale. The weights are not
     // written by earlier kernels of the stream, so these loads are issued before the wait for the producer of x.
     auto in_range = [&](const WarpCursor &c) { return c.b < b_last || (c.b == b_last && c.rr < rr_last_end); };
