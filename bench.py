@@ -11,7 +11,7 @@ CUDA graph and replayed per step. Attention, norms and the LM head are not part 
   value     tokens/s with inputs resident in HBM (device-timed with CUDA events, max over ranks)
   e2e       the same through the public op API with a pinned-host input vector copied in and the final output copied
             out every step
-  roofline  the dominant call type (p8_mul_mat_vec_group = k_act_prep + k_gemv): algorithmic bytes / per-call
+  roofline  the dominant call type (p8_mul_mat_vec_group = k_gemv + k_gemv_reduce): algorithmic bytes / per-call
             duration, timed with CUDA events around a graph of that call type's 32 per-layer calls, against
             MEASURED_PEAKS.json hbm_gbs; traffic = DRAM bytes of the same call from an ncu capture
   cpu_baseline  the reference's own CPU core (oracle/_ref, x16 vrc_tg) on one layer's 7 GEMVs, all host threads
@@ -151,9 +151,9 @@ class ClockSampler:
                 "samples": len(self.sm)}
 
 
-# DRAM bytes (read + write) of one call, from ncu captures of the same call at 1 GPU (profiles/k_gemv_llama8b_gate_up.md);
-# reported only for the configuration the capture measured
-TRAFFIC_BYTES = {"gate+up": 31587840}
+# DRAM bytes (read + write) of one call (k_gemv + k_gemv_reduce), from ncu captures of the same call at 1 GPU
+# (profiles/k_gemv_llama8b_gate_up.md); reported only for the configuration the capture measured
+TRAFFIC_BYTES = {"gate+up": 30377728 + 3584 + 2026240}
 
 
 def measured_bf16_tflops():
@@ -580,7 +580,7 @@ def run_b200(args, rank, world, local_rank):
             x = buf["down"]
         return x
 
-    launches_ops = 2 * len(groups) * model["layers"]  # k_act_prep + k_gemv per group
+    launches_ops = 2 * len(groups) * model["layers"]  # k_gemv + k_gemv_reduce per group
     # ---- (1 GPU) the same chain as chained launches (p8_chain: one persistent launch runs several projections with
     # one grid barrier each). Launches split where attention sits in a real decoder layer (between q/k/v and o):
     # [q/k/v 0], [o L-1, gate/up L-1, down L-1, q/k/v L] for L = 1..31, [o 31, gate/up 31, down 31]
@@ -953,7 +953,7 @@ def run_b200(args, rank, world, local_rank):
                 "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs (burst copy)",
                 "timing": "CUDA events around graph replays of the whole step; every kernel of the step is a k_chain launch"}
     else:
-        roof = {"kernel": f"p8_mul_mat_vec_group {dom} (k_act_prep + k_gemv)", "bound": "hbm", "achieved": round(achieved, 1),
+        roof = {"kernel": f"p8_mul_mat_vec_group {dom} (k_gemv + k_gemv_reduce)", "bound": "hbm", "achieved": round(achieved, 1),
                 "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                 "traffic": TRAFFIC_BYTES.get(dom) if world == 1 else None, "algorithmic_bytes": dom_bytes,
                 "call_us": round(dom_s * 1e6, 3), "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs (burst copy)",
@@ -979,7 +979,7 @@ def run_b200(args, rank, world, local_rank):
     }
     if t_other is not None and other == "ops":
         line["per_op_decode"] = {"tok_s": round(args.steps / t_other, 3), "ms_per_step": round(1e3 * t_other / args.steps, 4),
-                                 "kernels": "p8_mul_mat_vec_group per group call (k_act_prep + k_gemv), 256 launches per token",
+                                 "kernels": "p8_mul_mat_vec_group per group call (k_gemv + k_gemv_reduce), 256 launches per token",
                                  "per_call_type": per_call}
     if t_other is not None and other == "chain":
         line["chain_decode"] = {"tok_s": round(args.steps / t_other, 3), "ms_per_step": round(1e3 * t_other / args.steps, 4),
@@ -1010,7 +1010,7 @@ def run_b200(args, rank, world, local_rank):
         line["layer_prologues"] = {
             "ops": "RMSNorm*w -> q,k,v; o; RMSNorm*w -> gate,up; SwiGLU -> down (x 32 layers, graph-replayed, device-timed)",
             "fused_tok_s": round(1.0 / layer["fused"], 1), "torch_ops_tok_s": round(1.0 / layer["torch_ops"], 1),
-            "fused": "p8_mul_mat_vec_group_ex (prologue in k_act_prep)",
+            "fused": "p8_mul_mat_vec_group_ex (input op in k_gemv's table build)",
             "torch_ops": "separate torch elementwise/reduction kernels, then p8_mul_mat_vec_group"}
     if prefill is not None:
         ntok, t_pass, flop, t_sep = prefill
@@ -1045,7 +1045,7 @@ CASE_GROUPS = {  # Llama-3.1-8B: (rows, K) per tensor of a group that reads one 
 
 
 def run_case(args):
-    """--case gemv:GROUP          the grouped batch-1 GEMV (k_act_prep + k_gemv), --iters calls rotating over --copies
+    """--case gemv:GROUP          the grouped batch-1 GEMV (k_gemv + k_gemv_reduce), --iters calls rotating over --copies
                                   distinct weight copies (copies > 1 read DRAM rather than L2), optionally --graph
        --case gemm:GROUP:NCOLS    the batched product per tensor (tcgen05 GEMM), or :grouped for p8_mul_mat_group
        --case get_rows:GROUP:N    p8_get_rows of N random rows of each tensor of the group
