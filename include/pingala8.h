@@ -239,9 +239,9 @@ p8_status p8_tp_shard_cols(const uint8_t *slot, size_t nbytes, int64_t K, int64_
  * names another row count or another original row (the ranks called different tensors, or shards whose row order
  * differs) sets bit 4 (16).
  *
- * Exchange buffer of rank r: 2 * world * max_rows u64 entries; entry (parity s, source rank q, sorted row i) at index
- * (s * world + q) * max_rows + i holds (tag << 32) | float bits of rank q's partial y[prm[i]], tag = 0x80000000 |
- * prm[i] << 16 | rows / 32 (prm: the slot's row permutation, sorted -> original row); 0 = empty.
+ * Exchange buffer of rank r: 2 * world * max_rows u64 entries; entry (parity s, source rank q, output row ro) at index
+ * (s * world + q) * max_rows + ro holds (tag << 32) | float bits of rank q's partial y[ro], tag = 0x80000000 |
+ * ro << 16 | rows / 32; 0 = empty.
  * Parity s = the communicator's call count & 1 (the first call is 1). Peers' buffers must have the same world and
  * max_rows. All ranks make the same sequence of p8_tp_gemv_allreduce calls on their communicators, each with its
  * column shard of one tensor (same rows); a rank with no columns cannot take part (use a collective instead).

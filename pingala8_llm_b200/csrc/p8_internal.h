@@ -68,18 +68,18 @@ p8_status launch_gemv(const p8_tensor *t, const float *X, int64_t ncols, int64_t
                       size_t ws_bytes, cudaStream_t st);
 p8_status launch_gemv_group_pro(const p8_tensor *const *ts, int nt, const float *x, const p8_prologue *pro, float *const *Ys,
                                 void *ws, size_t ws_bytes, cudaStream_t st);
-// Fused row-parallel exchange of the GEMV epilogue (one-shot all-reduce over peer memory). Every rank owns an exchange
-// buffer of u64 entries: entry (parity s, source rank q, sorted row i) at index (s * world + q) * cap + i holds
-// (tag << 32) | float bits of rank q's partial y[prm[i]], 0 when empty; tag = 0x80000000 | prm[i] << 16 | rows / 32.
-// Indexing by sorted row keeps a warp's 32 entries contiguous (one coalesced write per peer), and the original row in
-// the tag checks that the ranks' shards share the row order. A rank stores its partials into every peer's buffer
+// Fused row-parallel exchange of the GEMV's row reduce (one-shot all-reduce over peer memory). Every rank owns an
+// exchange buffer of u64 entries: entry (parity s, source rank q, output row ro) at index (s * world + q) * cap + ro
+// holds (tag << 32) | float bits of rank q's partial y[ro], 0 when empty; tag = 0x80000000 | ro << 16 | rows / 32.
+// The reduce kernel's threads take consecutive output rows, so a warp's 32 entries are one coalesced write per peer;
+// the row count in the tag checks that the ranks run the same tensor. A rank stores its partials into every peer's buffer
 // (plain 8-byte stores over NVLink), then polls its own buffer for the peers' partials (bounded by timeout_ns), sums
 // the ranks' values in rank order and clears the entries it consumed. The parity s = epoch & 1 alternates per call, so
 // a rank one call ahead writes the other half while a slow peer still reads this one.
 constexpr int kTpMaxWorld = 8;
 struct TpExchange {
     unsigned long long *peer[kTpMaxWorld];  // each rank's exchange buffer as mapped here (peer[rank] = own)
-    const unsigned int *epoch;              // this rank's call counter, advanced by the call's prep kernel
+    const unsigned int *epoch;              // this rank's call counter, advanced by the call's k_gemv
     long long cap;                          // output rows per (parity, rank) section
     unsigned long long timeout_ns;
     unsigned int tag_rows;                  // rows / 32 (tag bits 0-15); an entry with another non-zero tag is a mismatch

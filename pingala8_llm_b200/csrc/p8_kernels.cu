@@ -222,8 +222,9 @@ cudaError_t launch_get_rows(const p8_tensor *t, const int32_t *ids, int64_t n, f
 //                  through global memory and no second kernel sits between x and the units. The payload words of a
 //                  warp's next unit are loaded into registers while the current unit computes; each lane owns one
 //                  row: per chunk 1 PRMT (field byte + rotated chunk offset -> table byte address) + 1 LDS + 1 FADD.
-//                  A unit stores its 32 row partials (coalesced, [b][rows]).
-//   k_gemv_reduce  the rows: y[prm[r]] = sum_b part[b][r] in block order + clamp delta (deterministic, no float
+//                  A unit stores its 32 row partials at the rows' original positions ([b][rows]).
+//   k_gemv_reduce  the rows, in original order: y[ro] = sum_b part[b][ro] in block order + clamp delta (coalesced;
+//                  deterministic, no float
 //                  atomics); the row-parallel exchange for the fused tensor-parallel call.
 // Both kernels use programmatic dependent launch: each is resident and waiting before its predecessor ends, and a
 // call is two kernel hand-offs (producer of x -> k_gemv -> k_gemv_reduce) with no grid barrier.
@@ -274,7 +275,7 @@ struct GemvArgs {
     int ustart[kGemvMaxCtas + 1];  // CTA c takes the units [ustart[c], ustart[c + 1]) of the block-major list
 };
 
-// the row reduction after k_gemv: y[prm[r]] = sum_b part[b][r] (block order) + clamp delta (+ row-parallel exchange)
+// the row reduction after k_gemv: y[ro] = sum_b part[b][ro] (block order) + clamp delta (+ row-parallel exchange)
 struct ReduceArgs {
     GemvTensor t[kMaxGroup];
     int rows_total, ntensors, nb;
@@ -619,7 +620,7 @@ __device__ __forceinline__ void build_tables(const GemvArgs &a, BuildSmem &s, in
 // CTA takes the contiguous range [ustart[c], ustart[c + 1]) of the block-major unit list (host-balanced: a unit
 // counts one, every extra block touched counts the cost of building its table) and builds the tables of the blocks
 // it touches in its own shared memory, two at a time; warp w takes units u0 + w, u0 + w + 16, ... The row partials
-// go to part[b][rows]; k_gemv_reduce (the next kernel) sums them.
+// go to part[b][ro] (original row ro = prm[r]); k_gemv_reduce (the next kernel) sums them.
 template <int PRO>
 __global__ void __maxnreg__(104) k_gemv(const __grid_constant__ GemvArgs a) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -665,10 +666,12 @@ __global__ void __maxnreg__(104) k_gemv(const __grid_constant__ GemvArgs a) {
     uint32_t nxt[16];
     uint32_t mt_n = 0, mt_nn = 0;
     uint16_t s_n = 0;
+    int16_t p_n = 0;
     auto fetch = [&](const WarpCursor &c, uint32_t mt) {  // payload + row scale of unit c (its M word known)
         const int ti = tensor_of(a, c.rr), g = c.rr - a.t[ti].g0;
         if ((mt >> 29) == 3) load3(a.t[ti].D + (mt & 0x1FFFFFFFu), lane, nxt);
         s_n = __ldg(a.t[ti].S + (size_t)c.b * a.t[ti].rows + g * 32 + lane);
+        p_n = __ldg(a.t[ti].prm + g * 32 + lane);  // the row's original position: partials are stored there
     };
     WarpCursor nc = {b_first, rr_first + warp};
     while (nc.rr >= a.ng_total) {
@@ -698,6 +701,7 @@ __global__ void __maxnreg__(104) k_gemv(const __grid_constant__ GemvArgs a) {
             const float d0 = bs.d[seg & 1][0], d1 = bs.d[seg & 1][1];
             const uint32_t mt = mt_n;
             const uint16_t sc = s_n;
+            const int ro = p_n;
             uint32_t cur[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) cur[i] = nxt[i];
@@ -726,15 +730,14 @@ __global__ void __maxnreg__(104) k_gemv(const __grid_constant__ GemvArgs a) {
                 const uint32_t *p0 = T.D + (mt & 0x1FFFFFFFu);
                 part = (seg & 1) ? tile_row_other<1>(c, p0, po, lane, d0, d1) : tile_row_other<0>(c, p0, po, lane, d0, d1);
             }
-            const int r = g * 32 + lane;
-            T.part[(size_t)b * T.rows + r] = __fmul_rn(part, h2f(sc));
+            T.part[(size_t)b * T.rows + ro] = __fmul_rn(part, h2f(sc));
         }
     }
 }
 
 // One thread per (row, block slice): a row's blocks are cut into S = ceil(nb / 16) slices of 16 (the last one
 // shorter); slice j sums blocks [16 j, 16 j + 16) of its row in block order with all its loads in flight, then one
-// thread adds the S slice sums in slice order, adds the clamp delta sum_e val_e x[col_e] and stores y[prm[r]] (with
+// thread adds the S slice sums in slice order, adds the clamp delta sum_e val_e x[col_e] and stores y[ro] (with
 // the row-parallel exchange first for TPX). The summation order depends on nb alone -- not on the grid, the group or
 // the rows per CTA -- so every entry point that computes a row gets the same bits.
 constexpr int kRedThreads = 256;
@@ -759,7 +762,7 @@ __global__ void __launch_bounds__(kRedThreads, 5) k_gemv_reduce(const __grid_con
         for (int i = 1; i < kMaxGroup; ++i)
             if (i < a.ntensors && rt >= a.t[i].row0) c_ti = i;
         const GemvTensor &T = a.t[c_ti];
-        c_ro = T.prm[rt - T.row0];
+        c_ro = rt - T.row0;
         c_e0 = T.cp[c_ro];
         c_e1 = T.cp[c_ro + 1];
     }
@@ -806,13 +809,13 @@ __global__ void __launch_bounds__(kRedThreads, 5) k_gemv_reduce(const __grid_con
                 for (int i = 1; i < kMaxGroup; ++i)
                     if (i < a.ntensors && rt2 >= a.t[i].row0) c_ti = i;
                 const GemvTensor &T = a.t[c_ti];
-                c_ro = T.prm[rt2 - T.row0];
+                c_ro = rt2 - T.row0;
                 c_e0 = T.cp[c_ro];
                 c_e1 = T.cp[c_ro + 1];
             }
             const GemvTensor &T = a.t[c_ti];
             for (int e = c_e0; e < c_e1; ++e) y = __fadd_rn(y, __fmul_rn(T.cv[e], a.X[T.cc[e]]));
-            if (tpx) y = tp_exchange_row(a.tp, par, rt2, c_ro, y, deadline, tp_ok);
+            if (tpx) y = tp_exchange_row(a.tp, par, c_ro, c_ro, y, deadline, tp_ok);
             T.Y[c_ro] = y;
         }
         __syncthreads();

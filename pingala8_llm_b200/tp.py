@@ -257,14 +257,14 @@ class TpComm:
             pass
 
 
-def exchange_entries(y, prm, rows):
-    """A rank's exchange entries (int64 bit patterns, sorted-row order) for its partial output y (original row order,
-    float32 CUDA) of a tensor with row permutation prm (sorted -> original row): entry i holds y[prm[i]] with the tag
-    0x80000000 | prm[i] << 16 | rows / 32 in its high word (layout: p8_tp_gemv_allreduce)."""
+def exchange_entries(y, rows):
+    """A rank's exchange entries (int64 bit patterns, output-row order) for its partial output y (float32 CUDA) of a
+    tensor with `rows` rows: entry ro holds y[ro] with the tag 0x80000000 | ro << 16 | rows / 32 in its high word
+    (layout: p8_tp_gemv_allreduce)."""
     import torch
 
-    p = torch.as_tensor(np.asarray(prm, np.int64), device=y.device)
-    bits = y[p].view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    p = torch.arange(y.numel(), dtype=torch.int64, device=y.device)
+    bits = y.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
     tag = (0x80000000 | (p << 16) | (int(rows) >> 5)) - (1 << 32)  # the tag as a negative int32 (bit 31 set)
     return bits | (tag << 32)  # the same 64 bits as a signed int64
 

@@ -24,8 +24,8 @@ PRM = {}
 
 
 def _entries(y, rows):
-    """exchange entries (sorted-row order, int64 bit patterns) of partial output y of the tensor set up last"""
-    return tp.exchange_entries(y, PRM["prm"], rows)
+    """exchange entries (output-row order, int64 bit patterns) of partial output y of the tensor set up last"""
+    return tp.exchange_entries(y, rows)
 
 
 def _setup(rows, K, world, seed=3, nd=11):
