@@ -236,7 +236,6 @@ constexpr int kGemvThreads = 512;
 constexpr int kGemvWarps = kGemvThreads / 32;
 constexpr int kMaxGroup = 4;
 constexpr int kGemvMaxCtas = 256;           // CTA ranges carried in the launch arguments
-constexpr unsigned long long kGridWaitNs = 20000000ull;  // grid-barrier deadline of the chain kernel: 20 ms
 // dynamic shared memory of k_gemv: two table buffers, two G buffers (both half-slices)
 constexpr int kSmemT0 = 0, kSmemT1 = kTabBytes, kSmemG0 = 2 * kTabBytes, kSmemG1 = kSmemG0 + 2 * kGInts * 4,
               kGemvSmem = kSmemG1 + 2 * kGInts * 4;
@@ -253,8 +252,39 @@ struct GemvTensor {
     const float *cv;
     float *Y;
     float *part;          // [nb][rows] row partials per block
+    const float *res;     // chained calls: residual added to the output (nullptr: none)
     int rows, ng, g0, row0;  // g0: first unit index of this tensor inside one block; row0: first row in the group
     int ucls;                // uniform class (payload of tile i at word i * 64 NW), 0 if the M words must be read
+};
+
+// Chained calls (p8_chain): a step's input may be an output y of the previous step, read straight from that step's
+// partials while the tables are built; the previous step's other outputs are reduced by this step's CTAs in equal
+// shares. Either way a previous output row is
+//     y[ro] = ((sum over 16-block slices, in order, of the slice's partials in block order) + clamp delta on x'_prev)
+//             * scale_prev + res[ro]
+// the same order as k_gemv_reduce, so a row's value does not depend on which kernel or CTA reduced it. scale_prev is
+// the previous step's deferred RMSNorm scale (1 / sqrt(sum of its blocks' x^2 / K + eps)) or 1.
+struct ChainSrc {
+    const float *part;    // the tensor's partials [nb][rows] (original row positions); nullptr: not from partials
+    const int *cp;        // its clamp-delta CSR by original row
+    const uint16_t *cc;
+    const float *cv;
+    const float *res;     // residual added to its output (nullptr: none)
+    float *Y;             // its output (the reducing CTA writes it)
+    int rows;
+};
+struct ChainIn {
+    ChainSrc x, x2;            // sources of this step's x and of the SwiGLU up (part == nullptr: from memory)
+    ChainSrc unc[kMaxGroup];   // previous-step outputs this step does not read
+    int nunc, unc_rows;
+    const float *xv;           // the previous step's x' (its outputs' clamp-delta term)
+    const float *ss;           // the previous step's per-block sums of x^2 when its RMSNorm scale is deferred, else nullptr
+    int nb, K;                 // the previous step's blocks and K
+    float eps;
+    int chained;               // 1: there is a previous step (the fields above are valid)
+    float *ss_out;             // this step's input comes from partials with RMSNorm: per-block sums of x^2 (the scale
+                               // is deferred to the outputs); nullptr otherwise
+    unsigned long long *trace; // optional phase stamps: [CTA][8] globaltimer ns (nullptr: off)
 };
 
 struct GemvArgs {
@@ -281,7 +311,39 @@ struct ReduceArgs {
     int rows_total, ntensors, nb;
     const float *X;  // x, or x' of the input op: the clamp delta multiplies it
     TpExchange tp;   // row-parallel exchange (tp.world > 1), single tensor only
+    const float *ss; // the last chain step's deferred RMSNorm: per-block sums of x^2 (nullptr: scale 1)
+    int ssK;
+    float eps;
 };
+
+// the deferred RMSNorm scale from nb per-block sums of squares (one thread; fixed order)
+__device__ __forceinline__ float deferred_scale(const float *ss, int nb, int K, float eps) {
+    float v = 0.f;
+#pragma unroll 8
+    for (int i = 0; i < nb; ++i) v = __fadd_rn(v, __ldcg(ss + i));
+    return __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fdiv_rn(v, (float)K), eps)));
+}
+
+// the 16-block slice sums of row ro of a [nb][rows] partial array (slice j: blocks 16 j .. 16 j + 15 in block order)
+__device__ __forceinline__ float slice_sum(const float *part, int rows, int nb, int ro, int j) {
+    const int b0 = 16 * j, n = min(16, nb - b0);
+    float v[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) v[k] = k < n ? __ldcg(part + (size_t)(b0 + k) * rows + ro) : 0.f;
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+        if (k < n) s = __fadd_rn(s, v[k]);
+    return s;
+}
+// y of a chained output row from its slice sums sl[0 .. S) (k_gemv_reduce's order), clamp delta, scale, residual
+__device__ __forceinline__ float chain_row_value(const ChainSrc &T, int ro, float y, const float *xv, float scale) {
+    const int e1 = __ldg(T.cp + ro + 1);
+    for (int e = __ldg(T.cp + ro); e < e1; ++e) y = __fadd_rn(y, __fmul_rn(__ldg(T.cv + e), __ldcg(xv + __ldg(T.cc + e))));
+    y = __fmul_rn(y, scale);
+    if (T.res) y = __fadd_rn(y, __ldcg(T.res + ro));
+    return y;
+}
 
 // x'[i] = (x[i] * scale) * w[i], scale = 1 / sqrt(mean(x^2) + eps): ggml's rms_norm (sum of squares, mean by float
 // division, 1 / sqrtf) followed by the weight multiply. Every CTA sums the whole vector in the same fixed order
@@ -525,12 +587,18 @@ struct WarpCursor {
 
 // table-build scratch of one k_gemv CTA (static shared memory): x16 ints and coset dot products of up to two blocks,
 // the codebook, the per-half-slice scales of each table buffer, the RMSNorm reduction
-struct BuildSmem {
+struct __align__(16) BuildSmem {
     float4 Af[256];  // the codebook as floats (entry f: its four int8 values)
     int q[2][256];
     int cx[2][64];
     float d[2][2];   // [buffer][half-slice]
     float red[kGemvThreads];
+};
+
+// chain steps only: the blocks' input values (and SwiGLU up), reduced from the previous step's partials or loaded;
+// read as float4 by build_tables, so 16-byte aligned
+struct __align__(16) ChainSmem {
+    float xin[2][256], x2in[2][256];
 };
 
 // The activation tables of blocks bA .. bA + nbld - 1 (nbld <= 2) into table buffers 0 .. nbld - 1 of this CTA's
@@ -540,14 +608,24 @@ struct BuildSmem {
 //   T[f][hs][t] = <A[f], q_t> as a float (exact: |T| < 2^23), four fp32 FMAs on the float codebook copy
 //   G[hs][grp][m] = sum over the set bits i of nibble m of <c, q_{4 grp + i}> (coset nibble tables, exact)
 // The first CTA of a block (the one holding the block's first unit) stores x' for the clamp-delta term.
-template <int PRO>
-__device__ __forceinline__ void build_tables(const GemvArgs &a, BuildSmem &s, int bA, int nbld, float scale, long long u0,
-                                             long long u1) {
+template <int PRO, bool CH>
+__device__ __forceinline__ void build_tables(const GemvArgs &a, BuildSmem &s, const ChainSmem *cs, float *ss_out, int bA, int nbld,
+                                             float scale, long long u0, long long u1) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (warp < nbld) {
         const int i = warp, b = bA + i;
-        const float *x = a.X + b * 256 + 8 * lane;
+        const float *x = CH ? &cs->xin[i][8 * lane] : a.X + b * 256 + 8 * lane;
         float4 x0 = *reinterpret_cast<const float4 *>(x), x1 = *reinterpret_cast<const float4 *>(x + 4);
+        const long long bu = (long long)b * a.ng_total;  // the block's first unit
+        if (PRO == P8_PROLOGUE_RMSNORM && CH && ss_out) {  // deferred RMSNorm: the block's sum of x^2 (fixed order)
+            float q2 = 0.f;
+            q2 = __fmaf_rn(x0.x, x0.x, q2); q2 = __fmaf_rn(x0.y, x0.y, q2); q2 = __fmaf_rn(x0.z, x0.z, q2);
+            q2 = __fmaf_rn(x0.w, x0.w, q2); q2 = __fmaf_rn(x1.x, x1.x, q2); q2 = __fmaf_rn(x1.y, x1.y, q2);
+            q2 = __fmaf_rn(x1.z, x1.z, q2); q2 = __fmaf_rn(x1.w, x1.w, q2);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) q2 = __fadd_rn(q2, __shfl_down_sync(0xffffffffu, q2, o));
+            if (lane == 0 && u0 <= bu && bu < u1) ss_out[b] = q2;
+        }
         const float *icp = a.ic + b * 256 + 8 * lane;
         const float4 i0 = *reinterpret_cast<const float4 *>(icp), i1 = *reinterpret_cast<const float4 *>(icp + 4);
         if (PRO == P8_PROLOGUE_RMSNORM) {
@@ -558,13 +636,13 @@ __device__ __forceinline__ void build_tables(const GemvArgs &a, BuildSmem &s, in
             x1 = make_float4(__fmul_rn(__fmul_rn(x1.x, scale), w1.x), __fmul_rn(__fmul_rn(x1.y, scale), w1.y),
                              __fmul_rn(__fmul_rn(x1.z, scale), w1.z), __fmul_rn(__fmul_rn(x1.w, scale), w1.w));
         } else if (PRO == P8_PROLOGUE_SWIGLU) {  // silu(gate) * up = gate / (1 + exp(-gate)) * up
-            const float4 u0v = *reinterpret_cast<const float4 *>(a.x2 + b * 256 + 8 * lane);
-            const float4 u1v = *reinterpret_cast<const float4 *>(a.x2 + b * 256 + 8 * lane + 4);
+            const float *x2p = CH ? &cs->x2in[i][8 * lane] : a.x2 + b * 256 + 8 * lane;
+            const float4 u0v = *reinterpret_cast<const float4 *>(x2p);
+            const float4 u1v = *reinterpret_cast<const float4 *>(x2p + 4);
             auto sw = [](float g, float u) { return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u); };
             x0 = make_float4(sw(x0.x, u0v.x), sw(x0.y, u0v.y), sw(x0.z, u0v.z), sw(x0.w, u0v.w));
             x1 = make_float4(sw(x1.x, u1v.x), sw(x1.y, u1v.y), sw(x1.z, u1v.z), sw(x1.w, u1v.w));
         }
-        const long long bu = (long long)b * a.ng_total;  // the block's first unit
         if (PRO != P8_PROLOGUE_NONE && u0 <= bu && bu < u1) {
             *reinterpret_cast<float4 *>(a.xv + b * 256 + 8 * lane) = x0;
             *reinterpret_cast<float4 *>(a.xv + b * 256 + 8 * lane + 4) = x1;
@@ -616,15 +694,79 @@ __device__ __forceinline__ void build_tables(const GemvArgs &a, BuildSmem &s, in
     __syncthreads();
 }
 
+// Chained step: the input values of blocks bA .. bA + nbld - 1 into s.xin (and the SwiGLU up into s.x2in), each
+// either reduced from the previous step's partials (the block's first CTA also writes those rows of the previous
+// output) or loaded from memory. Pass 1 sums the 16-block slices of every (source, block, row) with each slice's loads
+// in flight (the slice sums go to the table region, free until the tables are built); pass 2 adds the slices in order
+// and applies the clamp delta, the previous step's scale and residual. Every thread of the CTA takes part.
+template <int PRO>
+__device__ __forceinline__ void chain_inputs(const GemvArgs &a, const ChainIn &ch, ChainSmem &s, int bA, int nbld, float scale_prev,
+                                             long long u0, long long u1) {
+    const int tid = threadIdx.x;
+    const bool px = ch.x.part != nullptr, px2 = PRO == P8_PROLOGUE_SWIGLU && ch.x2.part != nullptr;
+    const int S = (ch.nb + 15) / 16;
+    float *sl = reinterpret_cast<float *>(g_smem + kSmemT0);  // [src][blk][slice][256]
+    const int per_src = nbld * 256 * S;
+    const int items = (px ? per_src : 0) + (px2 ? per_src : 0);
+    for (int it = tid; it < items; it += kGemvThreads) {
+        const int src = px ? (it >= per_src ? 1 : 0) : 1;
+        const int r = px ? (it >= per_src ? it - per_src : it) : it;
+        const int blk = r / (256 * S), rem = r - blk * 256 * S, j = rem >> 8, i = rem & 255;
+        const ChainSrc &T = src ? ch.x2 : ch.x;
+        sl[((src * 2 + blk) * S + j) * 256 + i] = slice_sum(T.part, T.rows, ch.nb, 256 * (bA + blk) + i, j);
+    }
+    for (int it = tid; it < nbld * 256; it += kGemvThreads) {  // sources in memory
+        const int blk = it >> 8, i = it & 255, col = 256 * (bA + blk) + i;
+        if (!px) s.xin[blk][i] = __ldcg(a.X + col);
+        if (PRO == P8_PROLOGUE_SWIGLU && !px2) s.x2in[blk][i] = __ldcg(a.x2 + col);
+    }
+    __syncthreads();
+    const int n2 = (px ? nbld * 256 : 0) + (px2 ? nbld * 256 : 0);
+    for (int it = tid; it < n2; it += kGemvThreads) {
+        const int src = px ? (it >= nbld * 256 ? 1 : 0) : 1;
+        const int r = px ? (it >= nbld * 256 ? it - nbld * 256 : it) : it;
+        const int blk = r >> 8, i = r & 255, ro = 256 * (bA + blk) + i;
+        const ChainSrc &T = src ? ch.x2 : ch.x;
+        const float *q = sl + (src * 2 + blk) * S * 256 + i;
+        float y = q[0];
+        for (int j = 1; j < S; ++j) y = __fadd_rn(y, q[j * 256]);
+        y = chain_row_value(T, ro, y, ch.xv, scale_prev);
+        (src ? s.x2in : s.xin)[blk][i] = y;
+        const long long bu = (long long)(bA + blk) * a.ng_total;
+        if (u0 <= bu && bu < u1) T.Y[ro] = y;  // the block's first CTA writes the previous step's output
+    }
+    __syncthreads();
+}
+
+// Chained step: this CTA's equal share of the previous step's outputs that this step does not read (one thread per
+// row, the k_gemv_reduce order)
+__device__ __forceinline__ void chain_unconsumed(const ChainIn &ch, float scale_prev) {
+    const int ra = (int)((long long)ch.unc_rows * blockIdx.x / gridDim.x), rb = (int)((long long)ch.unc_rows * (blockIdx.x + 1) / gridDim.x);
+    const int S = (ch.nb + 15) / 16;
+    for (int r = ra + (int)threadIdx.x; r < rb; r += kGemvThreads) {
+        int ti = 0, ro = r;
+        while (ti + 1 < ch.nunc && ro >= ch.unc[ti].rows) ro -= ch.unc[ti++].rows;
+        const ChainSrc &T = ch.unc[ti];
+        float y = slice_sum(T.part, T.rows, ch.nb, ro, 0);
+        for (int j = 1; j < S; ++j) y = __fadd_rn(y, slice_sum(T.part, T.rows, ch.nb, ro, j));
+        T.Y[ro] = chain_row_value(T, ro, y, ch.xv, scale_prev);
+    }
+}
+
 // One CTA per SM at most (512 threads, 104 registers: 16 warps leave room for a k_gemv_reduce CTA beside it). Each
 // CTA takes the contiguous range [ustart[c], ustart[c + 1]) of the block-major unit list (host-balanced: a unit
 // counts one, every extra block touched counts the cost of building its table) and builds the tables of the blocks
 // it touches in its own shared memory, two at a time; warp w takes units u0 + w, u0 + w + 16, ... The row partials
 // go to part[b][ro] (original row ro = prm[r]); k_gemv_reduce (the next kernel) sums them.
-template <int PRO>
-__global__ void __maxnreg__(104) k_gemv(const __grid_constant__ GemvArgs a) {
+template <int PRO, bool CH>
+__device__ __forceinline__ void gemv_body(const GemvArgs &a, const ChainIn *chp) {
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     __shared__ BuildSmem bs;
+    ChainSmem *cs = nullptr;
+    if constexpr (CH) {
+        __shared__ ChainSmem chs;
+        cs = &chs;
+    }
     const long long u0 = a.ustart[blockIdx.x], u1 = a.ustart[blockIdx.x + 1];
     pdl_launch_dependents();
     if (u1 <= u0) return;
@@ -687,13 +829,28 @@ __global__ void __maxnreg__(104) k_gemv(const __grid_constant__ GemvArgs a) {
     }
     pdl_wait();  // x (and the row-parallel call counter) belong to the preceding kernel until it completes
     if (a.epoch && blockIdx.x == 0 && tid == 0) *a.epoch += 1u;  // k_gemv_reduce reads it after this kernel completes
-    float scale = 1.f;
-    if (PRO == P8_PROLOGUE_RMSNORM) scale = rms_scale<kGemvThreads>(a.X, a.K, a.eps, bs.red);
+    __shared__ float s_scale_prev;
+    if (CH && tid == 0) s_scale_prev = chp->ss ? deferred_scale(chp->ss, chp->nb, chp->K, chp->eps) : 1.f;
+    // chain phase stamps (read from the parameters when taken: no register held across the unit loop)
+    auto stamp = [&](int k) {
+        if constexpr (CH)
+            if (chp->trace && threadIdx.x == 0) chp->trace[(size_t)blockIdx.x * 8 + k] = global_ns();
+    };
+    stamp(0);
+    float scale = 1.f;  // a deferred RMSNorm (ss_out) builds the tables from x * w and scales the outputs later
+    if (PRO == P8_PROLOGUE_RMSNORM && !(CH && chp->ss_out)) scale = rms_scale<kGemvThreads>(a.X, a.K, a.eps, bs.red);
     // segments (blocks) two at a time: build their tables (buffers 0, 1), run the warp's units in them; a CTA spans
     // more than two blocks only when nb > the number of CTAs
     for (int ph = 0; 2 * ph < nseg; ++ph) {
         if (ph > 0) __syncthreads();  // every warp is done with the previous pair of tables
-        build_tables<PRO>(a, bs, b_first + 2 * ph, nseg - 2 * ph < 2 ? nseg - 2 * ph : 2, scale, u0, u1);
+        if (CH) {
+            if (ph == 0) __syncthreads();  // s_scale_prev
+            chain_inputs<PRO>(a, *chp, *cs, b_first + 2 * ph, nseg - 2 * ph < 2 ? nseg - 2 * ph : 2, s_scale_prev, u0, u1);
+        }
+        if (ph == 0) stamp(1), stamp(2);
+        build_tables<PRO, CH>(a, bs, cs, CH ? chp->ss_out : nullptr, b_first + 2 * ph, nseg - 2 * ph < 2 ? nseg - 2 * ph : 2, scale, u0,
+                              u1);
+        if (ph == 0) stamp(3);
         const int seg_end = 2 * ph + 2;
         while (in_range(nc) && nc.b - b_first < seg_end) {
             const int seg = nc.b - b_first;
@@ -712,8 +869,7 @@ __global__ void __maxnreg__(104) k_gemv(const __grid_constant__ GemvArgs a) {
                 nc2 = advance(nc);
                 if (in_range(nc2)) mt_nn = m_of(nc2);
             }
-            const int ti = tensor_of(a, rr), g = rr - a.t[ti].g0;
-            const GemvTensor &T = a.t[ti];
+            const GemvTensor &T = a.t[tensor_of(a, rr)];
             const int c = (int)(mt >> 29);
             float part;
             if (c == 3) {
@@ -733,6 +889,24 @@ __global__ void __maxnreg__(104) k_gemv(const __grid_constant__ GemvArgs a) {
             T.part[(size_t)b * T.rows + ro] = __fmul_rn(part, h2f(sc));
         }
     }
+    if constexpr (CH) {
+        if (chp->trace) {
+            __syncthreads();
+            stamp(4);
+        }
+        if (chp->nunc) chain_unconsumed(*chp, s_scale_prev);
+        stamp(5);
+    }
+}
+
+template <int PRO>
+__global__ void __maxnreg__(104) k_gemv(const __grid_constant__ GemvArgs a) {
+    gemv_body<PRO, false>(a, nullptr);
+}
+// a chain step (p8_chain.cuh): the same kernel with the previous step's outputs as its input
+template <int PRO>
+__global__ void __maxnreg__(104) k_gemv_chain(const __grid_constant__ GemvArgs a, const __grid_constant__ ChainIn ch) {
+    gemv_body<PRO, true>(a, &ch);
 }
 
 // One thread per (row, block slice): a row's blocks are cut into S = ceil(nb / 16) slices of 16 (the last one
@@ -744,7 +918,9 @@ constexpr int kRedThreads = 256;
 constexpr int kRedRowsPerCta = 32;
 constexpr int kRedSlice = 16;
 
-template <bool TPX>
+// CHN: a chain's last step (its deferred RMSNorm scale and residuals); a separate instantiation, so the per-op reduce
+// carries none of it
+template <bool TPX, bool CHN = false>
 __global__ void __launch_bounds__(kRedThreads, 5) k_gemv_reduce(const __grid_constant__ ReduceArgs a) {
     const int tid = threadIdx.x;
     __shared__ float red[kRedThreads];
@@ -767,6 +943,8 @@ __global__ void __launch_bounds__(kRedThreads, 5) k_gemv_reduce(const __grid_con
         c_e1 = T.cp[c_ro + 1];
     }
     pdl_wait();  // the partials (and x' of an input op) come from k_gemv
+    __shared__ float s_scale;
+    if (CHN && a.ss && tid == 0) s_scale = deferred_scale(a.ss, a.nb, a.ssK, a.eps);  // read after the loop's first barrier
     constexpr bool tpx = TPX;
     const unsigned int par = tpx ? (__ldcg(a.tp.epoch) & 1u) : 0u;  // advanced by this call's k_gemv
     const unsigned long long deadline = tpx ? global_ns() + a.tp.timeout_ns : 0ull;
@@ -815,6 +993,10 @@ __global__ void __launch_bounds__(kRedThreads, 5) k_gemv_reduce(const __grid_con
             }
             const GemvTensor &T = a.t[c_ti];
             for (int e = c_e0; e < c_e1; ++e) y = __fadd_rn(y, __fmul_rn(T.cv[e], a.X[T.cc[e]]));
+            if (CHN) {  // a chain's last step: its deferred RMSNorm scale and its residual
+                if (a.ss) y = __fmul_rn(y, s_scale);
+                if (T.res) y = __fadd_rn(y, __ldcg(T.res + c_ro));
+            }
             if (tpx) y = tp_exchange_row(a.tp, par, c_ro, c_ro, y, deadline, tp_ok);
             T.Y[c_ro] = y;
         }
@@ -867,8 +1049,11 @@ static int sm_count() {
         cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
         if (v <= 0) v = 148;
         cudaFuncSetAttribute(k_gemv<P8_PROLOGUE_NONE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
+        cudaFuncSetAttribute(k_gemv_chain<P8_PROLOGUE_NONE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
         cudaFuncSetAttribute(k_gemv<P8_PROLOGUE_RMSNORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
+        cudaFuncSetAttribute(k_gemv_chain<P8_PROLOGUE_RMSNORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
         cudaFuncSetAttribute(k_gemv<P8_PROLOGUE_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
+        cudaFuncSetAttribute(k_gemv_chain<P8_PROLOGUE_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
         n[dev].store(v, std::memory_order_release);
     }
     return v;
