@@ -1204,14 +1204,20 @@ def _case_chain(nlayers, args):
         torch.cuda.synchronize()
         mid.trace(None)
         T = tb.view(4, nsm, 8).cpu().numpy().astype(np.float64)
-        t0 = T[0, :, 0].min()
+        # stamps of the chained steps (1..3; the first step reads memory and is not stamped): [0] past the wait,
+        # [2] inputs ready, [3] tables built, [4] units done, [5] the previous step's unread rows reduced
+        live = T[1:, :, 0] > 0
+        t0 = T[1:, :, 0][live].min()
         phases = {}
-        names = ["reduce_inputs", "prologue_fwht", "tables", "units", "barrier"]
-        for sidx in range(4):
-            d = {names[k]: [round(float(np.median(T[sidx, :, k + 1] - T[sidx, :, k])) / 1e3, 3),
-                            round(float(np.max(T[sidx, :, k + 1] - T[sidx, :, k])) / 1e3, 3)] for k in range(5)}
-            d["start_us"] = [round(float(T[sidx, :, 0].min() - t0) / 1e3, 3), round(float(T[sidx, :, 0].max() - t0) / 1e3, 3)]
-            d["end_us"] = round(float(T[sidx, :, 5].max() - t0) / 1e3, 3)
+        spans = [("inputs", 0, 2), ("tables", 2, 3), ("units", 3, 4), ("unread_rows", 4, 5)]
+        if (T[1:, :, 6] > 0).any():  # a build that also stamps inside the table build: [6] x16 ints ready, [7] coset ready
+            spans += [("fwht_q", 2, 6), ("coset", 6, 7), ("table_fill", 7, 3)]
+        for sidx in range(1, 4):
+            ok = T[sidx, :, 0] > 0
+            d = {nm: [round(float(np.median(T[sidx, ok, b] - T[sidx, ok, a])) / 1e3, 3),
+                      round(float(np.max(T[sidx, ok, b] - T[sidx, ok, a])) / 1e3, 3)] for nm, a, b in spans}
+            d["start_us"] = [round(float(T[sidx, ok, 0].min() - t0) / 1e3, 3), round(float(T[sidx, ok, 0].max() - t0) / 1e3, 3)]
+            d["end_us"] = round(float(T[sidx, ok, 5].max() - t0) / 1e3, 3)
             phases[f"step{sidx}"] = d
         out["trace_median_max_us"] = phases
     print(json.dumps(out), flush=True)
@@ -1255,11 +1261,10 @@ def _case_chain_tiny(nsteps, rows, K, args):
         mid = T[1:-1]
         med = lambda a: round(float(np.median(a)) / 1e3, 3)  # noqa: E731
         has = mid[:, :, 3] > 0
-        out["phase_median_us"] = {"reduce_inputs": med((mid[:, :, 1] - mid[:, :, 0])[has]),
-                                  "prologue_fwht": med((mid[:, :, 2] - mid[:, :, 1])[has]),
+        out["phase_median_us"] = {"inputs": med((mid[:, :, 2] - mid[:, :, 0])[has]),
                                   "tables": med((mid[:, :, 3] - mid[:, :, 2])[has]),
                                   "units": med((mid[:, :, 4] - mid[:, :, 3])[has]),
-                                  "barrier": med(mid[:, :, 5] - mid[:, :, 4]),
+                                  "unread_rows": med(mid[:, :, 5] - mid[:, :, 4]),
                                   "step_to_step": med(T[2:, :, 0].min(1) - T[1:-1, :, 0].min(1))}
     print(json.dumps(out), flush=True)
     return 0

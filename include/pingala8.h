@@ -125,20 +125,21 @@ p8_status p8_mul_mat_group(const p8_tensor *const *ts, int n, const float *X, in
 
 /* A decode step evaluates a fixed run of MUL_MAT nodes, each reading an earlier one's output, with RMS_NORM + MUL,
  * SWIGLU and ADD nodes between them (ggml_backend_cuda_graph_compute walking the graph, each MUL_MAT through
- * ggml_cuda_mul_mat, CU:1330-1342). A chain runs such a run of batch-1 Pingala-8 products as ONE persistent launch
- * with one grid barrier per step, instead of two kernels and a barrier per product; an extension, the reference
- * launches every op separately. Step s computes, for its n tensors (equal K and column tables, as
- * p8_mul_mat_vec_group):
+ * ggml_cuda_mul_mat, CU:1330-1342). A chain runs such a run of batch-1 Pingala-8 products with ONE GEMV launch per
+ * product (plus one row reduce after the last), instead of a GEMV and a row reduce per product: a step whose input is
+ * an output of the previous step reads it straight from that step's partial sums while it builds its tables; an
+ * extension, the reference launches every op separately. Step s computes, for its n tensors (equal K and column
+ * tables, as p8_mul_mat_vec_group):
  *     y_i = W_i x' (+ res_i),  x' = pro(x)
  * pro as p8_prologue (NONE, RMSNORM with w and eps, SWIGLU with x2 = up). x (and x2) may be any device buffer of K
  * floats, or exactly an output y_j of the previous step (then the chain reads it straight from that step's partial
  * sums); any other overlap with the previous step's outputs is refused. An earlier step's output (two or more steps
  * back) may be read as x, x2 or res. res_i must not overlap y_i. Results equal the separate calls up to float
- * rounding (the RMSNorm scale multiplies the product instead of its input; the integer table sums are exact).
- * A plan holds device copies of the steps (buffers are fixed at creation, like a captured graph) and two barrier words:
- * p8_chain_create allocates and synchronises (set-up time); p8_chain_run only enqueues one launch on the stream and
- * is capturable; runs of one plan must not overlap on the GPU. A bounded barrier wait that runs out sets bit 32 of
- * p8_device_error (results of that run invalid). Workspace: p8_chain_workspace_size bytes, 256-byte aligned. */
+ * rounding where a step's RMSNorm input comes from the previous step (the scale then multiplies the product instead
+ * of its input; the integer table sums are exact), and bit for bit elsewhere.
+ * A plan holds the launch arguments of every step (buffers are fixed at creation, like a captured graph):
+ * p8_chain_create is set-up time; p8_chain_run only enqueues the launches on the stream and is capturable; runs of
+ * one plan must not overlap on the GPU. Workspace: p8_chain_workspace_size bytes, 256-byte aligned. */
 typedef struct p8_chain_step {
     int n;                   /* tensors reading the same input, 1..4 */
     const p8_tensor *t[4];
@@ -152,9 +153,10 @@ p8_status p8_chain_create(const p8_chain_step *steps, int nsteps, p8_chain **out
 size_t p8_chain_workspace_size(const p8_chain *c);
 p8_status p8_chain_run(const p8_chain *c, void *workspace, size_t workspace_bytes, void *stream);
 p8_status p8_chain_destroy(p8_chain *c);
-/* Profiling aid: record, in later runs, per step and CTA, 8 globaltimer stamps (ns) into the device buffer dev_buf
- * (nsteps x CTAs x 8 words, CTAs = the device's SM count; [0] step start, [1] rows the step does not pass on reduced,
- * [2] input values ready, [3] tables built, [4] units done, [5] grid barrier passed). NULL turns it off. */
+/* Profiling aid: record, in later runs, per step (after the first) and CTA, globaltimer stamps (ns) into the device
+ * buffer dev_buf (nsteps x CTAs x 8 words, CTAs = the device's SM count; [0] after the wait for the previous launch,
+ * [1] and [2] input values ready, [3] tables built, [4] units done, [5] the previous step's unread rows reduced).
+ * NULL turns it off. */
 p8_status p8_chain_trace(p8_chain *c, uint64_t *dev_buf, size_t words);
 
 /* y = W x like p8_mul_mat_vec, but with no workspace argument and no allocation by this library: the scratch is a
@@ -245,9 +247,10 @@ p8_status p8_tp_shard_cols(const uint8_t *slot, size_t nbytes, int64_t K, int64_
  * Parity s = the communicator's call count & 1 (the first call is 1). Peers' buffers must have the same world and
  * max_rows. All ranks make the same sequence of p8_tp_gemv_allreduce calls on their communicators, each with its
  * column shard of one tensor (same rows); a rank with no columns cannot take part (use a collective instead).
- * The GEMV is a persistent kernel (one CTA per SM, all resident): while a fused call may be in flight, run no other
- * kernel on the GPU that waits for other ranks (an NCCL collective on another stream): its CTAs can keep a GEMV CTA
- * from becoming resident while the peers' GEMVs wait for this rank. Synchronise the device before such a collective. */
+ * The exchange runs in the call's row-reduce kernel, whose CTAs (at most one per SM) wait for their peers: while a
+ * fused call may be in flight, run no other kernel on the GPU that waits for other ranks (an NCCL collective on another
+ * stream): its CTAs can keep a reduce CTA from becoming resident while the peers' wait for this rank. Synchronise the
+ * device before such a collective. */
 typedef struct p8_tp_comm p8_tp_comm;
 #define P8_IPC_HANDLE_BYTES 64
 /* rank of world (1..8) on the current device, up to max_rows output rows per call, waits bounded by timeout_ms */
@@ -311,8 +314,8 @@ p8_status p8_gguf_linear_info(const p8_gguf *g, int64_t i, const char **name, in
 p8_status p8_gguf_load_linear(p8_gguf *g, int64_t i, uint8_t *out, size_t out_cap, size_t *out_n);
 
 /* Non-zero if a kernel since the last call gave up (that launch's results are invalid), then clears the word. Bits:
- * 1 GEMV table wait, 2 GEMV grid barrier, 4 GEMM pipeline wait timed out; 8 row-parallel exchange wait timed out,
- * 16 exchange entry with a foreign tag; 32 chain grid barrier timed out. Synchronises the device. */
+ * 4 GEMM pipeline wait timed out, 8 row-parallel exchange wait timed out, 16 exchange entry with a foreign tag (1, 2
+ * and 32 are unused). Synchronises the device. */
 int p8_device_error(void);
 
 const char *p8_status_str(p8_status s);
