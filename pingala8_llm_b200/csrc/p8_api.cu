@@ -275,17 +275,8 @@ p8_status p8_mul_mat_ex(const p8_tensor *t, const float *X, int64_t ncols, int64
     }
     cudaStream_t s = (cudaStream_t)stream;
     if (gemm_supported(t, ncols)) return launch_gemm(t, X, ncols, ldx, Y, ldy, workspace, workspace_bytes, s, pro);
-    for (int64_t n = 0; n < ncols; ++n) {  // below the GEMM's column count: the batch-1 GEMV per column
-        p8_prologue pn;
-        if (pro) {
-            pn = *pro;
-            if (pn.x2) pn.x2 += n * ldx;
-        }
-        float *yn = Y + n * ldy;
-        const p8_status st = launch_gemv_group_pro(&t, 1, X + n * ldx, pro ? &pn : nullptr, &yn, workspace, workspace_bytes, s);
-        if (st) return st;
-    }
-    return P8_OK;
+    // below the GEMM's column count: the batch-1 GEMV, two columns per call where it can
+    return launch_gemv_cols(&t, 1, X, ncols, ldx, pro, &Y, &ldy, workspace, workspace_bytes, s);
 }
 
 size_t p8_workspace_size_group_ex(const p8_tensor *const *ts, int n, int64_t ncols, int kind) {
@@ -333,20 +324,8 @@ p8_status p8_mul_mat_group(const p8_tensor *const *ts, int n, const float *X, in
     }
     cudaStream_t s = (cudaStream_t)stream;
     if (nsup == n) return launch_gemm_group(ts, n, X, ncols, ldx, Ys, ldys, workspace, workspace_bytes, s, pro);
-    if (nsup == 0) {  // below the GEMM's column count: the grouped batch-1 GEMV per column
-        for (int64_t c = 0; c < ncols; ++c) {
-            p8_prologue pn;
-            if (pro) {
-                pn = *pro;
-                if (pn.x2) pn.x2 += c * ldx;
-            }
-            float *yc[4];
-            for (int i = 0; i < n; ++i) yc[i] = Ys[i] + c * ldys[i];
-            const p8_status st = launch_gemv_group_pro(ts, n, X + c * ldx, pro ? &pn : nullptr, yc, workspace, workspace_bytes, s);
-            if (st) return st;
-        }
-        return P8_OK;
-    }
+    if (nsup == 0)  // below the GEMM's column count: the grouped batch-1 GEMV, two columns per call where it can
+        return launch_gemv_cols(ts, n, X, ncols, ldx, pro, Ys, ldys, workspace, workspace_bytes, s);
     for (int i = 0; i < n; ++i) {  // tensors on different paths: one call each
         const p8_status st = p8_mul_mat_ex(ts[i], X, ncols, ldx, pro, Ys[i], ldys[i], workspace, workspace_bytes, stream);
         if (st) return st;

@@ -68,6 +68,8 @@ p8_status launch_gemv(const p8_tensor *t, const float *X, int64_t ncols, int64_t
                       size_t ws_bytes, cudaStream_t st);
 p8_status launch_gemv_group_pro(const p8_tensor *const *ts, int nt, const float *x, const p8_prologue *pro, float *const *Ys,
                                 void *ws, size_t ws_bytes, cudaStream_t st);
+p8_status launch_gemv_cols(const p8_tensor *const *ts, int nt, const float *X, int64_t ncols, int64_t ldx, const p8_prologue *pro,
+                           float *const *Ys, const int64_t *ldys, void *ws, size_t ws_bytes, cudaStream_t st);
 // Fused row-parallel exchange of the GEMV's row reduce (one-shot all-reduce over peer memory). Every rank owns an
 // exchange buffer of u64 entries: entry (parity s, source rank q, output row ro) at index (s * world + q) * cap + ro
 // holds (tag << 32) | float bits of rank q's partial y[ro], 0 when empty; tag = 0x80000000 | ro << 16 | rows / 32.

@@ -303,6 +303,7 @@ struct GemvArgs {
     float *xv;             // x' of the input op for the clamp-delta term (written by the first CTA of each block)
     unsigned int *epoch;   // row-parallel exchange: this rank's call counter (advanced by CTA 0), else nullptr
     int ustart[kGemvMaxCtas + 1];  // CTA c takes the units [ustart[c], ustart[c + 1]) of the block-major list
+    long long ldx;         // k_gemv2: column 1's x (and SwiGLU up) at X + ldx (x2 + ldx)
 };
 
 // the row reduction after k_gemv: y[ro] = sum_b part[b][ro] (block order) + clamp delta (+ row-parallel exchange)
@@ -1004,23 +1005,310 @@ __global__ void __launch_bounds__(kRedThreads, 5) k_gemv_reduce(const __grid_con
     }
 }
 
+// ================================================================================================================
+// Two columns at once (batched decode of 2 or 3 sequences): the weights are decoded once for both columns. The two
+// columns' tables of a block are interleaved as float2, T2[hs][f][t] (64 KiB per half-slice, both half-slices = the
+// two table buffers of k_gemv), so one PRMT-built address and one 64-bit lookup per 4-weight chunk serve both columns;
+// the coset tables likewise (G2[hs][grp][m]). A CTA works on one block at a time. Class-3 tensors in the uniform
+// layout only (the synthetic and class-3 model files); other tensors take the per-column path.
+// ================================================================================================================
+constexpr int kG2Off = 2 * 65536;                  // G2 after the two half-slice tables
+constexpr int kGemv2Smem = kG2Off + 2 * 1024;       // G2: [hs][8 groups][16][2] floats
+
+struct __align__(16) Build2Smem {
+    float4 Af[256];     // the codebook as floats
+    int q[2][256];      // x16 ints per column
+    int cx[2][64];      // <c, q_t> per column
+    float d[2][2];      // [column][half-slice]
+    float red[kGemvThreads];
+};
+
+// the lane's chunk offsets for the float2 tables: po byte i of word q = ((lane + 3 q + i) & 31) * 8
+__device__ __forceinline__ void po2_init(uint32_t (&po)[11], int lane) {
+#pragma unroll
+    for (int q = 0; q < 11; ++q) {
+        uint32_t r = 0;
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+            if (3 * q + i < 32) r |= (((uint32_t)(lane + 3 * q + i) & 31u) << 3) << (8 * i);
+        po[q] = r;
+    }
+}
+
+// half-slice HS of a class-3 unit row for both columns: table sum (steps alternate two accumulators) + coset term
+template <int HS, int k>
+struct Step2 {
+    static __device__ __forceinline__ void run(const uint32_t (&w)[16], const uint32_t (&po)[11], float2 &a, float2 &b) {
+        const float2 v = *reinterpret_cast<const float2 *>(g_smem + HS * 65536 + __byte_perm(w[8 * HS + k / 4], po[k / 3], Sel<k>::v));
+        if (k & 1) { b.x += v.x; b.y += v.y; } else { a.x += v.x; a.y += v.y; }
+        Step2<HS, k + 1>::run(w, po, a, b);
+    }
+};
+template <int HS>
+struct Step2<HS, 32> {
+    static __device__ __forceinline__ void run(const uint32_t (&)[16], const uint32_t (&)[11], float2 &, float2 &) {}
+};
+template <int HS>
+__device__ __forceinline__ float2 slice2(const uint32_t (&w)[16], const uint32_t (&po)[11], int lane) {
+    uint32_t pm = 0;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {  // z bits in step order (as zbits_fast)
+        const uint32_t x = (w[8 * HS + 2 * p + 1] & 0x80808080u) | ((w[8 * HS + 2 * p] >> 4) & 0x08080808u);
+        pm |= ((x * 0x00204081u) >> 24) << (8 * p);
+    }
+    const uint32_t H = pingala8_h(__funnelshift_l(pm, pm, lane));
+    float2 cs = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int grp = 0; grp < 8; ++grp) {  // nibble grp of H times 8 bytes
+        const uint32_t sh = grp == 0 ? (H << 3) : (H >> (4 * grp - 3));
+        const float2 v = *reinterpret_cast<const float2 *>(g_smem + kG2Off + HS * 1024 + grp * 128 + (sh & 0x78u));
+        cs.x += v.x;
+        cs.y += v.y;
+    }
+    float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
+    Step2<HS, 0>::run(w, po, a, b);
+    return make_float2((a.x + b.x) + cs.x, (a.y + b.y) + cs.y);  // class 3: one stage, no shift, coset multiplicity 1
+}
+
+// both columns' tables of block b: warp c (c < 2) prepares column c's x16 ints; then coset and the interleaved table
+template <int PRO>
+__device__ __forceinline__ void build_tables2(const GemvArgs &a, Build2Smem &s, int b, const float (&scale)[2], long long u0,
+                                              long long u1) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (warp < 2) {
+        const int c = warp;
+        const float *x = a.X + (size_t)c * a.ldx + b * 256 + 8 * lane;
+        float4 x0 = *reinterpret_cast<const float4 *>(x), x1 = *reinterpret_cast<const float4 *>(x + 4);
+        const float *icp = a.ic + b * 256 + 8 * lane;
+        const float4 i0 = *reinterpret_cast<const float4 *>(icp), i1 = *reinterpret_cast<const float4 *>(icp + 4);
+        if (PRO == P8_PROLOGUE_RMSNORM) {
+            const float sc = scale[c];
+            const float4 w0 = *reinterpret_cast<const float4 *>(a.pw + b * 256 + 8 * lane);
+            const float4 w1 = *reinterpret_cast<const float4 *>(a.pw + b * 256 + 8 * lane + 4);
+            x0 = make_float4(__fmul_rn(__fmul_rn(x0.x, sc), w0.x), __fmul_rn(__fmul_rn(x0.y, sc), w0.y),
+                             __fmul_rn(__fmul_rn(x0.z, sc), w0.z), __fmul_rn(__fmul_rn(x0.w, sc), w0.w));
+            x1 = make_float4(__fmul_rn(__fmul_rn(x1.x, sc), w1.x), __fmul_rn(__fmul_rn(x1.y, sc), w1.y),
+                             __fmul_rn(__fmul_rn(x1.z, sc), w1.z), __fmul_rn(__fmul_rn(x1.w, sc), w1.w));
+        } else if (PRO == P8_PROLOGUE_SWIGLU) {
+            const float *x2p = a.x2 + (size_t)c * a.ldx + b * 256 + 8 * lane;
+            const float4 u0v = *reinterpret_cast<const float4 *>(x2p), u1v = *reinterpret_cast<const float4 *>(x2p + 4);
+            auto sw = [](float g, float u) { return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))), u); };
+            x0 = make_float4(sw(x0.x, u0v.x), sw(x0.y, u0v.y), sw(x0.z, u0v.z), sw(x0.w, u0v.w));
+            x1 = make_float4(sw(x1.x, u1v.x), sw(x1.y, u1v.y), sw(x1.z, u1v.z), sw(x1.w, u1v.w));
+        }
+        const long long bu = (long long)b * a.ng_total;
+        if (PRO != P8_PROLOGUE_NONE && u0 <= bu && bu < u1) {
+            float *xv = a.xv + (size_t)c * a.K + b * 256 + 8 * lane;
+            *reinterpret_cast<float4 *>(xv) = x0;
+            *reinterpret_cast<float4 *>(xv + 4) = x1;
+        }
+        float v[8] = {__fmul_rn(x0.x, i0.x), __fmul_rn(x0.y, i0.y), __fmul_rn(x0.z, i0.z), __fmul_rn(x0.w, i0.w),
+                      __fmul_rn(x1.x, i1.x), __fmul_rn(x1.y, i1.y), __fmul_rn(x1.z, i1.z), __fmul_rn(x1.w, i1.w)};
+        fwht256_warp(v, lane);
+        float am = 0.f;
+#pragma unroll
+        for (int m = 0; m < 8; ++m) am = fmaxf(am, fabsf(v[m]));
+#pragma unroll
+        for (int o = 1; o < 16; o <<= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+        const float d = __fdiv_rn(am, 8191.f), id = d > 0.f ? __fdiv_rn(1.f, d) : 0.f;
+#pragma unroll
+        for (int m = 0; m < 8; ++m) s.q[c][8 * lane + m] = __float2int_rn(__fmul_rn(v[m], id));
+        if ((lane & 15) == 0) s.d[c][lane >> 4] = d;
+    }
+    __syncthreads();
+    if (tid < 128) {
+        const int c = tid >> 6, t = tid & 63;
+        int cx = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) cx += (int)(int8_t)(a.cs >> (8 * e)) * s.q[c][4 * t + e];
+        s.cx[c][t] = cx;
+    }
+    __syncthreads();
+    {  // G2[hs][grp][m][c]: thread (c, hs, grp, m)
+        const int c = tid >> 8, hs = (tid >> 7) & 1, grp = (tid >> 4) & 7, m = tid & 15;
+        int gsum = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+            if ((m >> k) & 1) gsum += s.cx[c][hs * 32 + 4 * grp + k];
+        reinterpret_cast<float *>(g_smem + kG2Off)[((hs * 8 + grp) * 16 + m) * 2 + c] = (float)gsum;
+    }
+    // T2[hs][f][t] = (<A[f], q0_t>, <A[f], q1_t>): thread (chunk ht, f mod 8), 32 entries, one 8-byte store each
+    const int ht = tid & 63, f0 = tid >> 6, hs = ht >> 5, t = ht & 31;
+    const float q00 = (float)s.q[0][4 * ht], q01 = (float)s.q[0][4 * ht + 1], q02 = (float)s.q[0][4 * ht + 2], q03 = (float)s.q[0][4 * ht + 3];
+    const float q10 = (float)s.q[1][4 * ht], q11 = (float)s.q[1][4 * ht + 1], q12 = (float)s.q[1][4 * ht + 2], q13 = (float)s.q[1][4 * ht + 3];
+    uint8_t *T = g_smem + hs * 65536 + t * 8;
+#pragma unroll 8
+    for (int j = 0; j < 32; ++j) {
+        const int f = f0 + 8 * j;
+        const float4 w = s.Af[f];
+        *reinterpret_cast<float2 *>(T + f * 256) =
+            make_float2(__fmaf_rn(w.x, q00, __fmaf_rn(w.y, q01, __fmaf_rn(w.z, q02, __fmul_rn(w.w, q03)))),
+                        __fmaf_rn(w.x, q10, __fmaf_rn(w.y, q11, __fmaf_rn(w.z, q12, __fmul_rn(w.w, q13)))));
+    }
+    __syncthreads();
+}
+
+// Two-column GEMV: the k_gemv unit loop with both columns' sums per unit; partials [column][b][rows] per tensor
+// (column 1 at part + nb * rows), rows at their original positions. A CTA's blocks one at a time.
+template <int PRO>
+__global__ void __maxnreg__(104) k_gemv2(const __grid_constant__ GemvArgs a) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    __shared__ Build2Smem bs;
+    const long long u0 = a.ustart[blockIdx.x], u1 = a.ustart[blockIdx.x + 1];
+    pdl_launch_dependents();
+    if (u1 <= u0) return;
+    const int b_first = (int)(u0 / a.ng_total), b_last = (int)((u1 - 1) / a.ng_total);
+    const int rr_first = (int)(u0 - (long long)b_first * a.ng_total);
+    const int rr_last_end = (int)(u1 - (long long)b_last * a.ng_total);
+    uint32_t po[11];
+    po2_init(po, lane);
+    if (tid < 256) {  // the codebook belongs to the tensors: converted before the wait
+        const uint32_t w = __ldg(a.A + tid);
+        bs.Af[tid] = make_float4((float)(int8_t)w, (float)(int8_t)(w >> 8), (float)(int8_t)(w >> 16), (float)(int8_t)(w >> 24));
+    }
+    auto in_range = [&](const WarpCursor &c) { return c.b < b_last || (c.b == b_last && c.rr < rr_last_end); };
+    auto advance = [&](WarpCursor c) -> WarpCursor {
+        c.rr += kGemvWarps;
+        while (c.rr >= a.ng_total) {
+            c.rr -= a.ng_total;
+            ++c.b;
+        }
+        return c;
+    };
+    uint32_t nxt[16];
+    uint16_t s_n = 0;
+    int16_t p_n = 0;
+    auto fetch = [&](const WarpCursor &c) {  // class-3 uniform: payload of tile g * nb + b at word tile * 512
+        const int ti = tensor_of(a, c.rr), g = c.rr - a.t[ti].g0;
+        const uint32_t tile = (uint32_t)g * (uint32_t)a.nb + (uint32_t)c.b;
+        load3(a.t[ti].D + (size_t)tile * 512, lane, nxt);
+        s_n = __ldg(a.t[ti].S + (size_t)c.b * a.t[ti].rows + g * 32 + lane);
+        p_n = __ldg(a.t[ti].prm + g * 32 + lane);
+    };
+    WarpCursor nc = {b_first, rr_first + warp};
+    while (nc.rr >= a.ng_total) {
+        nc.rr -= a.ng_total;
+        ++nc.b;
+    }
+    if (in_range(nc)) fetch(nc);
+    pdl_wait();  // x belongs to the preceding kernel until it completes
+    float scale[2] = {1.f, 1.f};
+    if (PRO == P8_PROLOGUE_RMSNORM) {
+        scale[0] = rms_scale<kGemvThreads>(a.X, a.K, a.eps, bs.red);
+        __syncthreads();
+        scale[1] = rms_scale<kGemvThreads>(a.X + a.ldx, a.K, a.eps, bs.red);
+    }
+    for (int b = b_first; b <= b_last; ++b) {
+        if (b > b_first) __syncthreads();  // every warp is done with the previous block's tables
+        build_tables2<PRO>(a, bs, b, scale, u0, u1);
+        const float d00 = bs.d[0][0], d01 = bs.d[0][1], d10 = bs.d[1][0], d11 = bs.d[1][1];
+        while (in_range(nc) && nc.b == b) {
+            const int rr = nc.rr;
+            const uint16_t sc = s_n;
+            const int ro = p_n;
+            uint32_t cur[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) cur[i] = nxt[i];
+            nc = advance(nc);
+            if (in_range(nc)) fetch(nc);
+            const GemvTensor &T = a.t[tensor_of(a, rr)];
+            const float2 i0 = slice2<0>(cur, po, lane), i1 = slice2<1>(cur, po, lane);
+            const float s = h2f(sc);
+            T.part[(size_t)b * T.rows + ro] = __fmul_rn(__fadd_rn(__fmul_rn(i0.x, d00), __fmul_rn(i1.x, d01)), s);
+            T.part[(size_t)(a.nb + b) * T.rows + ro] = __fmul_rn(__fadd_rn(__fmul_rn(i0.y, d10), __fmul_rn(i1.y, d11)), s);
+        }
+    }
+}
+
+// the rows of a two-column call: virtual row r of [0, 2 rows_total) is column r / rows_total; the same slice order as
+// k_gemv_reduce, so each column's outputs equal a one-column call's bit for bit
+struct Reduce2Args {
+    ReduceArgs r;          // column 0's view (X: column 0's x or x')
+    long long ldy[kMaxGroup];
+    const float *X1;       // column 1's x or x'
+};
+__global__ void __launch_bounds__(kRedThreads, 5) k_gemv_reduce2(const __grid_constant__ Reduce2Args A) {
+    const ReduceArgs &a = A.r;
+    const int tid = threadIdx.x;
+    __shared__ float red[kRedThreads];
+    pdl_launch_dependents();
+    const int total = 2 * a.rows_total;
+    const int r0 = (int)((long long)total * blockIdx.x / gridDim.x), r1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
+    const int n_rows = r1 - r0;
+    const int S = (a.nb + kRedSlice - 1) / kRedSlice;
+    const int R = min(n_rows, kRedThreads / S);
+    const int rl = R > 0 ? tid % R : 0, sl = R > 0 ? tid / R : S;
+    pdl_wait();  // the partials (and x' of an input op) come from k_gemv2
+    const int b_lo = kRedSlice * sl, b_hi = min(a.nb, kRedSlice * (sl + 1));
+    auto locate = [&](int vr, int &c, int &ti, int &ro) {
+        c = vr >= a.rows_total ? 1 : 0;
+        const int rt = vr - c * a.rows_total;
+        ti = 0;
+#pragma unroll
+        for (int i = 1; i < kMaxGroup; ++i)
+            if (i < a.ntensors && rt >= a.t[i].row0) ti = i;
+        ro = rt - a.t[ti].row0;
+    };
+    for (int base = r0; base < r1; base += R) {
+        const int vr = base + rl;
+        float s = 0.f;
+        if (sl < S && vr < r1) {
+            int c, ti, ro;
+            locate(vr, c, ti, ro);
+            const GemvTensor &T = a.t[ti];
+            const float *p = T.part + (size_t)c * a.nb * T.rows + ro;
+            int bb = b_lo;
+            for (; bb + 16 <= b_hi; bb += 16) {
+                float v[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = __ldcg(p + (size_t)(bb + j) * T.rows);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) s = __fadd_rn(s, v[j]);
+            }
+            float v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = bb + j < b_hi ? __ldcg(p + (size_t)(bb + j) * T.rows) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (bb + j < b_hi) s = __fadd_rn(s, v[j]);
+        }
+        if (sl < S) red[sl * R + rl] = s;
+        __syncthreads();
+        if (tid < R && base + tid < r1) {
+            float y = red[tid];
+            for (int j = 1; j < S; ++j) y = __fadd_rn(y, red[j * R + tid]);
+            int c, ti, ro;
+            locate(base + tid, c, ti, ro);
+            const GemvTensor &T = a.t[ti];
+            const float *X = c ? A.X1 : a.X;
+            const int e1 = T.cp[ro + 1];
+            for (int e = T.cp[ro]; e < e1; ++e) y = __fadd_rn(y, __fmul_rn(T.cv[e], X[T.cc[e]]));
+            T.Y[(size_t)c * A.ldy[ti] + ro] = y;
+        }
+        __syncthreads();
+    }
+}
+
 // workspace layout (bytes, each part 256-aligned): x' of an input op | partials ([nb][rows] per tensor)
 struct GemvWs {
     size_t xv, part, total;
 };
 static size_t al256(size_t n) { return (n + 255) & ~(size_t)255; }
-static GemvWs gemv_ws_layout(const p8_tensor *const *ts, int nt) {
+// nc = 2: the two-column kernel's x' of both columns and partials [column][nb][rows] per tensor
+static GemvWs gemv_ws_layout(const p8_tensor *const *ts, int nt, int nc = 1) {
     const p8_tensor *t = ts[0];
     size_t part = 0;
-    for (int i = 0; i < nt; ++i) part += al256((size_t)ts[i]->nb * ts[i]->rows * 4);
+    for (int i = 0; i < nt; ++i) part += al256((size_t)nc * ts[i]->nb * ts[i]->rows * 4);
     GemvWs w;
     w.xv = 0;
-    w.part = w.xv + al256((size_t)t->K * 4);
+    w.part = w.xv + al256((size_t)nc * t->K * 4);
     w.total = w.part + part;
     return w;
 }
-size_t gemv_workspace(const p8_tensor *t, int64_t) { return gemv_ws_layout(&t, 1).total; }
-size_t gemv_group_workspace(const p8_tensor *const *ts, int nt, int64_t) { return gemv_ws_layout(ts, nt).total; }
+size_t gemv_workspace(const p8_tensor *t, int64_t ncols) { return gemv_ws_layout(&t, 1, ncols >= 2 ? 2 : 1).total; }
+size_t gemv_group_workspace(const p8_tensor *const *ts, int nt, int64_t ncols) {
+    return gemv_ws_layout(ts, nt, ncols >= 2 ? 2 : 1).total;
+}
 
 static cudaError_t launch_pdl(const void *fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void **args) {
     cudaLaunchConfig_t cfg = {};
@@ -1049,6 +1337,9 @@ static int sm_count() {
         cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
         if (v <= 0) v = 148;
         cudaFuncSetAttribute(k_gemv<P8_PROLOGUE_NONE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
+        cudaFuncSetAttribute(k_gemv2<P8_PROLOGUE_NONE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemv2Smem);
+        cudaFuncSetAttribute(k_gemv2<P8_PROLOGUE_RMSNORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemv2Smem);
+        cudaFuncSetAttribute(k_gemv2<P8_PROLOGUE_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemv2Smem);
         cudaFuncSetAttribute(k_gemv_chain<P8_PROLOGUE_NONE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
         cudaFuncSetAttribute(k_gemv<P8_PROLOGUE_RMSNORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
         cudaFuncSetAttribute(k_gemv_chain<P8_PROLOGUE_RMSNORM>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmem);
@@ -1063,7 +1354,7 @@ static int sm_count() {
 // largest CTA cost, cost = units taken + kTableCost per block touched (a table build costs about that many units of
 // work). Greedy filling under a bound, binary search on the bound. Returns the CTAs used; ustart[0 .. used] is filled.
 constexpr int kTableCost = 5;
-static int partition_units(long long units, long long ng, int P, int *ustart) {
+static int partition_units(long long units, long long ng, int P, int *ustart, int tcost = kTableCost) {
     auto fill = [&](long long C, int *out) -> int {  // CTAs needed under bound C (P + 1 if more than P)
         long long s = 0;
         int c = 0;
@@ -1073,10 +1364,10 @@ static int partition_units(long long units, long long ng, int P, int *ustart) {
             long long e = s, cost = 0;
             while (e < units) {
                 const long long blk_end = std::min(units, (e / ng + 1) * ng);
-                if (cost + kTableCost + 1 > C) break;
-                const long long take = std::min(blk_end - e, C - cost - kTableCost);
+                if (cost + tcost + 1 > C) break;
+                const long long take = std::min(blk_end - e, C - cost - tcost);
                 e += take;
-                cost += kTableCost + take;
+                cost += tcost + take;
                 if (e < blk_end) break;
             }
             if (e == s) return P + 1;
@@ -1086,7 +1377,7 @@ static int partition_units(long long units, long long ng, int P, int *ustart) {
         }
         return c;
     };
-    long long lo = (units + P - 1) / P + kTableCost, hi = units + kTableCost * (units / ng + 2);
+    long long lo = (units + P - 1) / P + tcost, hi = units + tcost * (units / ng + 2);
     while (lo < hi) {
         const long long mid = (lo + hi) / 2;
         if (fill(mid, nullptr) <= P) hi = mid;
@@ -1164,21 +1455,115 @@ static p8_status launch_gemv_col(const p8_tensor *const *ts, int nt, const float
     return P8_OK;
 }
 
+// two columns (x at x and x + ldx; outputs at Ys[i] and Ys[i] + ldys[i]): k_gemv2 + k_gemv_reduce2
+static p8_status launch_gemv2(const p8_tensor *const *ts, int nt, const float *x, int64_t ldx, const p8_prologue *pro,
+                              float *const *Ys, const int64_t *ldys, void *ws, size_t ws_bytes, cudaStream_t st) {
+    const p8_tensor *t0 = ts[0];
+    const GemvWs L = gemv_ws_layout(ts, nt, 2);
+    if (!ws || ws_bytes < L.total) return P8_ERR_WORKSPACE;
+    uint8_t *w = static_cast<uint8_t *>(ws);
+    const int nsm = sm_count();
+    const int pk = pro ? pro->kind : P8_PROLOGUE_NONE;
+    GemvArgs ga;
+    memset(&ga, 0, sizeof(ga));
+    ga.ntensors = nt;
+    ga.X = x;
+    ga.ldx = ldx;
+    ga.ic = t0->ic; ga.A = t0->A; ga.cs = t0->cs; ga.K = t0->K; ga.nb = t0->nb; ga.nsl = t0->nsl;
+    if (pk != P8_PROLOGUE_NONE) {
+        ga.pw = pro->w;
+        ga.x2 = pro->x2;
+        ga.eps = pro->eps;
+        ga.xv = reinterpret_cast<float *>(w + L.xv);
+    }
+    size_t poff = L.part;
+    int g0 = 0;
+    for (int i = 0; i < nt; ++i) {
+        const p8_tensor *t = ts[i];
+        GemvTensor &g = ga.t[i];
+        g.M = t->M; g.D = t->D; g.S = t->S; g.prm = t->prm; g.cp = t->cp; g.cc = t->cc; g.cv = t->cv;
+        g.Y = Ys[i];
+        g.part = reinterpret_cast<float *>(w + poff);
+        poff += al256((size_t)2 * t->nb * t->rows * 4);
+        g.rows = t->rows; g.ng = t->ng; g.g0 = g0; g.row0 = ga.rows_total; g.ucls = t->uniform_class;
+        g0 += t->ng;
+        ga.rows_total += t->rows;
+    }
+    ga.ng_total = g0;
+    ga.units = (long long)g0 * t0->nb;
+    const int P = (int)std::min<long long>(ga.units, std::min(nsm, kGemvMaxCtas));
+    const int grid = partition_units(ga.units, g0, P, ga.ustart, 2 * kTableCost);  // two tables per block
+    if (grid < 1 || grid > P) return P8_ERR_ARG;
+    {
+        void *args[] = {&ga};
+        const void *fn = pk == P8_PROLOGUE_RMSNORM ? (const void *)k_gemv2<P8_PROLOGUE_RMSNORM>
+                         : pk == P8_PROLOGUE_SWIGLU  ? (const void *)k_gemv2<P8_PROLOGUE_SWIGLU>
+                                                     : (const void *)k_gemv2<P8_PROLOGUE_NONE>;
+        if (launch_pdl(fn, dim3(grid), dim3(kGemvThreads), kGemv2Smem, st, args) != cudaSuccess) return P8_ERR_CUDA;
+    }
+    Reduce2Args ra;
+    memset(&ra, 0, sizeof(ra));
+    for (int i = 0; i < nt; ++i) {
+        ra.r.t[i] = ga.t[i];
+        ra.ldy[i] = ldys[i];
+    }
+    ra.r.rows_total = ga.rows_total;
+    ra.r.ntensors = nt;
+    ra.r.nb = t0->nb;
+    ra.r.X = pk != P8_PROLOGUE_NONE ? ga.xv : x;
+    ra.X1 = pk != P8_PROLOGUE_NONE ? ga.xv + t0->K : x + ldx;
+    const int rgrid = std::max(1, std::min((2 * ga.rows_total + kRedRowsPerCta - 1) / kRedRowsPerCta, nsm));
+    void *args[] = {&ra};
+    if (launch_pdl((const void *)k_gemv_reduce2, dim3(rgrid), dim3(kRedThreads), 0, st, args) != cudaSuccess) return P8_ERR_CUDA;
+    return P8_OK;
+}
+
+// ncols columns (x_n = X + n ldx, the SwiGLU up at pro->x2 + n ldx; y_i of column n at Ys[i] + n ldys[i]): pairs of
+// columns through the two-column kernel when every tensor is uniform class 3, the rest one column at a time
+p8_status launch_gemv_cols(const p8_tensor *const *ts, int nt, const float *X, int64_t ncols, int64_t ldx, const p8_prologue *pro,
+                           float *const *Ys, const int64_t *ldys, void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (nt < 1 || nt > kMaxGroup) return P8_ERR_ARG;
+    const p8_tensor *t0 = ts[0];
+    bool two = ncols >= 2 && (ldx & 3) == 0;
+    for (int i = 0; i < nt; ++i) {
+        if (ts[i]->K != t0->K || ts[i]->act_hash != t0->act_hash) return P8_ERR_ARG;
+        if (ts[i]->uniform_class != 3) two = false;
+    }
+    (void)sm_count();
+    int64_t n = 0;
+    for (; two && n + 1 < ncols; n += 2) {
+        p8_prologue pn;
+        if (pro) {
+            pn = *pro;
+            if (pn.x2) pn.x2 += n * ldx;
+        }
+        float *Yn[kMaxGroup];
+        for (int i = 0; i < nt; ++i) Yn[i] = Ys[i] + n * ldys[i];
+        const p8_status s = launch_gemv2(ts, nt, X + n * ldx, ldx, pro ? &pn : nullptr, Yn, ldys, ws, ws_bytes, st);
+        if (s) return s;
+    }
+    for (; n < ncols; ++n) {
+        p8_prologue pn;
+        if (pro) {
+            pn = *pro;
+            if (pn.x2) pn.x2 += n * ldx;
+        }
+        float *Yn[kMaxGroup];
+        for (int i = 0; i < nt; ++i) Yn[i] = Ys[i] + n * ldys[i];
+        const p8_status s = launch_gemv_col(ts, nt, X + n * ldx, Yn, ws, ws_bytes, st, nullptr, nullptr, pro ? &pn : nullptr);
+        if (s) return s;
+    }
+    return P8_OK;
+}
+
 p8_status launch_gemv_group(const p8_tensor *const *ts, int nt, const float *X, int64_t ncols, int64_t ldx, float *const *Ys,
                             const int64_t *ldys, void *ws, size_t ws_bytes, cudaStream_t st) {
     if (nt < 1 || nt > kMaxGroup) return P8_ERR_ARG;
     const p8_tensor *t0 = ts[0];
     for (int i = 0; i < nt; ++i)  // tensors of one launch share x and its table: same K, column scales, signs and codebook
         if (ts[i]->K != t0->K || ts[i]->act_hash != t0->act_hash) return P8_ERR_ARG;
-    (void)sm_count();
-    // columns run one after another; ncols > 1 is the batched fallback
-    for (int64_t n = 0; n < ncols; ++n) {
-        float *Yn[kMaxGroup];
-        for (int i = 0; i < nt; ++i) Yn[i] = Ys[i] + n * ldys[i];
-        p8_status s = launch_gemv_col(ts, nt, X + n * ldx, Yn, ws, ws_bytes, st);
-        if (s) return s;
-    }
-    return P8_OK;
+    // ncols > 1 (below the GEMM's column count): pairs of columns through the two-column kernel
+    return launch_gemv_cols(ts, nt, X, ncols, ldx, nullptr, Ys, ldys, ws, ws_bytes, st);
 }
 
 p8_status launch_gemv_group_pro(const p8_tensor *const *ts, int nt, const float *x, const p8_prologue *pro, float *const *Ys,
