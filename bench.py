@@ -18,9 +18,9 @@ CUDA graph and replayed per step. Attention, norms and the LM head are not part 
   prefill   (1 GPU) the batched product: 512 tokens through all 224 projections (tcgen05 GEMM), the projections on
             one input as grouped products (p8_mul_mat_group), TFLOP/s against MEASURED_PEAKS.json bf16_tflops; the
             same pass as separate p8_mul_mat calls beside it
-  batched_decode  (1 GPU) bs = 2, 3, 8, 32, 64 sequences stepping together through the same chain, every group call the
-            grouped batched product (bs 2-3: the two-column batch-1 GEMV, weights decoded once for two sequences; from bs
-            4 the split-K tcgen05 GEMM): tok/s per bs
+  batched_decode  (1 GPU) bs = 2, 3, 4, 8, 32, 64 sequences stepping together through the same chain, every group call the
+            grouped batched product (bs 2-5: the two-column batch-1 GEMV in pairs, weights decoded once per two
+            sequences; from bs 6 the split-K tcgen05 GEMM): tok/s per bs
   layer_prologues (1 GPU) the chain with each layer's input ops (RMSNorm x weight, SwiGLU) fused into the GEMV's
             activation prep, against the same ops as separate torch kernels
 
@@ -639,6 +639,9 @@ def run_b200(args, rank, world, local_rank):
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local_rank) as clk:
+        # the sampler thread is polling before the timed launches start, so its start-up (NVML calls under the GIL)
+        # cannot delay the enqueueing of the first replays
+        time.sleep(0.05)
         e0.record(stream)
         with torch.cuda.stream(stream):
             for _ in range(args.steps):
@@ -795,14 +798,14 @@ def run_b200(args, rank, world, local_rank):
             layer[name] = el0.elapsed_time(el1) / 1e3 / nrep
             del gl
     # ---- (1 GPU) batched decode: bs sequences step together through the same projection chain, each group of
-    # projections on one input (q/k/v, o, gate/up, down) one grouped batched product (p8_mul_mat_group: bs 2-3 the
-    # two-column batch-1 GEMV, from bs 4 one activation prep, then the split-K tcgen05 GEMM per tensor); one graph per
-    # bs, device-timed
+    # projections on one input (q/k/v, o, gate/up, down) one grouped batched product (p8_mul_mat_group: bs 2-5 the
+    # two-column batch-1 GEMV in pairs, from bs 6 one activation prep, then the split-K tcgen05 GEMM per tensor); one
+    # graph per bs, device-timed
     groups = (("q", "k", "v"), ("o",), ("gate", "up"), ("down",))
     batched = None
     if world == 1 and not args.no_batched:
         batched = {}
-        for bs in (2, 3, 8, 32, 64):
+        for bs in (2, 3, 4, 8, 32, 64):
             bws = torch.empty(max(group_workspace_size([ts[n] for n in g], bs) for ts in layers for g in groups),
                               dtype=torch.uint8, device=dev)
             bx = {"x": torch.randn(bs, h, device=dev)}
@@ -1005,8 +1008,8 @@ def run_b200(args, rank, world, local_rank):
                       "weights", **model_dec}
     if batched is not None:
         line["batched_decode"] = {
-            "kernel": "p8_mul_mat_group per input: bs 2-3 k_gemv2 + k_gemv_reduce2 (two columns per launch, a third column "
-                      "through k_gemv); from bs 4 k_gx_max + k_gx_prep once, then k_gemm + k_splitk_reduce per projection",
+            "kernel": "p8_mul_mat_group per input: bs 2-5 k_gemv2 + k_gemv_reduce2 (two columns per launch, an odd column "
+                      "through k_gemv); from bs 6 k_gx_max + k_gx_prep once, then k_gemm + k_splitk_reduce per projection",
             "per_bs": {str(bs): {"ms_per_step": round(t * 1e3, 3), "tok_s": round(v, 1),
                                  "weight_gbs": round(bytes_token / t / 1e9, 1)} for bs, (t, v) in batched.items()}}
     if layer is not None:

@@ -172,9 +172,10 @@ size_t p8_noalloc_scratch_bytes(void);
 p8_status p8_mul_mat_vec_noalloc(const p8_tensor *t, const float *x, float *y, void *stream);
 
 /* Y[n][ldy] (rows per column) = W X[n][ldx], n < ncols. ncols > 1: batched decode / prefill. Replaces
- * ggml_cuda_f44_mul_mat_q8 (CU:1014-1054). ncols >= 4 runs the tensor-core product (fp16 operands, fp32 accumulate,
- * within 1e-3 of the exact product); 2-3 columns run the batch-1 GEMV per column. Deterministic. Calls on the same
- * workspace must not overlap on the GPU. */
+ * ggml_cuda_f44_mul_mat_q8 (CU:1014-1054). From 4 columns (6 for a tensor whose tiles are all class 3) the
+ * tensor-core product runs (fp16 operands, fp32 accumulate, within 1e-3 of the exact product); below that the
+ * batch-1 GEMV, two columns per launch for class-3 tensors (the weights decoded once per pair; each column equal to
+ * the one-column call bit for bit). Deterministic. Calls on the same workspace must not overlap on the GPU. */
 p8_status p8_mul_mat(const p8_tensor *t, const float *X, int64_t ncols, int64_t ldx, float *Y, int64_t ldy,
                      void *workspace, size_t workspace_bytes, void *stream);
 

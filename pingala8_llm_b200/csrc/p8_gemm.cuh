@@ -57,6 +57,9 @@ constexpr int kGemmSmemMax = 227 * 1024;            // shared memory per CTA (sm
 constexpr int kGemmSmemDyn = kGemmSmemMax - 1024;   // dynamic part (the kernel's static shared memory takes 1 KB)
 constexpr uint32_t kGemmPolls = 1u << 22;
 constexpr int kGemmMinCols = 4;                     // below this the per-column table GEMV is faster (measured crossover)
+constexpr int kGemmMinColsC3 = 6;                   // uniform class-3 tensors: below this the two-column table GEMV (pairs)
+                                                    // is faster (Llama-3.1-8B decode chain: bs 4 3.4 vs 5.1 ms, bs 5 4.7 vs
+                                                    // 5.1, bs 6 5.1 vs 5.1, bs 7 6.4 vs 5.2 ms per step)
 constexpr int kGemmStagedMinCols = 64;              // from here (single split) outputs go out in sorted-row order first
 
 struct GemmArgs {
@@ -855,7 +858,7 @@ static GemmPlan gemm_plan(const p8_tensor *t, int64_t ncols, bool pro = false, i
 }
 
 bool gemm_supported(const p8_tensor *t, int64_t ncols) {
-    return ncols >= kGemmMinCols && t->K <= 65536 && t->rsc != nullptr &&
+    return ncols >= (t->uniform_class == 3 ? kGemmMinColsC3 : kGemmMinCols) && t->K <= 65536 && t->rsc != nullptr &&
            (size_t)gemm_plan(t, ncols).smem <= (size_t)kGemmSmemDyn;
 }
 
