@@ -1053,6 +1053,7 @@ CASE_GROUPS = {  # Llama-3.1-8B: (rows, K) per tensor of a group that reads one 
 def run_case(args):
     """--case gemv:GROUP          the grouped batch-1 GEMV (k_gemv + k_gemv_reduce), --iters calls rotating over --copies
                                   distinct weight copies (copies > 1 read DRAM rather than L2), optionally --graph
+       --case gemv2:GROUP         the grouped product of two columns (two sequences: k_gemv2 + k_gemv_reduce2)
        --case gemm:GROUP:NCOLS    the batched product per tensor (tcgen05 GEMM), or :grouped for p8_mul_mat_group
        --case get_rows:GROUP:N    p8_get_rows of N random rows of each tensor of the group
        --case dequant:GROUP       p8_dequant_f32 of each tensor of the group
@@ -1083,6 +1084,15 @@ def run_case(args):
             mul_mat_vec_group(copies[i % len(copies)], x, outs=outs, workspace=ws, stream=stream)
         nbytes = sum((r // 32) * (k // 256) * (68 + 2048) for r, k in shapes)
         unit = lambda us: f"{nbytes / us / 1e3:.1f} GB/s (algorithmic, class 3)"  # noqa: E731
+    elif kind == "gemv2":
+        X = torch.randn(2, K, device="cuda")
+        outs = [torch.empty(2, r, device="cuda") for r, _ in shapes]
+        ws = torch.empty(max(group_workspace_size(ts, 2) for ts in copies), dtype=torch.uint8, device="cuda")
+
+        def once(i, stream=None):
+            mul_mat_group(copies[i % len(copies)], X, outs=outs, workspace=ws, stream=stream)
+        nbytes = sum((r // 32) * (k // 256) * (68 + 2048) for r, k in shapes)
+        unit = lambda us: f"{nbytes / us / 1e3:.1f} GB/s of weights (algorithmic, class 3, read once for both columns)"  # noqa: E731
     elif kind == "gemm":
         ncols = int(rest[1])
         grouped = len(rest) > 2 and rest[2] == "grouped"
