@@ -10,7 +10,7 @@ CUDA graph and replayed per step. Attention, norms and the LM head are not part 
 
   value     tokens/s with inputs resident in HBM (device-timed with CUDA events, max over ranks)
   e2e       the same through the public op API with a pinned-host input vector copied in and the final output copied
-            out every step
+            out every step, the host waiting for each step's output before it starts the next
   roofline  the dominant call type (p8_mul_mat_vec_group = k_gemv + k_gemv_reduce): algorithmic bytes / per-call
             duration, timed with CUDA events around a graph of that call type's 32 per-layer calls, against
             MEASURED_PEAKS.json hbm_gbs; traffic = DRAM bytes of the same call from an ncu capture
@@ -662,10 +662,11 @@ def run_b200(args, rank, world, local_rank):
     e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2.record(stream)
     with torch.cuda.stream(stream):
-        for _ in range(args.steps):
+        for _ in range(args.steps):  # the host waits for each step's output, as a decode loop reading it would
             buf["x"].copy_(x_host, non_blocking=True)
             graph.replay()
             y_host.copy_(buf["down"], non_blocking=True)
+            stream.synchronize()
     e3.record(stream)
     torch.cuda.synchronize()
     barrier()
