@@ -989,8 +989,9 @@ def run_b200(args, rank, world, local_rank):
                                  "per_call_type": per_call}
     if t_other is not None and other == "chain":
         line["chain_decode"] = {"tok_s": round(args.steps / t_other, 3), "ms_per_step": round(1e3 * t_other / args.steps, 4),
-                                "kernels": f"k_chain (p8_chain_run): {len(chains)} launches per token, the projections between two "
-                                           "attention points in one launch with one grid barrier per projection",
+                                "kernels": f"p8_chain_run: {len(chains)} chains per token (the projections between two attention "
+                                           "points), each projection one k_gemv_chain launch that reads its input from the "
+                                           "previous one's partials, one k_gemv_reduce after a chain's last projection",
                                 "hbm_gbs_step": round(bytes_token / (t_other / args.steps) / 1e9, 1)}
     if tp_par is not None:
         line["tp_parity"] = {"what": "one layer's q, gate (column-parallel) and o, down (row-parallel) sharded by the plan "

@@ -1353,7 +1353,9 @@ static int sm_count() {
 // Cut the block-major list of `units` units (ng per block) into at most P contiguous CTA ranges that minimise the
 // largest CTA cost, cost = units taken + kTableCost per block touched (a table build costs about that many units of
 // work). Greedy filling under a bound, binary search on the bound. Returns the CTAs used; ustart[0 .. used] is filled.
-constexpr int kTableCost = 5;
+// The weight was measured on the Llama-3.1-8B decode step: 5 -> 763, 8 -> 789, 11 -> 788, 14 -> 783 tok/s (the small
+// q/k/v and o calls gain most: fewer CTAs build two tables).
+constexpr int kTableCost = 8;
 static int partition_units(long long units, long long ng, int P, int *ustart, int tcost = kTableCost) {
     auto fill = [&](long long C, int *out) -> int {  // CTAs needed under bound C (P + 1 if more than P)
         long long s = 0;
