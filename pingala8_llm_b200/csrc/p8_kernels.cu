@@ -348,7 +348,8 @@ __device__ __forceinline__ float chain_row_value(const ChainSrc &T, int ro, floa
 
 // x'[i] = (x[i] * scale) * w[i], scale = 1 / sqrt(mean(x^2) + eps): ggml's rms_norm (sum of squares, mean by float
 // division, 1 / sqrtf) followed by the weight multiply. Every CTA sums the whole vector in the same fixed order
-// (per-thread strided float4 sums, then a shared-memory tree over the CTA's threads), so all CTAs get the same scale.
+// (per-thread strided float4 sums, a butterfly over each warp, then the warp sums in warp order: one barrier), so all
+// CTAs get the same scale.
 template <int NT>
 __device__ __forceinline__ float rms_scale(const float *x, int K, float eps, float *red) {
     const int tid = threadIdx.x;
@@ -360,14 +361,14 @@ __device__ __forceinline__ float rms_scale(const float *x, int K, float eps, flo
         ss = __fmaf_rn(v.z, v.z, ss);
         ss = __fmaf_rn(v.w, v.w, ss);
     }
-    red[tid] = ss;
-    __syncthreads();
 #pragma unroll
-    for (int h = NT / 2; h > 0; h >>= 1) {
-        if (tid < h) red[tid] = __fadd_rn(red[tid], red[tid + h]);
-        __syncthreads();
-    }
-    const float mean = __fdiv_rn(red[0], (float)K);
+    for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));  // every lane: the warp sum
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    float t = red[0];
+#pragma unroll
+    for (int w = 1; w < NT / 32; ++w) t = __fadd_rn(t, red[w]);
+    const float mean = __fdiv_rn(t, (float)K);
     return __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(mean, eps)));
 }
 
