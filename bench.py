@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Pingala-8 batch-1 decode throughput on B200 (and the reference CPU path on the same host).
 
-Headline workload (BASELINE.json metric "decode tok/s bs1 (Llama-3.1-8B shape, 2-bit)"): one decode token through
+Headline workload (the metric "decode tok/s bs1 (Llama-3.1-8B shape, 2-bit)"): one decode token through
 every Pingala-8 projection of a Llama-3.1-8B-architecture model -- 32 layers x {q, k, v, o, gate, up, down}
 (224 GEMVs, 1.80 GB of class-3 slots: seeded random valid codes, shapes of the real model). The projections are
 chained on the device (x -> q,k,v; q-out -> o; o-out -> gate,up; gate-out -> down; down-out -> next layer), launched
@@ -41,7 +41,7 @@ REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, REPO)
 
 LLAMA8B = dict(name="llama3.1-8b", layers=32, hidden=4096, ffn=14336, q=4096, kv=1024)
-QWEN14B = dict(name="qwen3-14b", layers=40, hidden=5120, ffn=17408, q=5120, kv=1024)
+QWEN14B = dict(name="qwen3-14b", layers=40, hidden=5120, ffn=17408, q=5120, kv=1024)  # benchmark config C5
 # a small layer whose o split at 2 ranks is not whole 256-column blocks (5 query heads = 640 columns per rank): the
 # shared-boundary-block path that Qwen3-14B takes at 8 ranks, checked at 2
 UNALIGNED2 = dict(name="10-head-2-kv (o split 640 | 640)", layers=1, hidden=1280, ffn=2560, q=1280, kv=256)
@@ -385,7 +385,7 @@ def tp_parity(model, world, rank, dev, comm):
 
 
 def tp_model_decode(model, args, rank, world, dev, comm, stream):
-    """BASELINE config C5 on this model: every projection split over the ranks by tp.layer_plan (q/k/v/gate/up
+    """Benchmark config C5 on this model: every projection split over the ranks by tp.layer_plan (q/k/v/gate/up
     column-parallel, o/down row-parallel; an o split that is not whole 256-column blocks shares its boundary block,
     the rank's input zero-padded), each rank's shards synthesised directly (seeded random codes). bs 1: the grouped
     GEMV chain as a CUDA graph, row-parallel sums inside the GEMV over peer memory (comm) or NCCL; bs 16: the batched

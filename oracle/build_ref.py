@@ -8,7 +8,7 @@
    The new-file hunks are written out (leading '+' stripped) into oracle/_ref/ and compiled with oracle/ref_harness.c
    into two shared objects, one per ISA level, so the box that runs the tests can pick what its CPU supports:
      oracle/_ref/libp8ref_vnni.so (-mavx2 -mfma -mf16c -mavxvnni)   oracle/_ref/libp8ref_avx2.so (-mavx2 -mfma -mf16c)
-   Needs /root/reference (present only in the build container); when it is absent the step is skipped and the
+   Needs the reference checkout (P8_REFERENCE; present only in the build container); when it is absent the step is skipped and the
    prebuilt oracle/_ref/ (git-ignored, shipped with the working tree) is used as is.
 3. oracle/_ref/libp8ref_gpu.so -- the reference's OWN batch-1 GEMV kernels (k_vr, k_vr_qx_real) cut from vr49.cuh by
    line markers (GPU_CUTS below) and compiled for sm_100a with the launcher oracle/ref_gpu_harness.cu: the same-box
@@ -106,7 +106,7 @@ def cut_between(txt, start, end):
 
 def build_ref_gpu(reference):
     """oracle/_ref/libp8ref_gpu.so: the reference's own k_vr + k_vr_qx_real (cut from the patch text) behind the small
-    launcher oracle/ref_gpu_harness.cu, for sm_100a. Needs /root/reference; skipped (prebuilt kept) without it."""
+    launcher oracle/ref_gpu_harness.cu, for sm_100a. Needs the reference checkout; skipped (prebuilt kept) without it."""
     patch = os.path.join(reference, "patches/llama_cuda_vs_7ac59a6.patch")
     if not os.path.exists(patch):
         print(f"build_ref: {patch} not present; keeping prebuilt oracle/_ref/libp8ref_gpu.so", flush=True)

@@ -1,7 +1,7 @@
 """Model-level decode (a llama-style model with every projection Pingala-8, through the C ABI) against a plain fp32
 torch forward of the same architecture on the CPU oracle's dequantised weights.
 
-The model is the Qwen3-4B architecture of BASELINE config C2 (hidden 2560, FFN 9728, 32 query / 8 KV heads, head_dim
+The model is the Qwen3-4B architecture of benchmark config C2 (hidden 2560, FFN 9728, 32 query / 8 KV heads, head_dim
 128, q/k RMSNorm, RoPE theta 1e6) with 2 of its 36 layers and an 8192-token vocabulary, so that the oracle's CPU dequant
 and the fp32 reference stay small. The reference llama.cpp runtime is not available; the fp32 forward is its restatement.
 Teacher forcing: the reference runs on the decoder's own token sequence, and the comparison is per position. Bars: the

@@ -1,6 +1,6 @@
 """GPU parity of the batched product (tcgen05 GEMM: p8_mul_mat with ncols >= 4) through the C ABI.
 
-Bar: within 1e-3 relative L2 of the reference's CPU result (fp32 accumulate). The GEMM's
+Bar (the path's stated target): within 1e-3 relative L2 of the reference's CPU result (fp32 accumulate). The GEMM's
 operands are fp16 (weights int * S, activations H256(x sgn/c) / 16, each with a power-of-two range scale), so its
 error against the exact product is fp16 rounding, about 3e-4; the tests assert the 1e-3 bar.
 """
@@ -123,7 +123,7 @@ def test_gemm_strides_and_extreme_token_scales():
 
 @pytest.mark.parametrize("label,rows,K,ncols", [("llama_gate", 14336, 4096, 512), ("llama_down", 4096, 14336, 256)])
 def test_full_size_gemm_unit_vectors(label, rows, K, ncols):
-    """Size-independent property at the BASELINE shapes: a batch of unit vectors e_k gives the columns W[:, k] of the
+    """Size-independent property at the benchmark shapes: a batch of unit vectors e_k gives the columns W[:, k] of the
     bit-exact dequantized weight (up to the operands' fp16 rounding)."""
     s = synth.make_slot_device(rows, K, seed=rows ^ K)
     t = P8Tensor(s, K, rows)
@@ -140,7 +140,7 @@ def test_full_size_gemm_unit_vectors(label, rows, K, ncols):
 @pytest.mark.parametrize("label,rows,K,ncols", [("llama_gate", 14336, 4096, 2048), ("llama_gate", 14336, 4096, 512),
                                                 ("llama_down", 4096, 14336, 2048), ("llama_down", 4096, 14336, 512)])
 def test_full_size_gemm_dense_tokens(label, rows, K, ncols):
-    """BASELINE C3 at its token counts with dense N(0, 1) activations (every token accumulates over all of K):
+    """Benchmark config C3 at its token counts with dense N(0, 1) activations (every token accumulates over all of K):
     against the product with the bit-exact dequantized weight in fp64 on a subset of 1024 rows, and the first 8
     tokens against the reference's own CPU core (oracle/_ref, x16 batch path) on every row"""
     s = synth.make_slot_device(rows, K, seed=rows + K + ncols, nd=0)

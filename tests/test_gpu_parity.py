@@ -1,6 +1,6 @@
 """GPU parity: every CUDA entry point against the CPU oracle / the reference's stored outputs, through the C ABI.
 
-Bars: integer decode and f32 dequant BIT-EXACT vs the reference CPU path; GEMV / batched
+Bars (the path's stated targets): integer decode and f32 dequant BIT-EXACT vs the reference CPU path; GEMV / batched
 product within 1e-3 relative L2 of the reference's x16 CPU vec_dot (the GEMV's integer sums are exact, so the
 measured gap is float rounding, ~1e-7; the tests assert 1e-5 and the 1e-3 bar).
 """
@@ -104,7 +104,7 @@ def test_gemv_deterministic_and_graph_capturable(prepared):
     assert torch.equal(out, y1)
 
 
-# --------------------------------------------------------------------------- BASELINE shapes (synthetic, full size)
+# --------------------------------------------------------------------------- benchmark shapes (synthetic, full size)
 SHAPES = [
     ("c1_ffn_up", 9728, 2560),          # config C1 (Qwen3-4B ffn_up)
     ("llama_q", 4096, 4096),
@@ -117,7 +117,7 @@ SHAPES = [
 
 @pytest.mark.parametrize("label,rows,K", SHAPES)
 def test_full_size_gemv_vs_oracle(label, rows, K):
-    """BASELINE shapes at full size against the restated oracle AND the reference's own CPU core (oracle/_ref,
+    """Benchmark shapes at full size against the restated oracle AND the reference's own CPU core (oracle/_ref,
     vrc_tg with x16 activations) on the same slot and input"""
     s = synth.make_slot(rows, K, seed=rows + K, nd=37)
     t = P8Tensor(s, K, rows)
