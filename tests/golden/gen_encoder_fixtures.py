@@ -1,7 +1,7 @@
 """Generate tests/golden/encoder_fixtures.npz with the REFERENCE's own trellis encoder (research/detail/r48k.py encode,
 r48k.py:105, with vit_k r48k.py:57 and zero_ldlq r48k.py:97), run on CPU in the build container.
 
-Run here only (it imports the reference checkout):  python tests/golden/gen_encoder_fixtures.py  /root/reference
+Run here only (it imports the reference checkout):  python tests/golden/gen_encoder_fixtures.py  REFERENCE_CHECKOUT
 Settings are the production ones the golden slots use: R48K_NS=8 (Pingala-8 gana states) and
 R48K_SHIFTS=0,0,0,0,2,3,2,4/0,0,0,0,0,0,0,2, tables research/work/r48k3/tables_vrc.pt (the codebook shipped in
 pingala8_llm_b200/tables_pingala8.bin), trellis mode (tr = True).

@@ -4,7 +4,7 @@ Run in the build container only (it imports research/detail/*.py from the refere
 reference CPU core built by oracle/build_ref.py). The outputs are committed; nothing at test time reads the
 reference checkout.
 
-Pipeline per fixture (the reference's own steps, SURVEY-level summary in DESIGN.md):
+Pipeline per fixture (the reference's own steps):
   weights  W = N(0, 0.02^2) from numpy default_rng(seed); entries with rand < 1e-3 replaced by standard_t(3) * 0.1
   encode   r48k.k_tensor (research/detail/r48k.py:213) with R48K_NS=8, R48K_SHIFTS=0,0,0,0,2,3,2,4/0,0,0,0,0,0,0,2,
            c = 1 (uniform importance matrix), H = I, damp 0.1, alpha 1.05, tables research/work/r48k3/tables_vrc.pt
@@ -17,7 +17,7 @@ Golden values stored: the slot bytes, seeded activations, the reference CPU core
 (oracle/_ref), and SHA-256 digests of the reference Python decoders' outputs (r51_transcode.cpu_vr_port over the
 kernel bytes = v*S in sorted rows; r48k.unpack_blob + ifw/c = original-domain weights).
 
-usage: python tests/golden/gen_fixtures.py [--reference /root/reference]
+usage: python tests/golden/gen_fixtures.py [--reference REFERENCE_CHECKOUT]
 """
 import argparse
 import hashlib
