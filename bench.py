@@ -582,8 +582,8 @@ def run_b200(args, rank, world, local_rank):
         return x
 
     launches_ops = 2 * len(groups) * model["layers"]  # k_gemv + k_gemv_reduce per group
-    # ---- (1 GPU) the same chain as chained launches (p8_chain: one persistent launch runs several projections with
-    # one grid barrier each). Launches split where attention sits in a real decoder layer (between q/k/v and o):
+    # ---- (1 GPU) the same chain as chained launches (p8_chain: each projection one k_gemv_chain launch that reads
+    # the previous one's partials). Chains split where attention sits in a real decoder layer (between q/k/v and o):
     # [q/k/v 0], [o L-1, gate/up L-1, down L-1, q/k/v L] for L = 1..31, [o 31, gate/up 31, down 31]
     chains = None
     if world == 1 and (args.decode == "chain" or not args.no_chain):

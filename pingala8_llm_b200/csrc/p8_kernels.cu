@@ -16,7 +16,7 @@
 namespace p8 {
 
 // device-side error word (that launch's results are invalid): bit 2 GEMM pipeline wait timed out, bit 3 row-parallel
-// exchange wait timed out, bit 4 exchange entry with a foreign tag, bit 5 chain-kernel grid barrier (bits 0-1 unused)
+// exchange wait timed out, bit 4 exchange entry with a foreign tag (bits 0, 1 and 5 unused)
 __device__ unsigned int g_p8_device_error = 0;
 
 // ================================================================================================================

@@ -233,13 +233,14 @@ def mul_mat_group(tensors, X, outs=None, workspace=None, stream=None, norm_weigh
 
 
 class Chain:
-    """A run of batch-1 projections in one persistent launch (p8_chain_*): each step is a dict
+    """A run of batch-1 projections as chained launches (p8_chain_*): each step one GEMV launch that reads its input
+    straight from the previous step's partial sums, one row reduce after the last step. Each step is a dict
         tensors      list of P8Tensor reading the same input (1..4; q/k/v, gate/up)
         x            float32 CUDA [K]: any buffer, or exactly an output of the previous step (read from its partials)
         outs         float32 CUDA [rows_i] per tensor
         norm_weight  RMSNorm weight [K] (with eps), or up: SwiGLU's up [K] (may be the previous step's other output)
         res          optional list of residuals [rows_i] (or None entries) added to the outputs
-    Buffers are fixed at creation (like a captured graph); run() enqueues one launch and is capturable. Results equal
+    Buffers are fixed at creation (like a captured graph); run() enqueues the chain's launches and is capturable. Results equal
     the separate mul_mat_vec_group calls up to float rounding."""
 
     def __init__(self, steps):
