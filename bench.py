@@ -17,7 +17,8 @@ CUDA graph and replayed per step. Attention, norms and the LM head are not part 
   cpu_baseline  the reference's own CPU core (oracle/_ref, x16 vrc_tg) on one layer's 7 GEMVs, all host threads
   prefill   (1 GPU) the batched product: 512 tokens through all 224 projections (tcgen05 GEMM), the projections on
             one input as grouped products (p8_mul_mat_group), TFLOP/s against MEASURED_PEAKS.json bf16_tflops; the
-            same pass as separate p8_mul_mat calls beside it
+            same pass as separate p8_mul_mat calls beside it; c3_per_gemm: each of the 7 projections alone at 512 and
+            2,048 tokens
   batched_decode  (1 GPU) bs = 2, 3, 4, 8, 32, 64 sequences stepping together through the same chain, every group call the
             grouped batched product (bs 2-5: the two-column batch-1 GEMV in pairs, weights decoded once per two
             sequences; from bs 6 the split-K tcgen05 GEMM): tok/s per bs
@@ -882,7 +883,38 @@ def run_b200(args, rank, world, local_rank):
             t_pf[name] = ep0.elapsed_time(ep1) / 1e3 / npass
             del gp
         flop = sum(2.0 * r * k * ntok for _, r, k in shapes) * model["layers"]
-        prefill = (ntok, t_pf["grouped"], flop, t_pf["separate"])
+        # config C3 as stated: each projection of layer 0 alone (p8_mul_mat) at 512 and 2,048 tokens, a graph of 5
+        # calls replayed twice, device-timed (one tensor's weights, so they may stay in L2: this is the GEMM alone)
+        c3 = {}
+        for n3 in (512, 2048):
+            X3 = {K: torch.randn(n3, K, device=dev) for K in {tt.K for tt in layers[0].values()}}
+            ws3 = torch.empty(max(group_workspace_size([tt], n3) for tt in layers[0].values()), dtype=torch.uint8, device=dev)
+            per = {}
+            for nm, tt in layers[0].items():
+                Y3 = torch.empty(n3, tt.rows, device=dev)
+                with torch.cuda.stream(stream):
+                    tt.mul_mat(X3[tt.K], out=Y3, workspace=ws3, stream=stream)
+                torch.cuda.synchronize()
+                g3 = torch.cuda.CUDAGraph()
+                with torch.cuda.stream(stream):
+                    with torch.cuda.graph(g3, stream=stream):
+                        for _ in range(5):
+                            tt.mul_mat(X3[tt.K], out=Y3, workspace=ws3, stream=stream)
+                    g3.replay()
+                torch.cuda.synchronize()
+                e30, e31 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e30.record(stream)
+                with torch.cuda.stream(stream):
+                    for _ in range(2):
+                        g3.replay()
+                e31.record(stream)
+                torch.cuda.synchronize()
+                t3 = e30.elapsed_time(e31) / 1e3 / 10
+                per[nm] = {"us": round(t3 * 1e6, 1), "tflops": round(2.0 * tt.rows * tt.K * n3 / t3 / 1e12, 1)}
+                del g3, Y3
+            c3[str(n3)] = per
+            del X3, ws3
+        prefill = (ntok, t_pf["grouped"], flop, t_pf["separate"], c3)
     # ---- (1 GPU) model-level decode: a random-init model of the named architecture with every projection Pingala-8
     # (pingala8_llm_b200.decode: fused input ops, torch SDPA attention on a static KV cache, Q8_0 embeddings and head),
     # a seeded prompt through the batched product, then greedy tokens as graph replays; device-timed
@@ -1021,7 +1053,7 @@ def run_b200(args, rank, world, local_rank):
             "fused": "p8_mul_mat_vec_group_ex (input op in k_gemv's table build)",
             "torch_ops": "separate torch elementwise/reduction kernels, then p8_mul_mat_vec_group"}
     if prefill is not None:
-        ntok, t_pass, flop, t_sep = prefill
+        ntok, t_pass, flop, t_sep, c3 = prefill
         bf16_peak = measured_bf16_tflops()
         line["prefill"] = {"tokens": ntok, "ms": round(t_pass * 1e3, 3), "tok_s": round(ntok / t_pass, 1),
                            "kernel": "p8_mul_mat_group per input (k_gx_max + k_gx_prep once; k_gemm, tcgen05 kind::f16, "
@@ -1031,7 +1063,9 @@ def run_b200(args, rank, world, local_rank):
                            "tflops": round(flop / t_pass / 1e12, 1), "bound": "tensor", "peak_tflops": bf16_peak,
                            "frac": round(flop / t_pass / 1e12 / bf16_peak, 4),
                            "peak_source": "MEASURED_PEAKS.json bf16_tflops (cuBLAS bf16 burst; the GEMM runs fp16 operands at the same rate)",
-                           "config": "512 tokens x 224 projections (32 layers), distinct weights, inputs resident"}
+                           "config": "512 tokens x 224 projections (32 layers), distinct weights, inputs resident",
+                           "c3_per_gemm": {"what": "config C3: each projection alone (p8_mul_mat), per call; tflops of "
+                                                   "2 x rows x K x tokens", "tokens": c3}}
     if world == 1 and not args.no_cpu:
         tok_time, cores, isa = cpu_reference_token(model, reps=5, warmup=1)
         line["cpu_baseline"] = {"value": round(1.0 / tok_time, 4), "unit": "tok/s", "cores": cores, "kind": "reference",
