@@ -159,18 +159,23 @@ TRAFFIC_BYTES = {"gate+up": 30377728 + 3584 + 2026240}
 
 
 def measured_bf16_tflops():
+    """(peak, source): MEASURED_PEAKS.json bf16_tflops, else the pool's earlier measurement 1,590 TFLOP/s"""
     p = os.path.join(REPO, "MEASURED_PEAKS.json")
     if os.path.exists(p):
-        return json.load(open(p)).get("bf16_tflops", 1590.0)
-    return 1590.0
+        v = json.load(open(p)).get("bf16_tflops")
+        if v:
+            return float(v), "measured: MEASURED_PEAKS.json bf16_tflops (cuBLAS bf16 burst)"
+    return 1590.0, "fallback: 1,590 TFLOP/s, an earlier cuBLAS bf16 burst measurement on this pool (MEASURED_PEAKS.json absent)"
 
 
 def measured_peaks():
+    """(peak, source): MEASURED_PEAKS.json hbm_gbs, else the pool's earlier measurement 6,650 GB/s"""
     p = os.path.join(REPO, "MEASURED_PEAKS.json")
     if os.path.exists(p):
-        d = json.load(open(p))
-        return d.get("hbm_gbs", 6650.0), "measured"
-    return 6650.0, "fallback"
+        v = json.load(open(p)).get("hbm_gbs")
+        if v:
+            return float(v), "measured: MEASURED_PEAKS.json hbm_gbs (burst copy)"
+    return 6650.0, "fallback: 6,650 GB/s, an earlier copy measurement on this pool (MEASURED_PEAKS.json absent)"
 
 
 # ------------------------------------------------------------------------------------------------ CPU reference leg
@@ -984,17 +989,17 @@ def run_b200(args, rank, world, local_rank):
     if args.decode == "chain" and chains is not None:  # the step is nothing but chain launches: the kernel's bytes and time are the step's
         dom_s = t_dev / args.steps / len(chains)
         dom_bytes = bytes_token / len(chains)
-        roof = {"kernel": f"k_chain (p8_chain_run: {len(chains)} launches per token, 4 projections per launch in layers "
-                          f"1-31)", "bound": "hbm", "achieved": round(dom_bytes / dom_s / 1e9, 1), "peak": peak,
+        roof = {"kernel": f"p8_chain_run ({len(chains)} chains per token, 4 projections per chain in layers 1-31; "
+                          f"k_gemv_chain per projection, k_gemv_reduce per chain)", "bound": "hbm", "achieved": round(dom_bytes / dom_s / 1e9, 1), "peak": peak,
                 "unit": "GB/s", "frac": round(dom_bytes / dom_s / 1e9 / peak, 4),
                 "traffic": TRAFFIC_BYTES.get("chain"), "algorithmic_bytes": round(dom_bytes), "call_us": round(dom_s * 1e6, 3),
-                "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs (burst copy)",
-                "timing": "CUDA events around graph replays of the whole step; every kernel of the step is a k_chain launch"}
+                "peak_source": peak_kind,
+                "timing": "CUDA events around graph replays of the whole step; every kernel of the step is a chain launch"}
     else:
         roof = {"kernel": f"p8_mul_mat_vec_group {dom} (k_gemv + k_gemv_reduce)", "bound": "hbm", "achieved": round(achieved, 1),
                 "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                 "traffic": TRAFFIC_BYTES.get(dom) if world == 1 else None, "algorithmic_bytes": dom_bytes,
-                "call_us": round(dom_s * 1e6, 3), "peak_source": f"{peak_kind} MEASURED_PEAKS.json hbm_gbs (burst copy)",
+                "call_us": round(dom_s * 1e6, 3), "peak_source": peak_kind,
                 "per_call_type": per_call}
     tok_s = args.steps / t_dev  # one token stream; with N GPUs every token is split over the ranks (strong scaling)
     line = {
@@ -1054,7 +1059,7 @@ def run_b200(args, rank, world, local_rank):
             "torch_ops": "separate torch elementwise/reduction kernels, then p8_mul_mat_vec_group"}
     if prefill is not None:
         ntok, t_pass, flop, t_sep, c3 = prefill
-        bf16_peak = measured_bf16_tflops()
+        bf16_peak, bf16_kind = measured_bf16_tflops()
         line["prefill"] = {"tokens": ntok, "ms": round(t_pass * 1e3, 3), "tok_s": round(ntok / t_pass, 1),
                            "kernel": "p8_mul_mat_group per input (k_gx_max + k_gx_prep once; k_gemm, tcgen05 kind::f16, "
                                      "fp32 accumulate, + k_unpermute per projection)",
@@ -1062,7 +1067,7 @@ def run_b200(args, rank, world, local_rank):
                                               "kernel": "p8_mul_mat per projection"},
                            "tflops": round(flop / t_pass / 1e12, 1), "bound": "tensor", "peak_tflops": bf16_peak,
                            "frac": round(flop / t_pass / 1e12 / bf16_peak, 4),
-                           "peak_source": "MEASURED_PEAKS.json bf16_tflops (cuBLAS bf16 burst; the GEMM runs fp16 operands at the same rate)",
+                           "peak_source": bf16_kind + "; the GEMM runs fp16 operands at the bf16 rate",
                            "config": "512 tokens x 224 projections (32 layers), distinct weights, inputs resident",
                            "c3_per_gemm": {"what": "config C3: each projection alone (p8_mul_mat), per call; tflops of "
                                                    "2 x rows x K x tokens", "tokens": c3}}
